@@ -1,0 +1,375 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 Gaussian-splatting renderer.
+
+One step = one frame of the hot path (projection, binning, sort, bin ranges, splatting) of
+the 1,000,000-Gaussian SH3 scene at 1920x1080 with 16x16-pixel bins. Rank r renders, at step
+s, view (s * N + r) mod 64 of a 64-view orbit (radius 1.5, elevations -30..30 degrees, 60
+degree FOV): one view per GPU with the scene replicated, no data-path collective (weak
+scaling). Inputs are larger than L2: 240 MB of scene planes and ~390 MB of key buffers per
+frame, so no L2 flush is needed between frames.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``--impl reference`` times the CPU restatement of the reference algorithm (the oracle, C +
+OpenMP on all host cores) on the same workload; under torchrun only rank 0 runs it.
+Prints one JSON line (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "frames/s and Gaussians/s, 1M-splat SH3 1080p; multi-view fps at 1/2/4/8 B200"
+WORKLOAD = "single_1m"
+N_VIEWS = 64
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=400)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--e2e-steps", type=int, default=None, help="steps of the host-buffer pass (default: steps/4)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--small", action="store_true", help="tiny frame for profiler captures")
+    return p.parse_args()
+
+
+def workload_config(w) -> dict:
+    return {
+        "workload": f"{w.name}: {w.n:,} Gaussians SH{w.sh_degree} {w.width}x{w.height}, 16x16-px bins, "
+                    f"{N_VIEWS}-view orbit r={w.distance} elev -30..30 deg, {w.fovy_deg:.0f} deg FOV",
+        "n_gaussians": w.n, "sh_degree": w.sh_degree, "width": w.width, "height": w.height, "bin_px": 16,
+        "views": N_VIEWS, "parallelism": "multi-view: one view per GPU per step, scene replicated",
+        "l2": "inputs larger than L2 (scene planes 240 MB, key buffers ~390 MB per frame); no flush",
+        "seed": w.seed,
+    }
+
+
+# ----------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples of one GPU while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples: list[tuple[float, list[str]]] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), [x.strip() for x in line.split(",")]))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+
+    def summary(self, t0: float, t1: float) -> dict:
+        inside = [s for t, s in self.samples if t0 <= t <= t1]
+        note = None
+        if not inside and self.samples:
+            # the timed window was shorter than the sampling period: nearest samples
+            mid = 0.5 * (t0 + t1)
+            inside = [min(self.samples, key=lambda ts: abs(ts[0] - mid))[1]]
+            note = "timed window shorter than the 100 ms sampling period; nearest sample"
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(s[1]) for s in inside if num(s[1]) is not None]
+        smax = [num(s[2]) for s in inside if num(s[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in inside for i in range(4) if len(s) > 5 + i and s[5 + i] == "Active"})
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+               "reasons": reasons, "samples": len(inside)}
+        if note:
+            out["note"] = note
+        return out
+
+
+# --------------------------------------------------------------- reference arm
+
+def run_reference(args, w, cfg_block):
+    """Time the CPU restatement of the reference algorithm (oracle) on the same workload."""
+    import oracle
+    from klartraum_b200 import make_scene, orbit_views
+
+    g3d = make_scene(w)
+    cams = orbit_views(N_VIEWS, w.distance, w.width, w.height, fovy_deg=w.fovy_deg)
+    cfg = oracle.config(w.width, w.height, bin_size=16, sh_degree=w.sh_degree)
+    bg = np.zeros((w.height, w.width, 4), np.uint8)
+    bg[..., 3] = 255
+    threads = oracle.lib().ko_get_threads()
+    for s in range(args.warmup):
+        oracle.render_frame_fast(cfg, cams[s % N_VIEWS], g3d, bg)
+    t0 = time.perf_counter()
+    for s in range(args.steps):
+        oracle.render_frame_fast(cfg, cams[s % N_VIEWS], g3d, bg)
+    dt = time.perf_counter() - t0
+    fps = args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": fps, "unit": "frames/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dt / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": cfg_block, "gaussians_per_s": fps * w.n,
+        "cpu_baseline": {"value": fps, "unit": "frames/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} full frames of the workload on the host CPU: the C "
+                                   f"restatement of the reference shaders (oracle/kt_oracle.c), OpenMP"},
+        "e2e": {"value": fps, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's own path is Vulkan GLSL; no graphics stack exists on this machine, "
+                "so its CPU restatement is timed",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- our arm
+
+def algorithmic_bytes(st: dict, n: int, nplanes: int, width: int, height: int) -> dict:
+    K = st["num_keys"]
+    tiles = st["tiles_x"] * st["tiles_y"]
+    return {
+        # scene planes (pos, rot, scale + SH planes) read; record 48 + count 4 + rect 8 + depth 4 written
+        "project_count": n * (16 * (3 + nplanes) + 64),
+        # counts, rects, depths read; offsets written; K keys (8 B) + values (4 B) written
+        "scan_emit": n * (4 + 8 + 4 + 8) + K * 12,
+        # per executed pass: read + write of 8 B key and 4 B value
+        "sort": K * 24 * st["sort_passes"],
+        "ranges": K * 8 + tiles * 8,
+    }
+
+
+def load_peaks() -> tuple[float, str]:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def run_ours(args, w, cfg_block, rank, world, local_rank):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from klartraum_b200 import Renderer, make_scene, native as N, orbit_views
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if args.small:
+        w = type(w)(**{**w.__dict__, "n": 20000, "width": 640, "height": 360})
+    g3d = make_scene(w)
+    cams = orbit_views(N_VIEWS, w.distance, w.width, w.height, fovy_deg=w.fovy_deg)
+
+    def view_of(s):
+        return (s * world + rank) % N_VIEWS
+
+    r = Renderer(w.width, w.height, bin_size=16, sh_degree=w.sh_degree, device=local_rank, flags=N.FLAG_TIMING)
+    r.set_gaussians(g3d)
+    nplanes = (3 * (w.sh_degree + 1) ** 2 + 3) // 4
+    bg = torch.zeros((w.height, w.width, 4), dtype=torch.uint8, device=dev)
+    bg[..., 3] = 255
+    img = bg.clone()
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+
+    # warm-up: checked frames over every view this rank renders (sizes the key buffers)
+    views = sorted({view_of(s) for s in range(args.steps)} | {view_of(s) for s in range(args.warmup)})
+    for s in range(max(args.warmup, 3)):
+        r.render(cams[view_of(s)], img, stream=sptr)
+    for v in views:
+        r.render(cams[v], img, stream=sptr)
+    torch.cuda.synchronize()
+    r.stage_times_total()
+    r.counters()
+
+    # ---- timed region (device-resident inputs): frames enqueued back to back, no host sync
+    r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC)
+    clock = ClockSampler(local_rank)
+    clock.start()
+    time.sleep(0.5)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize()
+    t_wall0 = time.time()
+    ev0.record(stream)
+    for s in range(args.steps):
+        r.render(cams[view_of(s)], img, stream=sptr)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    r.sync()  # raises if any timed frame overflowed or timed out
+    clocks = clock.summary(t_wall0, t_wall1)
+    ms = ev0.elapsed_time(ev1)
+    stage_ms, timed_frames = r.stage_times_total()
+    cnt = r.counters()
+    assert cnt["frames"] == args.steps, cnt
+    st = r.stats()
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    fps = world * args.steps / (ms_max / 1000.0)
+
+    # ---- per-stage bandwidth over the timed region
+    peak, peak_kind = load_peaks()
+    frames = max(timed_frames, 1)
+    K_avg = cnt["keys"] / max(cnt["frames"], 1)
+    passes_avg = cnt["key_passes"] / max(cnt["keys"], 1)
+    per_frame_bytes = {
+        "project_count": w.n * (16 * (3 + nplanes) + 64),
+        "scan_emit": w.n * (4 + 8 + 4 + 8) + K_avg * 12,
+        "sort": cnt["key_passes"] / max(cnt["frames"], 1) * 24,
+        "ranges": K_avg * 8 + st["tiles_x"] * st["tiles_y"] * 8,
+    }
+    stages = {}
+    for name in N.STAGE_NAMES[:5]:
+        avg = stage_ms[name] / frames
+        d = {"ms": avg, "share": stage_ms[name] / max(stage_ms["frame"], 1e-12)}
+        if name in per_frame_bytes:
+            gbs = per_frame_bytes[name] / (avg / 1000.0) / 1e9 if avg > 0 else 0.0
+            d.update({"bytes": per_frame_bytes[name], "gbs": gbs, "frac": gbs / peak})
+        stages[name] = d
+    dominant = max(stages, key=lambda k: stages[k]["ms"])
+    dom = stages[dominant]
+    if "bytes" in dom:
+        roofline = {"kernel": dominant, "bound": "hbm", "achieved": dom["gbs"], "peak": peak, "unit": "GB/s",
+                    "frac": dom["frac"], "traffic": None, "peak_source": peak_kind,
+                    "bytes_per_launch": dom["bytes"]}
+    else:
+        hb = max((k for k in stages if "bytes" in stages[k]), key=lambda k: stages[k]["ms"])
+        roofline = {"kernel": hb, "bound": "hbm", "achieved": stages[hb]["gbs"], "peak": peak, "unit": "GB/s",
+                    "frac": stages[hb]["frac"], "traffic": None, "peak_source": peak_kind,
+                    "bytes_per_launch": stages[hb]["bytes"],
+                    "note": f"{dominant} (issue bound, not HBM) takes the most time; this is the top HBM-bound stage"}
+
+    # ---- end to end through the public API with host buffers
+    r.set_flags(0)
+    e2e_steps = args.e2e_steps or max(10, args.steps // 4)
+    host = torch.empty((w.height, w.width, 4), dtype=torch.uint8, pin_memory=True)
+    host.copy_(bg.cpu())
+    for s in range(3):
+        r.render_host(cams[view_of(s)], host.data_ptr(), stream=sptr)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(e2e_steps):
+        r.render_host(cams[view_of(s)], host.data_ptr(), stream=sptr)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_fps = world * e2e_steps / (float(te.item()) / 1000.0)
+    img_bytes = w.width * w.height * 4
+    clock.stop()
+
+    launches_per_frame = st["launches"]
+    line = {
+        "metric": METRIC, "value": fps, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg_block,
+        "gaussians_per_s": fps * w.n, "keys_per_frame": K_avg, "sort_passes_per_frame": passes_avg,
+        "stages": stages, "roofline": roofline,
+        "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": img_bytes + 192,
+                "d2h_bytes_per_step": img_bytes + st["status_bytes"], "steps": e2e_steps,
+                "api": "kt_gs_render_host (pinned host image in, rendered image out, waits per frame)"},
+        "gpu_launches": launches_per_frame * args.steps * world, "gpu_launches_per_step": launches_per_frame,
+        "clocks": clocks,
+    }
+    if world == 1 and rank == 0 and not args.no_cpu_baseline and not args.small:
+        line["cpu_baseline"] = cpu_baseline(w, cams)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    r.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def cpu_baseline(w, cams) -> dict:
+    """The oracle (C restatement of the reference shaders, OpenMP) on one full frame."""
+    import oracle
+    from klartraum_b200 import make_scene
+
+    g3d = make_scene(w)
+    cfg = oracle.config(w.width, w.height, bin_size=16, sh_degree=w.sh_degree)
+    bg = np.zeros((w.height, w.width, 4), np.uint8)
+    bg[..., 3] = 255
+    oracle.render_frame_fast(cfg, cams[0], g3d, bg)  # warm caches / page in
+    frames = 0
+    t0 = time.perf_counter()
+    while True:
+        oracle.render_frame_fast(cfg, cams[frames % N_VIEWS], g3d, bg)
+        frames += 1
+        if time.perf_counter() - t0 > 10.0 or frames >= 8:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": frames / dt, "unit": "frames/s", "cores": oracle.lib().ko_get_threads(), "kind": "port",
+            "sample": f"{frames} full frames of the same workload (views 0..{frames - 1}) through the C "
+                      f"restatement of the reference shaders (oracle/kt_oracle.c), OpenMP"}
+
+
+def main():
+    args = parse()
+    from klartraum_b200.scenes import WORKLOADS
+
+    w = WORKLOADS[WORKLOAD]
+    cfg_block = workload_config(w)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args, w, cfg_block)
+        return
+    run_ours(args, w, cfg_block, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

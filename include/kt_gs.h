@@ -1,0 +1,282 @@
+/*
+ * kt_gs.h - C ABI of the B200 Gaussian-splatting renderer.
+ *
+ * This library replaces the Vulkan compute pipeline that klartraum's
+ * VulkanGaussianSplatting graph node records (projection -> binning ->
+ * radix sort -> bin bounds -> binned splatting). Every entry point takes
+ * plain pointers and sizes; CUDA streams are passed as opaque `void*`
+ * (a cudaStream_t, NULL = the legacy default stream).
+ *
+ * Every call returns a kt_status. On failure kt_gs_last_error() gives a
+ * message for the context; the C++ node shim turns a non-OK status into
+ * std::runtime_error, the reference's error convention
+ * (src/vulkan_gaussian_splatting.cpp:33,37,223,227,230).
+ *
+ * Threading: a context is used by one host thread at a time. Contexts on
+ * different devices may be driven concurrently from different threads.
+ */
+#ifndef KT_GS_H
+#define KT_GS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KT_GS_ABI_VERSION 1
+
+typedef enum kt_status {
+    KT_OK = 0,
+    KT_ERR_ARG = 1,      /* invalid argument or configuration */
+    KT_ERR_CUDA = 2,     /* a CUDA runtime call failed */
+    KT_ERR_CAPACITY = 3, /* key buffer too small; kt_gs_frame_stats().num_keys holds the need */
+    KT_ERR_TIMEOUT = 4,  /* a bounded device-side wait (decoupled look-back) ran out */
+    KT_ERR_NCCL = 5,     /* reserved for the multi-GPU strip gather */
+    KT_ERR_IO = 6,       /* file could not be read or parsed */
+    KT_ERR_STATE = 7,    /* call out of order (e.g. render before any Gaussians were set) */
+    KT_ERR_NOMEM = 8     /* a device or pinned-host allocation failed */
+} kt_status;
+
+/*
+ * One 3D Gaussian, 236 bytes, field order of klartraum::Gaussian3D
+ * (include/klartraum/vulkan_gaussian_splatting_types.hpp:24-33) and of the
+ * GLSL `Gaussian` (shaders/gsplat/gsplat_types.glsl:1-10). scale is already
+ * exp()'d and alpha already sigmoid()'ed, as loadSPZModel leaves them
+ * (src/vulkan_gaussian_splatting.cpp:348,356-358). color is the raw SH DC
+ * coefficient per channel; shR/shG/shB are bands 1..3 (15 each).
+ */
+typedef struct kt_gaussian3d {
+    float position[3];
+    float rotation[4]; /* x, y, z, w */
+    float scale[3];
+    float color[3];
+    float alpha;
+    float shR[15];
+    float shG[15];
+    float shB[15];
+} kt_gaussian3d;
+
+/*
+ * Camera uniform block, 192 bytes: three column-major 4x4 matrices, element
+ * (col c, row r) at index 4*c + r. Layout of klartraum::CameraMVP
+ * (include/klartraum/camera.hpp:44-48) and of the projection shader's UBO
+ * (shaders/gsplat/gsplat_projection.comp:14-18).
+ */
+typedef struct kt_camera_mvp {
+    float model[16];
+    float view[16];
+    float proj[16];
+} kt_camera_mvp;
+
+/*
+ * Projected Gaussian, 48 bytes, the GLSL scalar layout of `Gaussian2D`
+ * (shaders/gsplat/gsplat_types.glsl:12-19): pixel position, clip-space z,
+ * bin mask, inverse covariance (column-major c00,c01,c10,c11), colour,
+ * alpha. Used for stage dumps and for kt_gs_render_projected().
+ */
+typedef struct kt_gaussian2d {
+    float position[2];
+    float z;
+    uint32_t binMask;
+    float covInv[4];
+    float color[3];
+    float alpha;
+} kt_gaussian2d;
+
+/* Flags for kt_gs_config.flags. */
+#define KT_GS_FLAG_EXIT_PER_ELEMENT 0x1u /* stop a pixel after any Gaussian once T <= 1-0.9999,
+                                            instead of only at 64-Gaussian batch ends
+                                            (gsplat_binned_splatting.comp:98,114) */
+#define KT_GS_FLAG_NO_AUTOGROW 0x2u      /* on key overflow return KT_ERR_CAPACITY instead of
+                                            growing the key buffers and rendering again */
+#define KT_GS_FLAG_ASYNC 0x4u            /* do not wait for the frame status after a render;
+                                            kt_gs_sync() reports overflow/timeouts later */
+#define KT_GS_FLAG_KEEP_UNSORTED 0x8u    /* keep a copy of the unsorted keys/values for dumps */
+#define KT_GS_FLAG_TIMING 0x10u          /* record CUDA events around every stage */
+
+typedef struct kt_gs_config {
+    uint32_t width;          /* screen width in pixels (reference: 512, vulkan_gaussian_splatting.cpp:20) */
+    uint32_t height;         /* screen height in pixels (reference: 512, :21) */
+    uint32_t bin_width;      /* binning cell in pixels; 16 = 16x16 tiles. 128 at 512x512 is the
+                                reference's 4x4 grid (:23, gsplat_binning.comp:55-56). Multiple of 16. */
+    uint32_t bin_height;
+    int32_t sh_degree;       /* 0..3 bands kept on the device; -1 = detect from the data */
+    float cull_z;            /* Gaussians with clip-space z below this are dropped (1.0,
+                                gsplat_binning.comp:113) */
+    uint32_t flags;          /* KT_GS_FLAG_* */
+    uint32_t num_paths;      /* frames in flight, each with its own device workspace (reference
+                                numberPaths, src/klartraum_engine.cpp:71) */
+    uint64_t key_capacity;   /* initial (tile, Gaussian) key capacity per path; 0 = size on demand */
+    uint32_t tile_row_begin; /* screen band: only bin rows [begin, end) are binned and drawn; */
+    uint32_t tile_row_end;   /* end = 0 means all rows (used by the banded multi-GPU split) */
+} kt_gs_config;
+
+/* Per-frame statistics of the last render on a path. */
+typedef struct kt_gs_stats {
+    uint64_t num_gaussians;  /* N */
+    uint64_t num_keys;       /* K = sum of tile counts = (bin, Gaussian) pairs */
+    uint64_t key_capacity;   /* current key capacity of the path */
+    uint64_t num_visible;    /* Gaussians with a non-zero tile count */
+    uint32_t tiles_x;
+    uint32_t tiles_y;
+    uint32_t key_bits;       /* significant bits of the compact sort key (bin bits + depth bits) */
+    uint32_t depth_bits;     /* bits of the depth field after subtracting the frame's minimum */
+    uint32_t sort_passes;    /* 8-bit LSD passes that moved data (the rest were skipped) */
+    uint32_t error_flags;    /* device error bits: 1 = capacity, 2 = look-back timeout */
+    uint32_t depth_min_bits; /* smallest (floatBitsToUint(z) ^ 0x80000000) over binned Gaussians */
+    uint32_t depth_max_bits;
+    uint32_t status_bytes;   /* bytes of frame status copied device->host after every frame */
+    uint32_t launches;       /* kernels launched per frame */
+} kt_gs_stats;
+
+/* Totals accumulated on the device over every frame rendered on a path since the last
+ * kt_gs_counters_take(); used to turn stage times into bandwidth without per-frame syncs. */
+typedef struct kt_gs_counters {
+    uint64_t frames;      /* frames whose sort plan ran */
+    uint64_t keys;        /* sum of K */
+    uint64_t key_passes;  /* sum of K * (executed sort passes) */
+    uint64_t visible;     /* sum of Gaussians with a non-zero tile count */
+} kt_gs_counters;
+
+/* Buffers that kt_gs_debug_dump() can copy out after a render. */
+typedef enum kt_gs_stage {
+    KT_GS_STAGE_PROJECTED = 0,       /* kt_gaussian2d[N], binMask = 0xFFFFFFFF as projected
+                                        (gsplat_projection.comp:228) */
+    KT_GS_STAGE_TILE_COUNTS = 1,     /* uint32[N] bins overlapped by each Gaussian (0 if culled) */
+    KT_GS_STAGE_OFFSETS = 2,         /* uint64[N] exclusive scan of the tile counts */
+    KT_GS_STAGE_KEYS_UNSORTED = 3,   /* uint64[K] bin<<32 | (floatBitsToUint(z) ^ 0x80000000);
+                                        needs KT_GS_FLAG_KEEP_UNSORTED */
+    KT_GS_STAGE_VALUES_UNSORTED = 4, /* uint32[K] Gaussian index; needs KT_GS_FLAG_KEEP_UNSORTED */
+    KT_GS_STAGE_KEYS_SORTED = 5,     /* uint64[K], same key layout, stably sorted */
+    KT_GS_STAGE_VALUES_SORTED = 6,   /* uint32[K] */
+    KT_GS_STAGE_TILE_RANGES = 7,     /* uint32[2 * tiles] {start, end} per bin (StartAndEnd,
+                                        gsplat_types.glsl:21-24); empty bins {0, 0} */
+    KT_GS_STAGE_COUNT = 8
+} kt_gs_stage;
+
+/* Stage timers (KT_GS_FLAG_TIMING), in the order the stages run. */
+#define KT_GS_NSTAGES 6
+/* 0 projection+count, 1 scan+emit, 2 sort, 3 bin ranges, 4 rasterise, 5 whole frame */
+
+typedef struct kt_gs_ctx kt_gs_ctx;
+
+/* Fill a config with the reference's defaults: 512x512, 128-px bins (4x4 grid), SH3, cull 1.0. */
+void kt_gs_config_default(kt_gs_config* cfg);
+
+/* Library ABI version (KT_GS_ABI_VERSION). */
+int kt_gs_abi_version(void);
+
+/* Human-readable name of a status code. */
+const char* kt_gs_status_string(kt_status status);
+
+/*
+ * Create a renderer on CUDA device `device`.
+ * Replaces the constructor VulkanGaussianSplatting(ctx, imageViewSrc, cameraUBO, path)
+ * (include/klartraum/vulkan_gaussian_splatting.hpp:44-48, src/vulkan_gaussian_splatting.cpp:13-213)
+ * minus the scene load, which is kt_gs_set_gaussians() / kt_gs_load_spz().
+ */
+kt_status kt_gs_create(const kt_gs_config* cfg, int device, kt_gs_ctx** out);
+
+/* Release every device buffer of the context (reference destructor, .cpp:215-218). */
+kt_status kt_gs_destroy(kt_gs_ctx* ctx);
+
+/* Message of the last failed call on this context ("" if none). Valid until the next call. */
+const char* kt_gs_last_error(const kt_gs_ctx* ctx);
+
+/* Replace the context's KT_GS_FLAG_* bits (e.g. switch to KT_GS_FLAG_ASYNC after warm-up). */
+kt_status kt_gs_set_flags(kt_gs_ctx* ctx, uint32_t flags);
+
+/* Copy of the context's configuration (with sh_degree resolved once Gaussians are set). */
+kt_status kt_gs_get_config(const kt_gs_ctx* ctx, kt_gs_config* cfg);
+
+/*
+ * Upload n Gaussians from host memory (array of structs, 236 B each) and keep them on the
+ * device as planes of float4. Replaces the Gaussians3D buffer upload
+ * (src/vulkan_gaussian_splatting.cpp:40-43). Synchronous.
+ */
+kt_status kt_gs_set_gaussians(kt_gs_ctx* ctx, const kt_gaussian3d* host, uint64_t n);
+
+/* Same from device memory (e.g. a buffer filled by a collective broadcast), on `stream`. */
+kt_status kt_gs_set_gaussians_device(kt_gs_ctx* ctx, const kt_gaussian3d* dev, uint64_t n,
+                                     void* stream);
+
+/*
+ * Load an .spz file (gzip-compressed packed Gaussians) and upload it with the activations of
+ * loadSPZModel (src/vulkan_gaussian_splatting.cpp:322-365): alpha = sigmoid, scale = exp.
+ */
+kt_status kt_gs_load_spz(kt_gs_ctx* ctx, const char* path);
+
+/*
+ * Render one frame. `cam` is host memory (the per-path camera UBO, uniformbufferobject.hpp:67-70).
+ * `d_rgba8` is a device image of width*height RGBA8 pixels, row-major, row 0 at the top; it
+ * is read-modify-written: out = clamp(in + vec4(C,1)*(1-T)) (gsplat_binned_splatting.comp:119-121).
+ * Work is enqueued on `stream`; unless KT_GS_FLAG_ASYNC is set the call waits for the frame
+ * status and, on key overflow, grows the key buffers and renders again.
+ * Replaces ComputeGraph::submitTo of the node's sub-graph (computegraph.hpp:122-139).
+ */
+kt_status kt_gs_render(kt_gs_ctx* ctx, const kt_camera_mvp* cam, void* d_rgba8, uint32_t path,
+                       void* stream);
+
+/*
+ * Render one frame into a host image: copies the host image to the device, renders, and
+ * copies it back, all on `stream`, and waits. `h_rgba8` should be pinned for full speed.
+ */
+kt_status kt_gs_render_host(kt_gs_ctx* ctx, const kt_camera_mvp* cam, void* h_rgba8,
+                            uint32_t path, void* stream);
+
+/* Render n_views cameras, view v into d_rgba8[v] (device pointers), on `stream`. */
+kt_status kt_gs_render_batch(kt_gs_ctx* ctx, const kt_camera_mvp* cams, uint32_t n_views,
+                             void* const* d_rgba8, void* stream);
+
+/*
+ * Run binning -> sort -> bin bounds -> splatting on n already projected Gaussians given in
+ * host memory (the input the reference's binning test feeds, tests/test_gaussian_splatting.cpp:247-320).
+ * The records' binMask fields are ignored.
+ */
+kt_status kt_gs_render_projected(kt_gs_ctx* ctx, const kt_gaussian2d* host, uint64_t n,
+                                 void* d_rgba8, uint32_t path, void* stream);
+
+/* Wait for all work of `path` and report any device error of the frames rendered on it since
+ * the previous sync (key overflow: those frames drew nothing; look-back timeout). */
+kt_status kt_gs_sync(kt_gs_ctx* ctx, uint32_t path);
+
+/* Statistics of the last frame rendered on `path` (waits for it). */
+kt_status kt_gs_frame_stats(kt_gs_ctx* ctx, uint32_t path, kt_gs_stats* out);
+
+/* Copy a stage buffer of the last frame on `path` to host memory (waits for it).
+ * `bytes` is the size of host_dst; *written receives the bytes copied. */
+kt_status kt_gs_debug_dump(kt_gs_ctx* ctx, uint32_t path, kt_gs_stage stage, void* host_dst,
+                           uint64_t bytes, uint64_t* written);
+
+/* Per-stage milliseconds of the last frame on `path` (needs KT_GS_FLAG_TIMING). */
+kt_status kt_gs_stage_times(kt_gs_ctx* ctx, uint32_t path, float ms[KT_GS_NSTAGES]);
+
+/* Read and reset the device-side frame counters of `path` (waits for its work). */
+kt_status kt_gs_counters_take(kt_gs_ctx* ctx, uint32_t path, kt_gs_counters* out);
+
+/*
+ * Sums of the per-stage milliseconds of every frame rendered on `path` with
+ * KT_GS_FLAG_TIMING since the previous call (waits for them), and their number; resets.
+ */
+kt_status kt_gs_stage_times_total(kt_gs_ctx* ctx, uint32_t path, double ms_total[KT_GS_NSTAGES],
+                                  uint64_t* frames);
+
+/*
+ * Stable LSD radix sort of (uint64 key, uint32 value) pairs by key bits [0, key_bits), on the
+ * device. The operator behind the GaussianSort BufferTransformation
+ * (src/vulkan_gaussian_splatting.cpp:95-143, shaders/gsplat/gsplat_radix_sort_*.comp).
+ * Two-phase scratch protocol: call with d_temp == NULL to get *temp_bytes, allocate, call again.
+ * keys_in/vals_in are not modified; keys_out/vals_out must not alias them.
+ */
+kt_status kt_gs_radix_sort_pairs(const uint64_t* d_keys_in, const uint32_t* d_vals_in,
+                                 uint64_t* d_keys_out, uint32_t* d_vals_out, uint64_t n,
+                                 uint32_t key_bits, void* d_temp, size_t* temp_bytes,
+                                 void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KT_GS_H */

@@ -1,0 +1,847 @@
+// C ABI of the renderer (include/kt_gs.h): context, device workspaces and the frame driver.
+//
+// Host-side counterpart of klartraum's VulkanGaussianSplatting node
+// (src/vulkan_gaussian_splatting.cpp:13-316): where the node builds a five-element compute
+// sub-graph with Vulkan buffers, this context owns the device buffers of each path (frame in
+// flight) and enqueues the kernels of one frame on a CUDA stream:
+//   init -> K1 project+count -> K2/3 scan+emit -> plan -> K4 sort passes -> K5 ranges -> K6.
+// No host synchronisation happens inside a frame: the key count, the sort plan and the pass
+// skipping live in device memory. After the frame a 2.6 KB control block is copied back;
+// unless KT_GS_FLAG_ASYNC is set the call waits for it and, if the keys did not fit, grows
+// the key buffers and renders again (nothing was drawn in that case).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstddef>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "kt_common.cuh"
+#include "kt_gs.h"
+#include "kt_kernels.h"
+
+namespace kt {
+
+int device_sm_count() {
+    static int cache[128] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 148;
+    if (cache[dev] == 0) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = v > 0 ? v : 148;
+    }
+    return cache[dev];
+}
+
+}  // namespace kt
+
+using namespace kt;
+
+namespace {
+
+constexpr uint64_t kMaxKeyCapacity = 0xFFFFF000ull;  // values and ranges are 32-bit
+
+struct PathWs {
+    uint64_t n_alloc = 0;
+    uint64_t cap = 0;
+    float4* rec = nullptr;
+    uint32_t* counts = nullptr;
+    uint2* rect = nullptr;
+    uint32_t* depth = nullptr;
+    unsigned long long* offsets = nullptr;
+    unsigned long long* scan_status = nullptr;
+    unsigned long long* keys[2] = {nullptr, nullptr};
+    uint32_t* vals[2] = {nullptr, nullptr};
+    unsigned long long* sort_status = nullptr;
+    uint2* ranges = nullptr;
+    FrameCtl* ctl = nullptr;
+    FrameCtl* host_ctl = nullptr;  // pinned copy of the last frame's control block
+    uint32_t scan_epoch = 0;
+    uint32_t sort_epoch = 0;
+    cudaEvent_t done_ev = nullptr;
+    // stage timers: a ring of event sets, one set per timed frame, drained into sums
+    static constexpr int kRing = 16;
+    cudaEvent_t ring[kRing][KT_GS_NSTAGES] = {};
+    bool ring_used[kRing] = {};
+    int ring_next = 0;
+    int ring_last = -1;
+    double stage_sum[KT_GS_NSTAGES] = {};
+    uint64_t timed_frames = 0;
+    FrameTotals* totals = nullptr;  // device: counters and sticky error bits across frames
+    bool timed = false;
+    bool have_frame = false;
+    uint64_t frame_n = 0;
+    // debug copies of the unsorted keys
+    unsigned long long* dbg_keys = nullptr;
+    uint32_t* dbg_vals = nullptr;
+    uint64_t dbg_count = 0;
+    uint64_t dbg_cap = 0;
+    // device image for kt_gs_render_host
+    uchar4* img = nullptr;
+    // device copy of caller-supplied projected records
+    float* g2d = nullptr;
+    uint64_t g2d_n = 0;
+};
+
+template <class T>
+void dfree(T*& p) {
+    if (p) cudaFree((void*)p);
+    p = nullptr;
+}
+
+}  // namespace
+
+struct kt_gs_ctx {
+    kt_gs_config cfg{};
+    int device = 0;
+    std::string err;
+    float4* pos = nullptr;
+    float4* rot = nullptr;
+    float4* scale = nullptr;
+    float4* sh = nullptr;
+    uint32_t nplanes = 0;
+    int deg = 0;
+    uint64_t n = 0;
+    bool has_scene = false;
+    GridParams gp{};
+    uint32_t max_passes = 0;
+    std::vector<PathWs> paths;
+};
+
+namespace {
+
+kt_status fail(kt_gs_ctx* c, kt_status s, const std::string& msg) {
+    if (c) c->err = msg;
+    return s;
+}
+
+#define KT_TRY_CUDA(ctx, call)                                                              \
+    do {                                                                                    \
+        cudaError_t e_ = (call);                                                            \
+        if (e_ != cudaSuccess)                                                              \
+            return fail((ctx), e_ == cudaErrorMemoryAllocation ? KT_ERR_NOMEM : KT_ERR_CUDA, \
+                        std::string(#call) + ": " + cudaGetErrorString(e_));                \
+    } while (0)
+
+// GLSL mat4 * mat4, column-major, products summed in ascending k (matches the shader).
+void mat4_mul(const float* a, const float* b, float* r) {
+    for (int c = 0; c < 4; ++c)
+        for (int k = 0; k < 4; ++k)
+            r[4 * c + k] = a[k] * b[4 * c] + a[4 + k] * b[4 * c + 1] + a[8 + k] * b[4 * c + 2] +
+                           a[12 + k] * b[4 * c + 3];
+}
+
+CamParams make_cam(const kt_camera_mvp* cam) {
+    CamParams p;
+    float pv[16];
+    mat4_mul(cam->proj, cam->view, pv);
+    mat4_mul(pv, cam->model, p.pvm);     // ubo.proj * ubo.view * ubo.model
+    mat4_mul(cam->model, cam->view, p.mv);  // ubo.model * ubo.view
+    p.focal_x = cam->proj[0];
+    p.focal_y = cam->proj[5];
+    return p;
+}
+
+GridParams make_grid(const kt_gs_config& c) {
+    GridParams g;
+    g.width = c.width;
+    g.height = c.height;
+    g.bin_w = c.bin_width;
+    g.bin_h = c.bin_height;
+    g.half_w = (float)c.width * 0.5f;
+    g.half_h = (float)c.height * 0.5f;
+    g.sxx = (float)c.width * (float)c.width;
+    g.syy = (float)c.height * (float)c.height;
+    g.sxy = (float)c.width * (float)c.height;
+    g.cell_w = (float)c.bin_width;
+    g.cell_h = (float)c.bin_height;
+    g.cull_z = c.cull_z;
+    g.tiles_x = (c.width + c.bin_width - 1) / c.bin_width;
+    g.tiles_y = (c.height + c.bin_height - 1) / c.bin_height;
+    g.row_end = c.tile_row_end == 0 ? g.tiles_y : std::min(c.tile_row_end, g.tiles_y);
+    g.row_begin = std::min(c.tile_row_begin, g.row_end);
+    g.tile_bits = bits_for((uint64_t)g.tiles_x * g.tiles_y - 1);
+    return g;
+}
+
+uint32_t ntiles(const kt_gs_ctx* c) { return c->gp.tiles_x * c->gp.tiles_y; }
+
+void free_path(PathWs& w) {
+    dfree(w.rec); dfree(w.counts); dfree(w.rect); dfree(w.depth); dfree(w.offsets);
+    dfree(w.scan_status); dfree(w.keys[0]); dfree(w.keys[1]); dfree(w.vals[0]); dfree(w.vals[1]);
+    dfree(w.sort_status); dfree(w.ranges); dfree(w.ctl); dfree(w.dbg_keys); dfree(w.dbg_vals);
+    dfree(w.img); dfree(w.g2d);
+    if (w.host_ctl) cudaFreeHost(w.host_ctl);
+    w.host_ctl = nullptr;
+    if (w.done_ev) cudaEventDestroy(w.done_ev);
+    w.done_ev = nullptr;
+    for (auto& set : w.ring)
+        for (auto& e : set) {
+            if (e) cudaEventDestroy(e);
+            e = nullptr;
+        }
+    dfree(w.totals);
+    w.n_alloc = w.cap = 0;
+}
+
+kt_status ensure_path_base(kt_gs_ctx* c, PathWs& w) {
+    if (!w.ctl) {
+        KT_TRY_CUDA(c, cudaMalloc(&w.ctl, sizeof(FrameCtl)));
+        KT_TRY_CUDA(c, cudaMemset(w.ctl, 0, sizeof(FrameCtl)));
+        KT_TRY_CUDA(c, cudaMallocHost(&w.host_ctl, sizeof(FrameCtl)));
+        std::memset(w.host_ctl, 0, sizeof(FrameCtl));
+        KT_TRY_CUDA(c, cudaMalloc(&w.ranges, sizeof(uint2) * std::max(1u, ntiles(c))));
+        KT_TRY_CUDA(c, cudaEventCreateWithFlags(&w.done_ev, cudaEventDisableTiming));
+        for (auto& set : w.ring)
+            for (auto& e : set) KT_TRY_CUDA(c, cudaEventCreate(&e));
+        KT_TRY_CUDA(c, cudaMalloc(&w.totals, sizeof(FrameTotals)));
+        KT_TRY_CUDA(c, cudaMemset(w.totals, 0, sizeof(FrameTotals)));
+    }
+    return KT_OK;
+}
+
+kt_status ensure_n(kt_gs_ctx* c, PathWs& w, uint64_t n) {
+    if (n <= w.n_alloc) return KT_OK;
+    dfree(w.rec); dfree(w.counts); dfree(w.rect); dfree(w.depth); dfree(w.offsets);
+    dfree(w.scan_status);
+    w.n_alloc = 0;
+    const uint64_t m = std::max<uint64_t>(n, 1);
+    KT_TRY_CUDA(c, cudaMalloc(&w.rec, sizeof(float4) * 3 * m));
+    KT_TRY_CUDA(c, cudaMalloc(&w.counts, sizeof(uint32_t) * m));
+    KT_TRY_CUDA(c, cudaMalloc(&w.rect, sizeof(uint2) * m));
+    KT_TRY_CUDA(c, cudaMalloc(&w.depth, sizeof(uint32_t) * m));
+    KT_TRY_CUDA(c, cudaMalloc(&w.offsets, sizeof(unsigned long long) * m));
+    const uint64_t chunks = (m + kScanChunk - 1) / kScanChunk;
+    KT_TRY_CUDA(c, cudaMalloc(&w.scan_status, sizeof(unsigned long long) * chunks));
+    KT_TRY_CUDA(c, cudaMemset(w.scan_status, 0, sizeof(unsigned long long) * chunks));
+    w.scan_epoch = 0;
+    w.n_alloc = m;
+    return KT_OK;
+}
+
+kt_status ensure_cap(kt_gs_ctx* c, PathWs& w, uint64_t cap) {
+    if (cap <= w.cap) return KT_OK;
+    if (cap > kMaxKeyCapacity)
+        return fail(c, KT_ERR_CAPACITY, "key count " + std::to_string(cap) +
+                                            " exceeds the 32-bit index range of the key buffers");
+    cap = std::min<uint64_t>(((cap + kSortTile - 1) / kSortTile) * kSortTile, kMaxKeyCapacity);
+    dfree(w.keys[0]); dfree(w.keys[1]); dfree(w.vals[0]); dfree(w.vals[1]); dfree(w.sort_status);
+    w.cap = 0;
+    for (int b = 0; b < 2; ++b) {
+        KT_TRY_CUDA(c, cudaMalloc(&w.keys[b], sizeof(unsigned long long) * cap));
+        KT_TRY_CUDA(c, cudaMalloc(&w.vals[b], sizeof(uint32_t) * cap));
+    }
+    const size_t words = sort_status_words(cap);
+    KT_TRY_CUDA(c, cudaMalloc(&w.sort_status, sizeof(unsigned long long) * words));
+    KT_TRY_CUDA(c, cudaMemset(w.sort_status, 0, sizeof(unsigned long long) * words));
+    w.sort_epoch = 0;
+    w.cap = cap;
+    return KT_OK;
+}
+
+FrameBufs frame_bufs(const PathWs& w) {
+    FrameBufs fb;
+    fb.rec = w.rec;
+    fb.counts = w.counts;
+    fb.rect = w.rect;
+    fb.depth = w.depth;
+    fb.offsets = w.offsets;
+    fb.keys[0] = w.keys[0];
+    fb.keys[1] = w.keys[1];
+    fb.vals[0] = w.vals[0];
+    fb.vals[1] = w.vals[1];
+    fb.ranges = w.ranges;
+    fb.scan_status = w.scan_status;
+    fb.sort_status = w.sort_status;
+    fb.ctl = w.ctl;
+    fb.key_capacity = w.cap;
+    return fb;
+}
+
+enum class Source { Scene, Projected };
+
+// bytes of FrameCtl copied back after every frame (everything before the histograms)
+constexpr size_t kCtlHeaderBytes = offsetof(FrameCtl, hist);
+
+// Wait for a timed frame's events and add its stage times to the running sums.
+kt_status drain_slot(kt_gs_ctx* c, PathWs& w, int slot) {
+    if (!w.ring_used[slot]) return KT_OK;
+    cudaEvent_t* ev = w.ring[slot];
+    KT_TRY_CUDA(c, cudaEventSynchronize(ev[5]));
+    float ms = 0.0f;
+    for (int i = 0; i < 5; ++i) {
+        KT_TRY_CUDA(c, cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+        w.stage_sum[i] += ms;
+    }
+    KT_TRY_CUDA(c, cudaEventElapsedTime(&ms, ev[0], ev[5]));
+    w.stage_sum[5] += ms;
+    w.timed_frames += 1;
+    w.ring_used[slot] = false;
+    return KT_OK;
+}
+
+// Enqueue one frame on `stream`. Does not wait.
+kt_status enqueue_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* cam, uchar4* img,
+                        cudaStream_t stream) {
+    const uint64_t n = src == Source::Scene ? c->n : w.g2d_n;
+    const bool timed = (c->cfg.flags & KT_GS_FLAG_TIMING) != 0;
+    w.timed = timed;
+    cudaEvent_t* ev = nullptr;
+    if (timed) {
+        const int slot = w.ring_next;
+        if (w.ring_used[slot]) {
+            kt_status s = drain_slot(c, w, slot);
+            if (s != KT_OK) return s;
+        }
+        ev = w.ring[slot];
+        w.ring_used[slot] = true;
+        w.ring_last = slot;
+        w.ring_next = (slot + 1) % PathWs::kRing;
+    }
+    // look-back epochs; a wrap clears the status words
+    if (++w.scan_epoch > kEpochMax) {
+        KT_TRY_CUDA(c, cudaMemsetAsync(w.scan_status, 0,
+                                       sizeof(unsigned long long) * ((w.n_alloc + kScanChunk - 1) / kScanChunk),
+                                       stream));
+        w.scan_epoch = 1;
+    }
+    if (w.sort_epoch + c->max_passes + 1 > kEpochMax) {
+        KT_TRY_CUDA(c, cudaMemsetAsync(w.sort_status, 0,
+                                       sizeof(unsigned long long) * sort_status_words(w.cap), stream));
+        w.sort_epoch = 0;
+    }
+    const uint32_t sort_epoch0 = w.sort_epoch + 1;
+    w.sort_epoch += c->max_passes;
+
+    FrameBufs fb = frame_bufs(w);
+    SortIO io{};
+    io.keys[0] = w.keys[0];
+    io.keys[1] = w.keys[1];
+    io.vals[0] = w.vals[0];
+    io.vals[1] = w.vals[1];
+
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[0], stream));
+    KT_TRY_CUDA(c, launch_frame_init(w.ctl, w.ranges, ntiles(c), stream));
+    if (src == Source::Scene) {
+        SceneDev sc{c->pos, c->rot, c->scale, c->sh, c->nplanes, c->deg, c->n};
+        KT_TRY_CUDA(c, launch_project_count(sc, *cam, c->gp, fb, stream));
+    } else {
+        KT_TRY_CUDA(c, launch_load_projected(w.g2d, n, c->gp, fb, stream));
+    }
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[1], stream));
+    KT_TRY_CUDA(c, launch_scan_emit(fb, c->gp, n, w.scan_epoch, c->max_passes, stream));
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[2], stream));
+    KT_TRY_CUDA(c, launch_plan(w.ctl, w.cap, c->max_passes, 0, stream));
+    if (c->cfg.flags & KT_GS_FLAG_KEEP_UNSORTED) {
+        // debug path: read K now and keep a copy of the emitted pairs
+        unsigned long long k = 0;
+        KT_TRY_CUDA(c, cudaMemcpyAsync(&k, &w.ctl->num_keys, sizeof(k), cudaMemcpyDeviceToHost, stream));
+        KT_TRY_CUDA(c, cudaStreamSynchronize(stream));
+        w.dbg_count = 0;
+        if (k <= w.cap) {
+            if (k > w.dbg_cap) {
+                dfree(w.dbg_keys);
+                dfree(w.dbg_vals);
+                w.dbg_cap = 0;
+                KT_TRY_CUDA(c, cudaMalloc(&w.dbg_keys, sizeof(unsigned long long) * std::max<uint64_t>(k, 1)));
+                KT_TRY_CUDA(c, cudaMalloc(&w.dbg_vals, sizeof(uint32_t) * std::max<uint64_t>(k, 1)));
+                w.dbg_cap = std::max<uint64_t>(k, 1);
+            }
+            KT_TRY_CUDA(c, cudaMemcpyAsync(w.dbg_keys, w.keys[0], k * 8, cudaMemcpyDeviceToDevice, stream));
+            KT_TRY_CUDA(c, cudaMemcpyAsync(w.dbg_vals, w.vals[0], k * 4, cudaMemcpyDeviceToDevice, stream));
+            w.dbg_count = k;
+        }
+    }
+    for (uint32_t p = 0; p < c->max_passes; ++p)
+        KT_TRY_CUDA(c, launch_sort_pass(io, w.ctl, w.sort_status, p, sort_epoch0 + p, w.cap, stream));
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[3], stream));
+    KT_TRY_CUDA(c, launch_ranges(io, w.ctl, w.ranges, w.totals, stream));
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[4], stream));
+    KT_TRY_CUDA(c, launch_rasterize(w.rec, io, w.ranges, w.ctl, c->gp, img,
+                                    (c->cfg.flags & KT_GS_FLAG_EXIT_PER_ELEMENT) != 0, stream));
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[5], stream));
+    KT_TRY_CUDA(c, cudaMemcpyAsync(w.host_ctl, w.ctl, kCtlHeaderBytes, cudaMemcpyDeviceToHost, stream));
+    KT_TRY_CUDA(c, cudaEventRecord(w.done_ev, stream));
+    w.have_frame = true;
+    w.frame_n = n;
+    return KT_OK;
+}
+
+// Wait for the path's last frame and translate its device error flags.
+kt_status check_frame(kt_gs_ctx* c, PathWs& w) {
+    if (!w.have_frame) return KT_OK;
+    KT_TRY_CUDA(c, cudaEventSynchronize(w.done_ev));
+    const uint32_t e = w.host_ctl->error_flags;
+    if (e & kErrTimeout) return fail(c, KT_ERR_TIMEOUT, "a decoupled look-back wait timed out");
+    if (e & kErrCapacity)
+        return fail(c, KT_ERR_CAPACITY, "frame needs " + std::to_string(w.host_ctl->num_keys) +
+                                            " keys, capacity is " + std::to_string(w.cap));
+    return KT_OK;
+}
+
+kt_status render_impl(kt_gs_ctx* c, uint32_t path, Source src, const kt_camera_mvp* cam,
+                      uchar4* img, cudaStream_t stream) {
+    if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
+    if (src == Source::Scene && !c->has_scene)
+        return fail(c, KT_ERR_STATE, "no Gaussians set on this context");
+    if (!img) return fail(c, KT_ERR_ARG, "output image is NULL");
+    KT_TRY_CUDA(c, cudaSetDevice(c->device));
+    PathWs& w = c->paths[path];
+    kt_status s = ensure_path_base(c, w);
+    if (s != KT_OK) return s;
+    const uint64_t n = src == Source::Scene ? c->n : w.g2d_n;
+    if ((s = ensure_n(c, w, n)) != KT_OK) return s;
+    if (w.cap == 0) {
+        uint64_t guess = c->cfg.key_capacity ? c->cfg.key_capacity : std::max<uint64_t>(16 * n, 1u << 20);
+        guess = std::min(guess, kMaxKeyCapacity);
+        if ((s = ensure_cap(c, w, guess)) != KT_OK) return s;
+    }
+    CamParams cp{};
+    if (cam) cp = make_cam(cam);
+    const bool async = (c->cfg.flags & KT_GS_FLAG_ASYNC) != 0;
+    for (int attempt = 0; attempt < 4; ++attempt) {
+        if ((s = enqueue_frame(c, w, src, cam ? &cp : nullptr, img, stream)) != KT_OK) return s;
+        if (async) return KT_OK;
+        s = check_frame(c, w);
+        if (s != KT_ERR_CAPACITY || (c->cfg.flags & KT_GS_FLAG_NO_AUTOGROW)) return s;
+        const uint64_t need = w.host_ctl->num_keys;
+        const uint64_t grow = need + need / 4 + kSortTile;
+        if ((s = ensure_cap(c, w, std::min(grow, kMaxKeyCapacity))) != KT_OK) return s;
+        if (need > w.cap) return fail(c, KT_ERR_CAPACITY, "key count exceeds the maximum capacity");
+    }
+    return fail(c, KT_ERR_CAPACITY, "key buffers kept overflowing");
+}
+
+int detect_degree(const kt_gaussian3d* g, uint64_t n) {
+    int deg = 0;
+    for (uint64_t i = 0; i < n && deg < 3; ++i) {
+        const float* bands[3] = {g[i].shR, g[i].shG, g[i].shB};
+        for (int ch = 0; ch < 3; ++ch)
+            for (int k = 0; k < 15; ++k)
+                if (bands[ch][k] != 0.0f) {
+                    const int d = k < 3 ? 1 : (k < 8 ? 2 : 3);
+                    deg = std::max(deg, d);
+                }
+    }
+    return deg;
+}
+
+kt_status upload_scene(kt_gs_ctx* c, const kt_gaussian3d* src, bool src_on_device, uint64_t n,
+                       int deg, cudaStream_t stream) {
+    KT_TRY_CUDA(c, cudaSetDevice(c->device));
+    dfree(c->pos); dfree(c->rot); dfree(c->scale); dfree(c->sh);
+    c->has_scene = false;
+    c->n = n;
+    c->deg = deg;
+    c->nplanes = (uint32_t)((3 * (deg + 1) * (deg + 1) + 3) / 4);
+    const uint64_t m = std::max<uint64_t>(n, 1);
+    KT_TRY_CUDA(c, cudaMalloc(&c->pos, sizeof(float4) * m));
+    KT_TRY_CUDA(c, cudaMalloc(&c->rot, sizeof(float4) * m));
+    KT_TRY_CUDA(c, cudaMalloc(&c->scale, sizeof(float4) * m));
+    KT_TRY_CUDA(c, cudaMalloc(&c->sh, sizeof(float4) * m * c->nplanes));
+    if (n > 0) {
+        const float* aos = reinterpret_cast<const float*>(src);
+        float* tmp = nullptr;
+        if (!src_on_device) {
+            KT_TRY_CUDA(c, cudaMalloc(&tmp, sizeof(kt_gaussian3d) * n));
+            KT_TRY_CUDA(c, cudaMemcpyAsync(tmp, src, sizeof(kt_gaussian3d) * n, cudaMemcpyHostToDevice, stream));
+            aos = tmp;
+        }
+        cudaError_t e = launch_pack_scene(aos, n, c->pos, c->rot, c->scale, c->sh, deg, c->nplanes, stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        if (tmp) cudaFree(tmp);
+        KT_TRY_CUDA(c, e);
+    }
+    c->has_scene = true;
+    return KT_OK;
+}
+
+// compact key (bin << dbits | depth - dmin) -> reference key (bin << 32 | depth)
+void expand_keys(unsigned long long* k, uint64_t count, uint32_t dbits, uint32_t dmin) {
+    const unsigned long long m = dbits >= 64 ? ~0ull : ((1ull << dbits) - 1ull);
+    for (uint64_t i = 0; i < count; ++i) {
+        const unsigned long long bin = dbits >= 64 ? 0ull : (k[i] >> dbits);
+        const uint32_t depth = (uint32_t)((k[i] & m) + dmin);
+        k[i] = (bin << 32) | depth;
+    }
+}
+
+}  // namespace
+
+// ======================================================================= C ABI
+
+extern "C" {
+
+void kt_gs_config_default(kt_gs_config* cfg) {
+    if (!cfg) return;
+    std::memset(cfg, 0, sizeof(*cfg));
+    cfg->width = 512;
+    cfg->height = 512;
+    cfg->bin_width = 128;
+    cfg->bin_height = 128;
+    cfg->sh_degree = 3;
+    cfg->cull_z = 1.0f;
+    cfg->flags = 0;
+    cfg->num_paths = 1;
+    cfg->key_capacity = 0;
+    cfg->tile_row_begin = 0;
+    cfg->tile_row_end = 0;
+}
+
+int kt_gs_abi_version(void) { return KT_GS_ABI_VERSION; }
+
+const char* kt_gs_status_string(kt_status s) {
+    switch (s) {
+        case KT_OK: return "KT_OK";
+        case KT_ERR_ARG: return "KT_ERR_ARG";
+        case KT_ERR_CUDA: return "KT_ERR_CUDA";
+        case KT_ERR_CAPACITY: return "KT_ERR_CAPACITY";
+        case KT_ERR_TIMEOUT: return "KT_ERR_TIMEOUT";
+        case KT_ERR_NCCL: return "KT_ERR_NCCL";
+        case KT_ERR_IO: return "KT_ERR_IO";
+        case KT_ERR_STATE: return "KT_ERR_STATE";
+        case KT_ERR_NOMEM: return "KT_ERR_NOMEM";
+    }
+    return "KT_ERR_UNKNOWN";
+}
+
+kt_status kt_gs_create(const kt_gs_config* cfg, int device, kt_gs_ctx** out) {
+    if (!cfg || !out) return KT_ERR_ARG;
+    *out = nullptr;
+    if (cfg->width == 0 || cfg->height == 0 || cfg->width > 65535 * 16 || cfg->height > 65535 * 16)
+        return KT_ERR_ARG;
+    if (cfg->bin_width == 0 || cfg->bin_height == 0 || cfg->bin_width % 16 != 0 ||
+        cfg->bin_height % 16 != 0)
+        return KT_ERR_ARG;
+    if (cfg->sh_degree < -1 || cfg->sh_degree > 3) return KT_ERR_ARG;
+    if (cfg->num_paths == 0 || cfg->num_paths > 16) return KT_ERR_ARG;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return KT_ERR_CUDA;
+    if (cudaSetDevice(device) != cudaSuccess) return KT_ERR_CUDA;
+    kt_gs_ctx* c = new (std::nothrow) kt_gs_ctx();
+    if (!c) return KT_ERR_NOMEM;
+    c->cfg = *cfg;
+    c->device = device;
+    c->gp = make_grid(*cfg);
+    c->max_passes = (c->gp.tile_bits + 32 + 7) / 8;
+    c->paths.resize(cfg->num_paths);
+    *out = c;
+    return KT_OK;
+}
+
+kt_status kt_gs_destroy(kt_gs_ctx* c) {
+    if (!c) return KT_OK;
+    cudaSetDevice(c->device);
+    for (auto& w : c->paths) {
+        if (w.have_frame && w.done_ev) cudaEventSynchronize(w.done_ev);
+        free_path(w);
+    }
+    dfree(c->pos); dfree(c->rot); dfree(c->scale); dfree(c->sh);
+    delete c;
+    return KT_OK;
+}
+
+const char* kt_gs_last_error(const kt_gs_ctx* c) { return c ? c->err.c_str() : "null context"; }
+
+kt_status kt_gs_get_config(const kt_gs_ctx* c, kt_gs_config* cfg) {
+    if (!c || !cfg) return KT_ERR_ARG;
+    *cfg = c->cfg;
+    if (c->has_scene) cfg->sh_degree = c->deg;
+    return KT_OK;
+}
+
+kt_status kt_gs_set_gaussians(kt_gs_ctx* c, const kt_gaussian3d* host, uint64_t n) {
+    if (!c) return KT_ERR_ARG;
+    if (n > 0 && !host) return fail(c, KT_ERR_ARG, "NULL Gaussian array");
+    if (n > 0xFFFFFFFFull) return fail(c, KT_ERR_ARG, "more than 2^32-1 Gaussians");
+    const int deg = c->cfg.sh_degree >= 0 ? c->cfg.sh_degree : detect_degree(host, n);
+    return upload_scene(c, host, false, n, deg, nullptr);
+}
+
+kt_status kt_gs_set_gaussians_device(kt_gs_ctx* c, const kt_gaussian3d* dev, uint64_t n,
+                                     void* stream) {
+    if (!c) return KT_ERR_ARG;
+    if (n > 0 && !dev) return fail(c, KT_ERR_ARG, "NULL Gaussian array");
+    if (n > 0xFFFFFFFFull) return fail(c, KT_ERR_ARG, "more than 2^32-1 Gaussians");
+    const int deg = c->cfg.sh_degree >= 0 ? c->cfg.sh_degree : 3;
+    return upload_scene(c, dev, true, n, deg, (cudaStream_t)stream);
+}
+
+kt_status kt_gs_render(kt_gs_ctx* c, const kt_camera_mvp* cam, void* d_rgba8, uint32_t path,
+                       void* stream) {
+    if (!c) return KT_ERR_ARG;
+    if (!cam) return fail(c, KT_ERR_ARG, "camera is NULL");
+    return render_impl(c, path, Source::Scene, cam, (uchar4*)d_rgba8, (cudaStream_t)stream);
+}
+
+kt_status kt_gs_render_host(kt_gs_ctx* c, const kt_camera_mvp* cam, void* h_rgba8, uint32_t path,
+                            void* stream) {
+    if (!c) return KT_ERR_ARG;
+    if (!cam || !h_rgba8) return fail(c, KT_ERR_ARG, "NULL camera or image");
+    if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
+    KT_TRY_CUDA(c, cudaSetDevice(c->device));
+    PathWs& w = c->paths[path];
+    const size_t bytes = (size_t)c->cfg.width * c->cfg.height * 4;
+    if (!w.img) KT_TRY_CUDA(c, cudaMalloc(&w.img, bytes));
+    cudaStream_t s = (cudaStream_t)stream;
+    KT_TRY_CUDA(c, cudaMemcpyAsync(w.img, h_rgba8, bytes, cudaMemcpyHostToDevice, s));
+    const uint32_t saved = c->cfg.flags;
+    c->cfg.flags &= ~KT_GS_FLAG_ASYNC;
+    kt_status st = render_impl(c, path, Source::Scene, cam, w.img, s);
+    c->cfg.flags = saved;
+    if (st != KT_OK) return st;
+    KT_TRY_CUDA(c, cudaMemcpyAsync(h_rgba8, w.img, bytes, cudaMemcpyDeviceToHost, s));
+    KT_TRY_CUDA(c, cudaStreamSynchronize(s));
+    return KT_OK;
+}
+
+kt_status kt_gs_render_batch(kt_gs_ctx* c, const kt_camera_mvp* cams, uint32_t n_views,
+                             void* const* d_rgba8, void* stream) {
+    if (!c) return KT_ERR_ARG;
+    if (n_views > 0 && (!cams || !d_rgba8)) return fail(c, KT_ERR_ARG, "NULL cameras or images");
+    for (uint32_t v = 0; v < n_views; ++v) {
+        kt_status s = render_impl(c, 0, Source::Scene, &cams[v], (uchar4*)d_rgba8[v], (cudaStream_t)stream);
+        if (s != KT_OK) return s;
+    }
+    return KT_OK;
+}
+
+kt_status kt_gs_render_projected(kt_gs_ctx* c, const kt_gaussian2d* host, uint64_t n,
+                                 void* d_rgba8, uint32_t path, void* stream) {
+    if (!c) return KT_ERR_ARG;
+    if (n > 0 && !host) return fail(c, KT_ERR_ARG, "NULL record array");
+    if (n > 0xFFFFFFFFull) return fail(c, KT_ERR_ARG, "more than 2^32-1 records");
+    if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
+    KT_TRY_CUDA(c, cudaSetDevice(c->device));
+    PathWs& w = c->paths[path];
+    if (n > w.g2d_n || !w.g2d) {
+        dfree(w.g2d);
+        KT_TRY_CUDA(c, cudaMalloc(&w.g2d, sizeof(kt_gaussian2d) * std::max<uint64_t>(n, 1)));
+    }
+    w.g2d_n = n;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (n) KT_TRY_CUDA(c, cudaMemcpyAsync(w.g2d, host, sizeof(kt_gaussian2d) * n, cudaMemcpyHostToDevice, s));
+    return render_impl(c, path, Source::Projected, nullptr, (uchar4*)d_rgba8, s);
+}
+
+kt_status kt_gs_sync(kt_gs_ctx* c, uint32_t path) {
+    if (!c) return KT_ERR_ARG;
+    if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
+    KT_TRY_CUDA(c, cudaSetDevice(c->device));
+    PathWs& w = c->paths[path];
+    kt_status s = check_frame(c, w);
+    if (s != KT_OK || !w.totals) return s;
+    unsigned int sticky = 0;
+    KT_TRY_CUDA(c, cudaMemcpy(&sticky, &w.totals->sticky_errors, sizeof(sticky), cudaMemcpyDeviceToHost));
+    KT_TRY_CUDA(c, cudaMemset(&w.totals->sticky_errors, 0, sizeof(sticky)));
+    if (sticky & kErrTimeout) return fail(c, KT_ERR_TIMEOUT, "a frame since the last sync timed out in a look-back wait");
+    if (sticky & kErrCapacity)
+        return fail(c, KT_ERR_CAPACITY, "a frame since the last sync overflowed the key buffers (nothing drawn)");
+    return KT_OK;
+}
+
+kt_status kt_gs_frame_stats(kt_gs_ctx* c, uint32_t path, kt_gs_stats* out) {
+    if (!c || !out) return KT_ERR_ARG;
+    if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
+    KT_TRY_CUDA(c, cudaSetDevice(c->device));
+    PathWs& w = c->paths[path];
+    std::memset(out, 0, sizeof(*out));
+    out->tiles_x = c->gp.tiles_x;
+    out->tiles_y = c->gp.tiles_y;
+    out->key_capacity = w.cap;
+    if (!w.have_frame) return KT_OK;
+    KT_TRY_CUDA(c, cudaEventSynchronize(w.done_ev));
+    const FrameCtl& h = *w.host_ctl;
+    out->num_gaussians = w.frame_n;
+    out->num_keys = h.num_keys;
+    out->num_visible = h.num_visible;
+    out->key_bits = h.key_bits;
+    out->depth_bits = h.depth_bits;
+    out->sort_passes = h.passes_run;
+    out->error_flags = h.error_flags;
+    out->depth_min_bits = h.depth_min;
+    out->depth_max_bits = h.depth_max;
+    out->status_bytes = (uint32_t)kCtlHeaderBytes;
+    out->launches = 6 + c->max_passes;
+    return KT_OK;
+}
+
+kt_status kt_gs_counters_take(kt_gs_ctx* c, uint32_t path, kt_gs_counters* out) {
+    if (!c || !out) return KT_ERR_ARG;
+    if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
+    KT_TRY_CUDA(c, cudaSetDevice(c->device));
+    PathWs& w = c->paths[path];
+    std::memset(out, 0, sizeof(*out));
+    if (!w.totals) return KT_OK;
+    if (w.have_frame) KT_TRY_CUDA(c, cudaEventSynchronize(w.done_ev));
+    FrameTotals t;
+    KT_TRY_CUDA(c, cudaMemcpy(&t, w.totals, sizeof(t), cudaMemcpyDeviceToHost));
+    out->frames = t.frames;
+    out->keys = t.keys;
+    out->key_passes = t.key_passes;
+    out->visible = t.visible;
+    // reset the counters; the sticky error bits stay until kt_gs_sync reports them
+    KT_TRY_CUDA(c, cudaMemset(w.totals, 0, offsetof(FrameTotals, sticky_errors)));
+    return KT_OK;
+}
+
+kt_status kt_gs_set_flags(kt_gs_ctx* c, uint32_t flags) {
+    if (!c) return KT_ERR_ARG;
+    c->cfg.flags = flags;
+    return KT_OK;
+}
+
+kt_status kt_gs_debug_dump(kt_gs_ctx* c, uint32_t path, kt_gs_stage stage, void* dst,
+                           uint64_t bytes, uint64_t* written) {
+    if (!c) return KT_ERR_ARG;
+    if (written) *written = 0;
+    if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
+    KT_TRY_CUDA(c, cudaSetDevice(c->device));
+    PathWs& w = c->paths[path];
+    if (!w.have_frame) return fail(c, KT_ERR_STATE, "no frame rendered on this path");
+    KT_TRY_CUDA(c, cudaEventSynchronize(w.done_ev));
+    const FrameCtl& h = *w.host_ctl;
+    const uint64_t n = w.frame_n;
+    const uint64_t K = h.num_keys;
+    const bool sorted_ok = h.plan_ok != 0;
+    uint64_t need = 0;
+    const void* src = nullptr;
+    switch (stage) {
+        case KT_GS_STAGE_PROJECTED: need = n * sizeof(kt_gaussian2d); break;
+        case KT_GS_STAGE_TILE_COUNTS: need = n * 4; src = w.counts; break;
+        case KT_GS_STAGE_OFFSETS: need = n * 8; src = w.offsets; break;
+        case KT_GS_STAGE_KEYS_UNSORTED:
+            if (!w.dbg_keys && K) return fail(c, KT_ERR_STATE, "unsorted keys need KT_GS_FLAG_KEEP_UNSORTED");
+            need = w.dbg_count * 8; src = w.dbg_keys; break;
+        case KT_GS_STAGE_VALUES_UNSORTED:
+            if (!w.dbg_vals && K) return fail(c, KT_ERR_STATE, "unsorted values need KT_GS_FLAG_KEEP_UNSORTED");
+            need = w.dbg_count * 4; src = w.dbg_vals; break;
+        case KT_GS_STAGE_KEYS_SORTED:
+            if (!sorted_ok) return fail(c, KT_ERR_STATE, "the last frame was not sorted");
+            need = K * 8; src = w.keys[h.final_buf]; break;
+        case KT_GS_STAGE_VALUES_SORTED:
+            if (!sorted_ok) return fail(c, KT_ERR_STATE, "the last frame was not sorted");
+            need = K * 4; src = w.vals[h.final_buf]; break;
+        case KT_GS_STAGE_TILE_RANGES: need = (uint64_t)ntiles(c) * 8; src = w.ranges; break;
+        default: return fail(c, KT_ERR_ARG, "unknown stage");
+    }
+    if (!dst) {
+        if (written) *written = need;
+        return KT_OK;
+    }
+    if (bytes < need) return fail(c, KT_ERR_ARG, "buffer too small: need " + std::to_string(need) + " bytes");
+    if (stage == KT_GS_STAGE_PROJECTED) {
+        std::vector<float4> rec(3 * n);
+        if (n) KT_TRY_CUDA(c, cudaMemcpy(rec.data(), w.rec, sizeof(float4) * 3 * n, cudaMemcpyDeviceToHost));
+        kt_gaussian2d* o = (kt_gaussian2d*)dst;
+        for (uint64_t i = 0; i < n; ++i) {
+            const float4 a = rec[3 * i], b = rec[3 * i + 1], cc = rec[3 * i + 2];
+            o[i].position[0] = a.x;
+            o[i].position[1] = a.y;
+            o[i].z = a.w;
+            o[i].binMask = 0xFFFFFFFFu;
+            o[i].covInv[0] = b.x;
+            o[i].covInv[1] = b.y;
+            o[i].covInv[2] = b.z;
+            o[i].covInv[3] = b.w;
+            o[i].color[0] = cc.x;
+            o[i].color[1] = cc.y;
+            o[i].color[2] = cc.z;
+            o[i].alpha = a.z;
+        }
+    } else if (need) {
+        KT_TRY_CUDA(c, cudaMemcpy(dst, src, need, cudaMemcpyDeviceToHost));
+        if (stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_KEYS_UNSORTED)
+            expand_keys((unsigned long long*)dst, need / 8, h.depth_bits, h.depth_min);
+    }
+    if (written) *written = need;
+    return KT_OK;
+}
+
+kt_status kt_gs_stage_times(kt_gs_ctx* c, uint32_t path, float ms[KT_GS_NSTAGES]) {
+    if (!c || !ms) return KT_ERR_ARG;
+    if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
+    PathWs& w = c->paths[path];
+    if (!w.have_frame || !w.timed) return fail(c, KT_ERR_STATE, "no timed frame (KT_GS_FLAG_TIMING)");
+    KT_TRY_CUDA(c, cudaSetDevice(c->device));
+    KT_TRY_CUDA(c, cudaEventSynchronize(w.done_ev));
+    cudaEvent_t* ev = w.ring[w.ring_last];
+    KT_TRY_CUDA(c, cudaEventSynchronize(ev[5]));
+    for (int i = 0; i < 5; ++i) KT_TRY_CUDA(c, cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]));
+    KT_TRY_CUDA(c, cudaEventElapsedTime(&ms[5], ev[0], ev[5]));
+    return KT_OK;
+}
+
+kt_status kt_gs_stage_times_total(kt_gs_ctx* c, uint32_t path, double ms_total[KT_GS_NSTAGES],
+                                  uint64_t* frames) {
+    if (!c || !ms_total) return KT_ERR_ARG;
+    if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
+    KT_TRY_CUDA(c, cudaSetDevice(c->device));
+    PathWs& w = c->paths[path];
+    for (int k = 0; k < PathWs::kRing; ++k) {
+        const int slot = (w.ring_next + k) % PathWs::kRing;  // oldest first
+        kt_status s = drain_slot(c, w, slot);
+        if (s != KT_OK) return s;
+    }
+    for (int i = 0; i < KT_GS_NSTAGES; ++i) {
+        ms_total[i] = w.stage_sum[i];
+        w.stage_sum[i] = 0.0;
+    }
+    if (frames) *frames = w.timed_frames;
+    w.timed_frames = 0;
+    return KT_OK;
+}
+
+kt_status kt_gs_load_spz(kt_gs_ctx* c, const char* path) {
+    if (!c) return KT_ERR_ARG;
+    return fail(c, KT_ERR_IO, std::string("spz loading is not available in this build: ") +
+                                  (path ? path : "(null)"));
+}
+
+kt_status kt_gs_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* vals_in,
+                                 uint64_t* keys_out, uint32_t* vals_out, uint64_t n,
+                                 uint32_t key_bits, void* d_temp, size_t* temp_bytes,
+                                 void* stream) {
+    if (!temp_bytes || key_bits > 64) return KT_ERR_ARG;
+    const size_t ctl_bytes = (sizeof(FrameCtl) + 255) & ~size_t(255);
+    const size_t kbytes = ((size_t)n * 8 + 255) & ~size_t(255);
+    const size_t vbytes = ((size_t)n * 4 + 255) & ~size_t(255);
+    const size_t sbytes = sort_status_words(n) * 8;
+    const size_t total = ctl_bytes + kbytes + vbytes + sbytes;
+    if (!d_temp) {
+        *temp_bytes = total;
+        return KT_OK;
+    }
+    if (*temp_bytes < total) return KT_ERR_ARG;
+    if (n == 0) return KT_OK;
+    if (n > kMaxKeyCapacity || !keys_in || !vals_in || !keys_out || !vals_out) return KT_ERR_ARG;
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned char* t = (unsigned char*)d_temp;
+    FrameCtl* ctl = (FrameCtl*)t;
+    unsigned long long* alt_k = (unsigned long long*)(t + ctl_bytes);
+    uint32_t* alt_v = (uint32_t*)(t + ctl_bytes + kbytes);
+    unsigned long long* status = (unsigned long long*)(t + ctl_bytes + kbytes + vbytes);
+    const uint32_t max_passes = std::max<uint32_t>(1, (key_bits + 7) / 8);
+    if (cudaMemsetAsync(ctl, 0, sizeof(FrameCtl), s) != cudaSuccess) return KT_ERR_CUDA;
+    if (cudaMemsetAsync(status, 0, sbytes, s) != cudaSuccess) return KT_ERR_CUDA;
+    if (launch_key_histogram((const unsigned long long*)keys_in, n, key_bits, ctl, s) != cudaSuccess)
+        return KT_ERR_CUDA;
+    if (launch_plan(ctl, n, max_passes, 1, s) != cudaSuccess) return KT_ERR_CUDA;
+    SortIO io{};
+    io.keys[0] = (unsigned long long*)keys_in;
+    io.keys[1] = alt_k;
+    io.keys[2] = (unsigned long long*)keys_out;
+    io.vals[0] = (uint32_t*)vals_in;
+    io.vals[1] = alt_v;
+    io.vals[2] = vals_out;
+    for (uint32_t p = 0; p < max_passes; ++p)
+        if (launch_sort_pass(io, ctl, status, p, p + 1, n, s) != cudaSuccess) return KT_ERR_CUDA;
+    return KT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,136 @@
+// Internal types shared by the renderer's kernels and its host code.
+//
+// Device data layout (per context):
+//   scene planes   pos   float4[N]  (x, y, z, alpha)
+//                  rot   float4[N]  (x, y, z, w)
+//                  scale float4[N]  (sx, sy, sz, 0)
+//                  sh    float4[P][N], P = ceil(3 (d+1)^2 / 4): the SH coefficients of
+//                        degree d interleaved per coefficient (R,G,B), DC first
+//   per path       rec   float4[3N] (px, py, alpha, z) (covInv 00,01,10,11) (r, g, b, 0)
+//                  counts u32[N], rect u32x2[N] (x0|x1<<16, y0|y1<<16), depth u32[N],
+//                  offsets u64[N], keys u64[2][cap], vals u32[2][cap],
+//                  ranges u32x2[tiles], look-back status words, FrameCtl.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace kt {
+
+constexpr int kMaxPasses = 8;          // 8-bit digits over at most 64 key bits
+constexpr uint32_t kErrCapacity = 1u;  // key count above the key buffers' capacity
+constexpr uint32_t kErrTimeout = 2u;   // a look-back wait ran out of iterations
+constexpr uint32_t kSpinLimit = 1u << 22;  // look-back polls before giving up (~seconds)
+
+// Look-back status word: [epoch:24][flag:2][value:38].
+constexpr uint64_t kFlagAggregate = 1ull;
+constexpr uint64_t kFlagInclusive = 2ull;
+constexpr int kValueBits = 38;
+constexpr uint64_t kValueMask = (1ull << kValueBits) - 1ull;
+constexpr uint32_t kEpochMax = (1u << 24) - 1u;
+
+__host__ __device__ inline uint64_t pack_status(uint32_t epoch, uint64_t flag, uint64_t value) {
+    return ((uint64_t)epoch << 40) | (flag << kValueBits) | (value & kValueMask);
+}
+__host__ __device__ inline uint32_t status_epoch(uint64_t w) { return (uint32_t)(w >> 40); }
+__host__ __device__ inline uint64_t status_flag(uint64_t w) { return (w >> kValueBits) & 3ull; }
+__host__ __device__ inline uint64_t status_value(uint64_t w) { return w & kValueMask; }
+
+// Per-frame control block in device memory, reset by k_frame_init.
+struct FrameCtl {
+    unsigned long long num_keys;      // K, written by the last scan chunk
+    unsigned int depth_min;           // min / max of floatBitsToUint(z) ^ 0x80000000
+    unsigned int depth_max;           //   over Gaussians with a non-zero tile count
+    unsigned int num_visible;         // Gaussians with a non-zero tile count
+    unsigned int error_flags;         // kErr*
+    unsigned int scan_ticket;         // chunk ticket of the scan/emit kernel
+    unsigned int plan_ok;             // set by k_plan when the sort may run
+    unsigned int depth_bits;          // set by the emit kernel (all CTAs agree)
+    unsigned int key_bits;
+    unsigned int passes_run;
+    unsigned int final_buf;           // which key/value buffer holds the sorted data
+    unsigned int pass_ticket[kMaxPasses];
+    unsigned int pass_run[kMaxPasses];
+    unsigned int pass_src[kMaxPasses];
+    unsigned int pass_dst[kMaxPasses];
+    unsigned int pass_mask[kMaxPasses];  // digit mask: 255, or fewer bits in the last pass
+    unsigned int hist[kMaxPasses][256];   // digit histograms of the keys
+    unsigned int base[kMaxPasses][256];   // exclusive scans of hist
+};
+
+// Device-side totals over frames (kt_gs_counters), accumulated by the ranges kernel.
+struct FrameTotals {
+    unsigned long long frames;
+    unsigned long long keys;
+    unsigned long long key_passes;
+    unsigned long long visible;
+    unsigned int sticky_errors;  // error bits of every frame since the last sync
+    unsigned int pad;
+};
+
+// Camera values derived once per frame on the host (same formulas as the shader).
+struct CamParams {
+    float pvm[16];   // ubo.proj * ubo.view * ubo.model
+    float mv[16];    // ubo.model * ubo.view
+    float focal_x;   // ubo.proj[0][0]
+    float focal_y;   // ubo.proj[1][1]
+};
+
+// Screen / binning geometry.
+struct GridParams {
+    float half_w, half_h;        // W/2, H/2 (256 at 512: gsplat_projection.comp:202)
+    float sxx, syy, sxy;         // covariance scale (512*512 at 512: comp:208)
+    float cell_w, cell_h;        // bin size in px, as float
+    float cull_z;
+    uint32_t tiles_x, tiles_y;
+    uint32_t row_begin, row_end; // binned bin rows [begin, end)
+    uint32_t width, height;
+    uint32_t bin_w, bin_h;       // bin size in px
+    uint32_t tile_bits;          // bits of (tiles_x * tiles_y - 1)
+};
+
+struct SceneDev {
+    const float4* pos;
+    const float4* rot;
+    const float4* scale;
+    const float4* sh;   // planes of n float4
+    uint32_t nplanes;
+    int deg;
+    uint64_t n;
+};
+
+struct FrameBufs {
+    float4* rec;
+    uint32_t* counts;
+    uint2* rect;
+    uint32_t* depth;
+    unsigned long long* offsets;
+    unsigned long long* keys[2];
+    uint32_t* vals[2];
+    uint2* ranges;
+    unsigned long long* scan_status;
+    unsigned long long* sort_status;
+    FrameCtl* ctl;
+    uint64_t key_capacity;
+};
+
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// SM count of the current device (cached per device).
+int device_sm_count();
+
+__host__ __device__ inline uint32_t bits_for(uint64_t v) {
+    uint32_t b = 0;
+    while (b < 64 && (v >> b) != 0) ++b;
+    return b;
+}
+
+}  // namespace kt

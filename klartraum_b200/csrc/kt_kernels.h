@@ -1,0 +1,59 @@
+// Host-side launchers of the renderer's kernels (one .cu file per stage).
+#pragma once
+
+#include "kt_common.cuh"
+
+namespace kt {
+
+// Key/value buffers of the sort: render path uses [0]/[1] ping-pong; the standalone
+// operator uses [0] = input, [1] = scratch, [2] = output.
+struct SortIO {
+    unsigned long long* keys[3];
+    uint32_t* vals[3];
+};
+
+// Buffer i of a SortIO without dynamic indexing of the kernel-parameter array (which would
+// force a local-memory copy).
+__device__ __forceinline__ unsigned long long* io_keys(const SortIO& io, uint32_t i) {
+    return i == 0 ? io.keys[0] : (i == 1 ? io.keys[1] : io.keys[2]);
+}
+__device__ __forceinline__ uint32_t* io_vals(const SortIO& io, uint32_t i) {
+    return i == 0 ? io.vals[0] : (i == 1 ? io.vals[1] : io.vals[2]);
+}
+
+constexpr int kScanChunk = 2048;  // Gaussians per scan/emit CTA
+constexpr int kSortTile = 4096;   // keys per onesweep CTA iteration
+
+// project.cu (compiled with -fmad=false)
+cudaError_t launch_project_count(const SceneDev& sc, const CamParams& cam, const GridParams& gp,
+                                 const FrameBufs& fb, cudaStream_t stream);
+cudaError_t launch_load_projected(const float* d_g2d, uint64_t n, const GridParams& gp,
+                                  const FrameBufs& fb, cudaStream_t stream);
+cudaError_t launch_pack_scene(const float* d_aos, uint64_t n, float4* pos, float4* rot,
+                              float4* scale, float4* sh, int deg, uint32_t nplanes,
+                              cudaStream_t stream);
+
+// binning.cu
+cudaError_t launch_frame_init(FrameCtl* ctl, uint2* ranges, uint32_t ntiles, cudaStream_t stream);
+cudaError_t launch_scan_emit(const FrameBufs& fb, const GridParams& gp, uint64_t n, uint32_t epoch,
+                             uint32_t max_passes, cudaStream_t stream);
+// mode 0: ping-pong between io.keys[0] and [1]; mode 1: [0] -> ... -> [2] via [1]
+cudaError_t launch_plan(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes, int mode,
+                        cudaStream_t stream);
+cudaError_t launch_ranges(const SortIO& io, const FrameCtl* ctl, uint2* ranges, FrameTotals* totals,
+                          cudaStream_t stream);
+
+// sort.cu
+cudaError_t launch_key_histogram(const unsigned long long* keys, uint64_t n, uint32_t key_bits,
+                                 FrameCtl* ctl, cudaStream_t stream);
+cudaError_t launch_sort_pass(const SortIO& io, FrameCtl* ctl, unsigned long long* status,
+                             uint32_t pass, uint32_t epoch, uint64_t max_keys,
+                             cudaStream_t stream);
+size_t sort_status_words(uint64_t max_keys);
+
+// raster.cu
+cudaError_t launch_rasterize(const float4* rec, const SortIO& io, const uint2* ranges,
+                             const FrameCtl* ctl, const GridParams& gp, uchar4* img,
+                             bool per_element_exit, cudaStream_t stream);
+
+}  // namespace kt

@@ -1,0 +1,129 @@
+// K6: front-to-back splatting, one CTA per 16x16 pixel block, one thread per pixel.
+//
+// Restates shaders/gsplat/gsplat_binned_splatting.comp:41-125 per pixel:
+//   a = exp(-0.5 * dot(d, covInv * d)) * alpha, d = pixel - mean (integer pixel coordinates)
+//   C += color * a * T;  T *= 1 - a
+//   out = clamp(in + vec4(C, 1) * (1 - T), 0, 1) stored as RGBA8 (read-modify-write).
+// A pixel stops once T <= 1 - 0.9999, tested (reference mode) only at the end of each
+// 64-Gaussian batch counted from the bin's start; after such a stop the reference's tail
+// loop still blends the first element past the last full batch (comp:104-117). With
+// KT_GS_FLAG_EXIT_PER_ELEMENT the test runs after every Gaussian.
+//
+// The CTA stages 256 sorted Gaussians at a time in shared memory (each thread gathers one
+// 48-B record by index) and leaves the list as soon as every pixel of the block is done.
+#include "kt_common.cuh"
+#include "kt_kernels.h"
+
+namespace kt {
+namespace {
+
+constexpr int kRasterThreads = 256;
+constexpr int kBatch = 256;
+
+template <bool PER_ELEM>
+__global__ void __launch_bounds__(kRasterThreads)
+k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__ ranges,
+            const FrameCtl* __restrict__ ctl, GridParams gp, uchar4* __restrict__ img,
+            uint32_t ypix0) {
+    __shared__ float4 s_pos[kBatch];  // px, py, alpha, z
+    __shared__ float4 s_cov[kBatch];  // covInv 00, 01, 10, 11
+    __shared__ float4 s_col[kBatch];  // r, g, b
+    if (!ctl->plan_ok) return;
+
+    const int tid = threadIdx.x;
+    const uint32_t bx0 = blockIdx.x * 16, by0 = ypix0 + blockIdx.y * 16;
+    const uint32_t px = bx0 + (tid & 15), py = by0 + (tid >> 4);
+    const bool inside = px < gp.width && py < gp.height;
+    const uint32_t bin = (by0 / gp.bin_h) * gp.tiles_x + bx0 / gp.bin_w;
+    const uint2 r = ranges[bin];
+    const uint32_t start = r.x, end = r.y;
+    const uint32_t preend = start + ((end - start) / 64) * 64;
+    const uint32_t* __restrict__ vals = io_vals(io, ctl->final_buf);
+    const float tmin = (float)(1.0 - 0.9999);
+    const float fx = (float)px, fy = (float)py;
+
+    float C0 = 0.0f, C1 = 0.0f, C2 = 0.0f, T = 1.0f;
+    bool done = !inside;
+    uint32_t skip_until = start;
+
+    for (uint32_t b = start; b < end; b += kBatch) {
+        if (__syncthreads_and(done)) break;
+        const uint32_t nb = min((uint32_t)kBatch, end - b);
+        if ((uint32_t)tid < nb) {
+            const uint32_t idx = vals[b + tid];
+            s_pos[tid] = rec[3 * (uint64_t)idx + 0];
+            s_cov[tid] = rec[3 * (uint64_t)idx + 1];
+            s_col[tid] = rec[3 * (uint64_t)idx + 2];
+        }
+        __syncthreads();
+        if (done) continue;
+        for (uint32_t jj = 0; jj < nb; ++jj) {
+            const uint32_t pos = b + jj;
+            if (pos < skip_until) continue;
+            const float4 p = s_pos[jj];
+            const float4 c = s_cov[jj];
+            const float dx = fx - p.x, dy = fy - p.y;
+            const float sx = c.x * dx + c.z * dy;
+            const float sy = c.y * dx + c.w * dy;
+            const float distance = dx * sx + dy * sy;
+            const float a = __expf(-0.5f * distance) * p.z;
+            const float4 col = s_col[jj];
+            C0 += col.x * a * T;
+            C1 += col.y * a * T;
+            C2 += col.z * a * T;
+            T *= (1.0f - a);
+            if (PER_ELEM) {
+                if (T <= tmin) { done = true; break; }
+            } else if (pos < preend) {
+                if (((pos + 1 - start) & 63u) == 0u && T <= tmin) {
+                    if (preend < end) {
+                        skip_until = preend;  // comp:104: the tail loop still runs once
+                    } else {
+                        done = true;
+                        break;
+                    }
+                }
+            } else if (T <= tmin) {
+                done = true;
+                break;
+            }
+        }
+    }
+
+    if (inside) {
+        uchar4* pix = &img[(uint64_t)py * gp.width + px];
+        const uchar4 in = *pix;
+        const float w = 1.0f - T;
+        float o0 = (float)in.x / 255.0f + C0 * w;
+        float o1 = (float)in.y / 255.0f + C1 * w;
+        float o2 = (float)in.z / 255.0f + C2 * w;
+        float o3 = (float)in.w / 255.0f + 1.0f * w;
+        o0 = fminf(fmaxf(o0, 0.0f), 1.0f);
+        o1 = fminf(fmaxf(o1, 0.0f), 1.0f);
+        o2 = fminf(fmaxf(o2, 0.0f), 1.0f);
+        o3 = fminf(fmaxf(o3, 0.0f), 1.0f);
+        *pix = make_uchar4((unsigned char)__float2uint_rn(o0 * 255.0f),
+                           (unsigned char)__float2uint_rn(o1 * 255.0f),
+                           (unsigned char)__float2uint_rn(o2 * 255.0f),
+                           (unsigned char)__float2uint_rn(o3 * 255.0f));
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_rasterize(const float4* rec, const SortIO& io, const uint2* ranges,
+                             const FrameCtl* ctl, const GridParams& gp, uchar4* img,
+                             bool per_element_exit, cudaStream_t stream) {
+    const uint32_t y0 = gp.row_begin * gp.bin_h;
+    uint32_t y1 = gp.row_end * gp.bin_h;
+    if (y1 > gp.height) y1 = gp.height;
+    if (y1 <= y0) return cudaSuccess;
+    const dim3 grid((gp.width + 15) / 16, (y1 - y0 + 15) / 16);
+    if (per_element_exit)
+        k_rasterize<true><<<grid, kRasterThreads, 0, stream>>>(rec, io, ranges, ctl, gp, img, y0);
+    else
+        k_rasterize<false><<<grid, kRasterThreads, 0, stream>>>(rec, io, ranges, ctl, gp, img, y0);
+    return cudaGetLastError();
+}
+
+}  // namespace kt

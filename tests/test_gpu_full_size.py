@@ -1,0 +1,105 @@
+"""Full-size workloads: exact integer-stage parity with the oracle on the 1M-Gaussian SH3
+1080p frame, the oracle's image on a band of bin rows, and size-independent properties
+(sortedness, range coverage, count conservation, replay) on the larger scenes."""
+
+import numpy as np
+import pytest
+
+import oracle
+from klartraum_b200 import Renderer, make_scene, native as N, workload_camera
+from klartraum_b200.scenes import WORKLOADS
+
+from helpers import background, compare_projected, psnr
+
+pytestmark = [pytest.mark.gpu, pytest.mark.slow]
+
+torch = pytest.importorskip("torch")
+
+
+def check_properties(r: Renderer, n: int):
+    st = r.stats()
+    K = st["num_keys"]
+    counts = r.dump(N.STAGE_TILE_COUNTS)
+    offsets = r.dump(N.STAGE_OFFSETS)
+    keys = r.dump(N.STAGE_KEYS_SORTED)
+    vals = r.dump(N.STAGE_VALUES_SORTED)
+    ranges = r.dump(N.STAGE_TILE_RANGES)
+    assert len(counts) == n and int(counts.sum(dtype=np.uint64)) == K == len(keys)
+    assert offsets[0] == 0 and np.array_equal(offsets[1:], np.cumsum(counts[:-1], dtype=np.uint64))
+    assert np.all(keys[1:] >= keys[:-1])                                  # sorted
+    ties = keys[1:] == keys[:-1]
+    assert np.all(vals[1:][ties] > vals[:-1][ties])                       # stable: index order
+    assert np.array_equal(np.bincount(vals, minlength=n), counts)         # every pair once
+    bins = (keys >> np.uint64(32)).astype(np.int64)
+    nt = st["tiles_x"] * st["tiles_y"]
+    per_bin = np.bincount(bins, minlength=nt)
+    nz = per_bin > 0
+    assert np.array_equal((ranges[:, 1] - ranges[:, 0])[nz], per_bin[nz])  # ranges cover the runs
+    assert np.all(ranges[~nz] == 0)
+    return st
+
+
+def test_single_1m_exact_stages_and_band_image():
+    w = WORKLOADS["single_1m"]
+    g3d = make_scene(w)
+    cam = workload_camera(w)
+    bg = background(w.height, w.width)
+    r = Renderer(w.width, w.height, bin_size=16, sh_degree=3)
+    r.set_gaussians(g3d)
+    img = torch.from_numpy(bg.copy()).cuda()
+    r.render(cam, img)
+    st = check_properties(r, w.n)
+
+    cfg = oracle.config(w.width, w.height, bin_size=16, sh_degree=3)
+    g2d = oracle.project(cfg, cam, g3d)
+    compare_projected(r.dump(N.STAGE_PROJECTED), g2d)
+    counts = oracle.tile_counts(cfg, g2d)
+    assert np.array_equal(r.dump(N.STAGE_TILE_COUNTS), counts)
+    off, total = oracle.exclusive_scan(counts)
+    assert st["num_keys"] == total
+    ku, vu = oracle.emit_keys(cfg, g2d, off, total)
+    tx, ty = oracle.tiles(cfg)
+    ks, vs = oracle.sort_pairs(ku, vu, 32 + int(tx * ty - 1).bit_length())
+    assert np.array_equal(r.dump(N.STAGE_KEYS_SORTED), ks)
+    assert np.array_equal(r.dump(N.STAGE_VALUES_SORTED), vs)
+    ranges = oracle.tile_ranges(ks, tx * ty)
+    assert np.array_equal(r.dump(N.STAGE_TILE_RANGES), ranges)
+    # image on a band of 6 bin rows through the middle of the screen
+    rows = (31, 37)
+    band = oracle.config(w.width, w.height, bin_size=16, sh_degree=3, tile_rows=rows)
+    ref = oracle.rasterize(band, g2d, vs, ranges, bg)
+    y0, y1 = rows[0] * 16, rows[1] * 16
+    out = img.cpu().numpy()
+    d = np.abs(out[y0:y1].astype(int) - ref[y0:y1].astype(int))
+    assert d.max() <= 1
+    assert psnr(out[y0:y1], ref[y0:y1]) >= 50.0
+
+
+@pytest.mark.parametrize("wname", ["large_6m", "stress_2m"])
+def test_large_scene_properties_and_replay(wname):
+    """6M SH3 4K (310M keys): every property on host dumps. 2M SH1 4K stress scene (3.1G keys,
+    ~95 GB of key buffers): counts exact vs the oracle, K, bin ranges covering K, replay."""
+    w = WORKLOADS[wname]
+    g3d = make_scene(w)
+    cam = workload_camera(w)
+    r = Renderer(w.width, w.height, bin_size=16, sh_degree=w.sh_degree)
+    r.set_gaussians(g3d)
+    img = torch.from_numpy(background(w.height, w.width)).cuda()
+    r.render(cam, img)
+    st = r.stats()
+    assert st["error_flags"] == 0
+    counts = r.dump(N.STAGE_TILE_COUNTS)
+    cfg = oracle.config(w.width, w.height, bin_size=16, sh_degree=w.sh_degree)
+    assert np.array_equal(counts, oracle.tile_counts(cfg, oracle.project(cfg, cam, g3d)))
+    assert int(counts.sum(dtype=np.uint64)) == st["num_keys"]
+    if st["num_keys"] < 1_000_000_000:
+        check_properties(r, w.n)
+    else:
+        ranges = r.dump(N.STAGE_TILE_RANGES).astype(np.int64)
+        assert int((ranges[:, 1] - ranges[:, 0]).sum()) == st["num_keys"]
+        nz = ranges[ranges[:, 1] > ranges[:, 0]]
+        order = np.argsort(nz[:, 0])
+        assert np.array_equal(nz[order][1:, 0], nz[order][:-1, 1])  # runs tile [0, K)
+    img2 = torch.from_numpy(background(w.height, w.width)).cuda()
+    r.render(cam, img2)
+    assert torch.equal(img, img2)
