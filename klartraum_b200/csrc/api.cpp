@@ -408,6 +408,10 @@ kt_status render_impl(kt_gs_ctx* c, uint32_t path, Source src, const kt_camera_m
         if ((s = enqueue_frame(c, w, src, cam ? &cp : nullptr, img, stream)) != KT_OK) return s;
         if (async) return KT_OK;
         s = check_frame(c, w);
+        if (s != KT_OK) {
+            // this frame's error is reported (or handled) here, not by a later kt_gs_sync
+            KT_TRY_CUDA(c, cudaMemsetAsync(&w.totals->sticky_errors, 0, sizeof(unsigned int), stream));
+        }
         if (s != KT_ERR_CAPACITY || (c->cfg.flags & KT_GS_FLAG_NO_AUTOGROW)) return s;
         const uint64_t need = w.host_ctl->num_keys;
         const uint64_t grow = need + need / 4 + kSortTile;
@@ -634,8 +638,10 @@ kt_status kt_gs_sync(kt_gs_ctx* c, uint32_t path) {
     if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
     KT_TRY_CUDA(c, cudaSetDevice(c->device));
     PathWs& w = c->paths[path];
-    kt_status s = check_frame(c, w);
-    if (s != KT_OK || !w.totals) return s;
+    if (!w.have_frame || !w.totals) return KT_OK;
+    KT_TRY_CUDA(c, cudaEventSynchronize(w.done_ev));
+    // every frame folds its error bits into the sticky word; checked frames clear what they
+    // already reported, so each error is reported once
     unsigned int sticky = 0;
     KT_TRY_CUDA(c, cudaMemcpy(&sticky, &w.totals->sticky_errors, sizeof(sticky), cudaMemcpyDeviceToHost));
     KT_TRY_CUDA(c, cudaMemset(&w.totals->sticky_errors, 0, sizeof(sticky)));

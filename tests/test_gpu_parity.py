@@ -266,3 +266,52 @@ def test_sh_degree_detection():
     r0 = Renderer(320, 240, bin_size=16, sh_degree=-1)
     r0.set_gaussians(g0)
     assert r0.sh_degree == 0
+
+
+def test_async_frames_report_overflow_at_sync_only_once():
+    w = WORKLOADS["single_1m"]
+    g3d = make_scene(w, n=50000)
+    cam = workload_camera(w)
+    bg = background(w.height, w.width)
+    # a checked frame that had to grow its buffers leaves nothing for a later sync
+    r = Renderer(w.width, w.height, bin_size=16, key_capacity=4096)
+    r.set_gaussians(g3d)
+    img = device_image(bg)
+    r.render(cam, img)
+    r.sync()
+    # an async frame that overflows draws nothing and is reported by the next sync, once
+    r2 = Renderer(w.width, w.height, bin_size=16, key_capacity=4096, flags=N.FLAG_ASYNC | N.FLAG_NO_AUTOGROW)
+    r2.set_gaussians(g3d)
+    img2 = device_image(bg)
+    r2.render(cam, img2)
+    r2.render(cam, img2)
+    with pytest.raises(N.KtError) as e:
+        r2.sync()
+    assert e.value.status == N.KT_ERR_CAPACITY
+    assert np.array_equal(img2.cpu().numpy(), bg)
+    r2.set_flags(N.FLAG_NO_AUTOGROW)
+    with pytest.raises(N.KtError):
+        r2.render(cam, img2)
+    r2.sync()  # the failed checked frame was reported by render() itself
+
+
+def test_counters_accumulate_frames_and_keys():
+    g3d = make_scene("plumbing", n=8000)
+    cam = workload_camera("plumbing")
+    r = Renderer(256, 256, bin_size=16, sh_degree=0, flags=N.FLAG_TIMING)
+    r.set_gaussians(g3d)
+    img = device_image(background(256, 256))
+    r.render(cam, img)
+    r.counters()
+    r.stage_times_total()
+    r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC)
+    for _ in range(20):
+        r.render(cam, img)
+    r.sync()
+    c = r.counters()
+    st = r.stats()
+    assert c["frames"] == 20 and c["keys"] == 20 * st["num_keys"]
+    assert c["key_passes"] == 20 * st["num_keys"] * st["sort_passes"]
+    ms, frames = r.stage_times_total()
+    assert frames == 20 and ms["frame"] > 0 and ms["sort"] > 0
+    assert r.counters()["frames"] == 0
