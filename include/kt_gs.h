@@ -275,6 +275,26 @@ kt_status kt_gs_radix_sort_pairs(const uint64_t* d_keys_in, const uint32_t* d_va
                                  uint32_t key_bits, void* d_temp, size_t* temp_bytes,
                                  void* stream);
 
+/*
+ * The same stable pair sort as kt_gs_radix_sort_pairs, for callers that cannot allocate device
+ * memory: a render loop with a fixed frame budget (cudaMalloc/cudaFree may synchronise the
+ * device), a plugin inside a host engine whose allocator owns all device memory, a process whose
+ * memory pool already holds the device's free memory. No counterpart in the reference.
+ *
+ * The caller passes inputs and outputs only; the scratch is one fixed array of
+ * KT_GS_STATIC_SORT_SCRATCH_BYTES in the library, kept on every device that loads it until the
+ * process exits. n above KT_GS_STATIC_SORT_MAX_PAIRS returns KT_ERR_CAPACITY without doing
+ * anything. The first call on a device looks up the array's device address (set-up done once
+ * per device, with that device current); make that first call before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race and must be ordered by the
+ * caller (e.g. issued on one stream). Asynchronous on `stream`; no allocation of any kind.
+ */
+#define KT_GS_STATIC_SORT_MAX_PAIRS 1048576u
+#define KT_GS_STATIC_SORT_SCRATCH_BYTES 13123840u
+kt_status kt_gs_radix_sort_pairs_static(const uint64_t* d_keys_in, const uint32_t* d_vals_in,
+                                        uint64_t* d_keys_out, uint32_t* d_vals_out, uint64_t n,
+                                        uint32_t key_bits, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -33,6 +33,7 @@ SOURCES = {
     "binning.cu": [],
     "sort.cu": [],
     "raster.cu": [],
+    "sort_static.cu": [],
     "api.cpp": [],
 }
 

@@ -1,0 +1,92 @@
+// kt_gs_radix_sort_pairs_static: the pair sort of kt_gs_radix_sort_pairs for callers that
+// cannot allocate device memory, with its scratch in a fixed array of this module.
+//
+// Some callers cannot call cudaMalloc: a render loop with a fixed frame budget (an allocation
+// or free may synchronise the whole device), a plugin inside a host engine whose own allocator
+// owns all device memory, or a process whose memory pool already holds the device's free
+// memory. They pass their inputs and outputs; the scratch (control block, the second key and
+// value buffers, look-back status words) lives in g_sort_scratch below.
+//
+// The array is KT_GS_STATIC_SORT_SCRATCH_BYTES (about 12.6 MB) and every device that loads this
+// module keeps it until the process exits. In host code the name g_sort_scratch is only a
+// host-side stand-in for the symbol, not a device address; the device address is looked up
+// with cudaGetSymbolAddress on the first call on each device (with that device current) and
+// cached. That first call on a device should therefore come before any stream capture.
+// All calls share the one array: calls whose work overlaps on the GPU race on it and must be
+// ordered by the caller (e.g. one stream). Each call clears what must start at zero (the
+// control block and the status words it uses); the rest keeps the previous call's contents
+// and is overwritten before it is read.
+#include "kt_common.cuh"
+#include "kt_gs.h"
+#include "kt_kernels.h"
+
+namespace kt {
+namespace {
+
+constexpr uint64_t kStaticMaxPairs = KT_GS_STATIC_SORT_MAX_PAIRS;
+constexpr size_t kCtlBytes = (sizeof(FrameCtl) + 255) & ~size_t(255);
+constexpr size_t kKeyBytes = kStaticMaxPairs * 8;
+constexpr size_t kValBytes = kStaticMaxPairs * 4;
+constexpr size_t kStatusBytes = (kStaticMaxPairs / kSortTile) * 256 * 8;
+constexpr size_t kScratchBytes = kCtlBytes + kKeyBytes + kValBytes + kStatusBytes;
+static_assert(kScratchBytes == KT_GS_STATIC_SORT_SCRATCH_BYTES, "scratch size in kt_gs.h is stale");
+static_assert(kStaticMaxPairs % kSortTile == 0, "maximum must be a whole number of sort tiles");
+
+static __device__ __align__(256) unsigned char g_sort_scratch[kScratchBytes];
+
+constexpr int kMaxDevices = 128;
+void* g_scratch_addr[kMaxDevices] = {};  // device address of g_sort_scratch per device
+
+// Device address of the scratch on the current device, looked up once per device.
+cudaError_t scratch_address(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (!g_scratch_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_sort_scratch);
+        if (e != cudaSuccess) return e;
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace kt
+
+using namespace kt;
+
+extern "C" kt_status kt_gs_radix_sort_pairs_static(const uint64_t* keys_in, const uint32_t* vals_in,
+                                                   uint64_t* keys_out, uint32_t* vals_out, uint64_t n,
+                                                   uint32_t key_bits, void* stream) {
+    if (key_bits > 64) return KT_ERR_ARG;
+    if (n > kStaticMaxPairs) return KT_ERR_CAPACITY;  // more pairs than the fixed scratch holds
+    if (n == 0) return KT_OK;
+    if (!keys_in || !vals_in || !keys_out || !vals_out) return KT_ERR_ARG;
+    void* base = nullptr;
+    if (scratch_address(&base) != cudaSuccess) return KT_ERR_CUDA;
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned char* t = (unsigned char*)base;
+    FrameCtl* ctl = (FrameCtl*)t;
+    unsigned long long* alt_k = (unsigned long long*)(t + kCtlBytes);
+    uint32_t* alt_v = (uint32_t*)(t + kCtlBytes + kKeyBytes);
+    unsigned long long* status = (unsigned long long*)(t + kCtlBytes + kKeyBytes + kValBytes);
+    const uint32_t max_passes = key_bits == 0 ? 1u : (key_bits + 7) / 8;
+    if (cudaMemsetAsync(ctl, 0, sizeof(FrameCtl), s) != cudaSuccess) return KT_ERR_CUDA;
+    if (cudaMemsetAsync(status, 0, sort_status_words(n) * 8, s) != cudaSuccess) return KT_ERR_CUDA;
+    if (launch_key_histogram((const unsigned long long*)keys_in, n, key_bits, ctl, s) != cudaSuccess)
+        return KT_ERR_CUDA;
+    if (launch_plan(ctl, n, max_passes, 1, s) != cudaSuccess) return KT_ERR_CUDA;
+    SortIO io{};
+    io.keys[0] = (unsigned long long*)keys_in;
+    io.keys[1] = alt_k;
+    io.keys[2] = (unsigned long long*)keys_out;
+    io.vals[0] = (uint32_t*)vals_in;
+    io.vals[1] = alt_v;
+    io.vals[2] = vals_out;
+    for (uint32_t p = 0; p < max_passes; ++p)
+        if (launch_sort_pass(io, ctl, status, p, p + 1, n, s) != cudaSuccess) return KT_ERR_CUDA;
+    return KT_OK;
+}
