@@ -10,7 +10,8 @@
 // KT_GS_FLAG_EXIT_PER_ELEMENT the test runs after every Gaussian.
 //
 // The CTA stages 256 sorted Gaussians at a time in shared memory (each thread gathers one
-// 48-B record by index) and leaves the list as soon as every pixel of the block is done.
+// 48-B record by index) and leaves the list as soon as every pixel of the block is done or
+// only owes the reference's one tail element, which it then blends from global memory.
 #include "kt_common.cuh"
 #include "kt_kernels.h"
 
@@ -20,13 +21,27 @@ namespace {
 constexpr int kRasterThreads = 256;
 constexpr int kBatch = 256;
 
+// One blend step: a = exp(-0.5 * dot(d, covInv d)) * alpha; C += color * a * T; T *= 1 - a.
+// `cq` is covInv pre-multiplied by -0.5 * log2(e) so that the exponential is one exp2.
+__device__ __forceinline__ void blend(float fx, float fy, const float4& p, const float4& cq, const float4& col,
+                                      float& C0, float& C1, float& C2, float& T) {
+    const float dx = fx - p.x, dy = fy - p.y;
+    const float sx = cq.x * dx + cq.z * dy;
+    const float sy = cq.y * dx + cq.w * dy;
+    const float a = exp2f(dx * sx + dy * sy) * p.z;
+    C0 += col.x * a * T;
+    C1 += col.y * a * T;
+    C2 += col.z * a * T;
+    T *= (1.0f - a);
+}
+
 template <bool PER_ELEM>
 __global__ void __launch_bounds__(kRasterThreads)
 k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__ ranges,
             const FrameCtl* __restrict__ ctl, GridParams gp, uchar4* __restrict__ img,
             uint32_t ypix0) {
     __shared__ float4 s_pos[kBatch];  // px, py, alpha, z
-    __shared__ float4 s_cov[kBatch];  // covInv 00, 01, 10, 11
+    __shared__ float4 s_cov[kBatch];  // covInv * (-0.5 log2 e)
     __shared__ float4 s_col[kBatch];  // r, g, b
     if (!ctl->plan_ok) return;
 
@@ -40,53 +55,53 @@ k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__
     const uint32_t preend = start + ((end - start) / 64) * 64;
     const uint32_t* __restrict__ vals = io_vals(io, ctl->final_buf);
     const float tmin = (float)(1.0 - 0.9999);
+    const float kq = -0.5f * 1.44269504088896340736f;  // -0.5 * log2(e)
     const float fx = (float)px, fy = (float)py;
 
     float C0 = 0.0f, C1 = 0.0f, C2 = 0.0f, T = 1.0f;
     bool done = !inside;
-    uint32_t skip_until = start;
+    // Reference exit rule: a pixel whose T <= 1-0.9999 at the end of a 64-batch leaves the batch
+    // loop, but the tail loop (comp:104-117) still blends the element at `preend` before it
+    // stops. Such a pixel waits here and takes that one element after the staged loop.
+    bool wait_tail = false;
 
     for (uint32_t b = start; b < end; b += kBatch) {
-        if (__syncthreads_and(done)) break;
+        if (__syncthreads_and(done || wait_tail)) break;
         const uint32_t nb = min((uint32_t)kBatch, end - b);
         if ((uint32_t)tid < nb) {
             const uint32_t idx = vals[b + tid];
+            const float4 c = rec[3 * (uint64_t)idx + 1];
             s_pos[tid] = rec[3 * (uint64_t)idx + 0];
-            s_cov[tid] = rec[3 * (uint64_t)idx + 1];
+            s_cov[tid] = make_float4(c.x * kq, c.y * kq, c.z * kq, c.w * kq);
             s_col[tid] = rec[3 * (uint64_t)idx + 2];
         }
         __syncthreads();
-        if (done) continue;
+        if (done || wait_tail) continue;
         for (uint32_t jj = 0; jj < nb; ++jj) {
             const uint32_t pos = b + jj;
-            if (pos < skip_until) continue;
-            const float4 p = s_pos[jj];
-            const float4 c = s_cov[jj];
-            const float dx = fx - p.x, dy = fy - p.y;
-            const float sx = c.x * dx + c.z * dy;
-            const float sy = c.y * dx + c.w * dy;
-            const float distance = dx * sx + dy * sy;
-            const float a = __expf(-0.5f * distance) * p.z;
-            const float4 col = s_col[jj];
-            C0 += col.x * a * T;
-            C1 += col.y * a * T;
-            C2 += col.z * a * T;
-            T *= (1.0f - a);
+            blend(fx, fy, s_pos[jj], s_cov[jj], s_col[jj], C0, C1, C2, T);
             if (PER_ELEM) {
                 if (T <= tmin) { done = true; break; }
             } else if (pos < preend) {
                 if (((pos + 1 - start) & 63u) == 0u && T <= tmin) {
-                    if (preend < end) {
-                        skip_until = preend;  // comp:104: the tail loop still runs once
-                    } else {
-                        done = true;
-                        break;
-                    }
+                    wait_tail = preend < end;
+                    done = !wait_tail;
+                    break;
                 }
             } else if (T <= tmin) {
                 done = true;
                 break;
             }
+        }
+    }
+    if (wait_tail) {
+        // the tail loop from `preend`: one element unless that element raised T again
+        for (uint32_t i = preend; i < end; ++i) {
+            const uint32_t idx = vals[i];
+            const float4 c = rec[3 * (uint64_t)idx + 1];
+            blend(fx, fy, rec[3 * (uint64_t)idx + 0], make_float4(c.x * kq, c.y * kq, c.z * kq, c.w * kq),
+                  rec[3 * (uint64_t)idx + 2], C0, C1, C2, T);
+            if (T <= tmin) break;
         }
     }
 
