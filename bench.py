@@ -163,20 +163,6 @@ def run_reference(args, w, cfg_block):
 
 # ------------------------------------------------------------------- our arm
 
-def algorithmic_bytes(st: dict, n: int, nplanes: int, width: int, height: int) -> dict:
-    K = st["num_keys"]
-    tiles = st["tiles_x"] * st["tiles_y"]
-    return {
-        # scene planes (pos, rot, scale + SH planes) read; record 48 + count 4 + rect 8 + depth 4 written
-        "project_count": n * (16 * (3 + nplanes) + 64),
-        # counts, rects, depths read; offsets written; K keys (8 B) + values (4 B) written
-        "scan_emit": n * (4 + 8 + 4 + 8) + K * 12,
-        # per executed pass: read + write of 8 B key and 4 B value
-        "sort": K * 24 * st["sort_passes"],
-        "ranges": K * 8 + tiles * 8,
-    }
-
-
 def load_peaks() -> tuple[float, str]:
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -260,14 +246,21 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     frames = max(timed_frames, 1)
     K_avg = cnt["keys"] / max(cnt["frames"], 1)
     passes_avg = cnt["key_passes"] / max(cnt["keys"], 1)
+    nf = max(cnt["frames"], 1)
     per_frame_bytes = {
+        # scene planes read; record 48 + count 4 + rect 8 + depth 4 written
         "project_count": w.n * (16 * (3 + nplanes) + 64),
-        "scan_emit": w.n * (4 + 8 + 4 + 8) + K_avg * 12,
-        "sort": cnt["key_passes"] / max(cnt["frames"], 1) * 24,
+        # depth keys (counts + depths read, 8-B keys written) and the depth sort passes (16 B per
+        # Gaussian per pass)
+        "depth_sort": w.n * (4 + 4 + 8) + cnt["depth_sort_bytes"] / nf,
+        # scan/emit: order, counts and rects gathered per Gaussian; 8 B written per pair
+        "emit": w.n * (8 + 4 + 8) + K_avg * 8,
+        # per executed pass of the pair sort: 8-B element read and written
+        "bin_sort": cnt["sort_bytes"] / nf,
         "ranges": K_avg * 8 + st["tiles_x"] * st["tiles_y"] * 8,
     }
     stages = {}
-    for name in N.STAGE_NAMES[:5]:
+    for name in N.STAGE_NAMES[:-1]:
         avg = stage_ms[name] / frames
         d = {"ms": avg, "share": stage_ms[name] / max(stage_ms["frame"], 1e-12)}
         if name in per_frame_bytes:
@@ -316,6 +309,7 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg_block,
         "gaussians_per_s": fps * w.n, "keys_per_frame": K_avg, "sort_passes_per_frame": passes_avg,
+        "sort_layout": "Gaussians by depth, then (bin | index) pairs by bin; packed u64 elements",
         "stages": stages, "roofline": roofline,
         "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": img_bytes + 192,
                 "d2h_bytes_per_step": img_bytes + st["status_bytes"], "steps": e2e_steps,

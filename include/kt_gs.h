@@ -93,7 +93,8 @@ typedef struct kt_gaussian2d {
                                             growing the key buffers and rendering again */
 #define KT_GS_FLAG_ASYNC 0x4u            /* do not wait for the frame status after a render;
                                             kt_gs_sync() reports overflow/timeouts later */
-#define KT_GS_FLAG_KEEP_UNSORTED 0x8u    /* keep a copy of the unsorted keys/values for dumps */
+#define KT_GS_FLAG_KEEP_UNSORTED 0x8u    /* accepted for compatibility; the unsorted dumps are always
+                                            available (rebuilt from the device's bin rectangles) */
 #define KT_GS_FLAG_TIMING 0x10u          /* record CUDA events around every stage */
 
 typedef struct kt_gs_config {
@@ -129,6 +130,8 @@ typedef struct kt_gs_stats {
     uint32_t depth_max_bits;
     uint32_t status_bytes;   /* bytes of frame status copied device->host after every frame */
     uint32_t launches;       /* kernels launched per frame */
+    uint32_t packed;         /* 1: the sort moved (key << idx_bits | index) words, 0: keys + values */
+    uint32_t idx_bits;       /* index bits of a packed element */
 } kt_gs_stats;
 
 /* Totals accumulated on the device over every frame rendered on a path since the last
@@ -138,6 +141,8 @@ typedef struct kt_gs_counters {
     uint64_t keys;        /* sum of K */
     uint64_t key_passes;  /* sum of K * (executed sort passes) */
     uint64_t visible;     /* sum of Gaussians with a non-zero tile count */
+    uint64_t sort_bytes;  /* sum of bytes the executed passes of the pair sort read and wrote */
+    uint64_t depth_sort_bytes; /* same for the depth sort of the Gaussians */
 } kt_gs_counters;
 
 /* Buffers that kt_gs_debug_dump() can copy out after a render. */
@@ -145,10 +150,12 @@ typedef enum kt_gs_stage {
     KT_GS_STAGE_PROJECTED = 0,       /* kt_gaussian2d[N], binMask = 0xFFFFFFFF as projected
                                         (gsplat_projection.comp:228) */
     KT_GS_STAGE_TILE_COUNTS = 1,     /* uint32[N] bins overlapped by each Gaussian (0 if culled) */
-    KT_GS_STAGE_OFFSETS = 2,         /* uint64[N] exclusive scan of the tile counts */
-    KT_GS_STAGE_KEYS_UNSORTED = 3,   /* uint64[K] bin<<32 | (floatBitsToUint(z) ^ 0x80000000);
-                                        needs KT_GS_FLAG_KEEP_UNSORTED */
-    KT_GS_STAGE_VALUES_UNSORTED = 4, /* uint32[K] Gaussian index; needs KT_GS_FLAG_KEEP_UNSORTED */
+    KT_GS_STAGE_OFFSETS = 2,         /* uint64[N] exclusive scan of the tile counts in Gaussian index
+                                        order (derived from the counts; the device scans in depth order) */
+    KT_GS_STAGE_KEYS_UNSORTED = 3,   /* uint64[K] bin<<32 | (floatBitsToUint(z) ^ 0x80000000), Gaussians
+                                        in index order, bins ascending (rebuilt from the device's
+                                        per-Gaussian bin rectangles and depths) */
+    KT_GS_STAGE_VALUES_UNSORTED = 4, /* uint32[K] Gaussian index, same order */
     KT_GS_STAGE_KEYS_SORTED = 5,     /* uint64[K], same key layout, stably sorted */
     KT_GS_STAGE_VALUES_SORTED = 6,   /* uint32[K] */
     KT_GS_STAGE_TILE_RANGES = 7,     /* uint32[2 * tiles] {start, end} per bin (StartAndEnd,
@@ -157,8 +164,9 @@ typedef enum kt_gs_stage {
 } kt_gs_stage;
 
 /* Stage timers (KT_GS_FLAG_TIMING), in the order the stages run. */
-#define KT_GS_NSTAGES 6
-/* 0 projection+count, 1 scan+emit, 2 sort, 3 bin ranges, 4 rasterise, 5 whole frame */
+#define KT_GS_NSTAGES 7
+/* 0 projection+count, 1 depth keys + depth sort of the Gaussians, 2 scan/emit of the (bin,
+ * Gaussian) pairs, 3 sort of the pairs by bin, 4 bin ranges, 5 rasterise, 6 whole frame */
 
 typedef struct kt_gs_ctx kt_gs_ctx;
 

@@ -35,8 +35,8 @@ STAGE_VALUES_UNSORTED = 4
 STAGE_KEYS_SORTED = 5
 STAGE_VALUES_SORTED = 6
 STAGE_TILE_RANGES = 7
-NSTAGES = 6
-STAGE_NAMES = ["project_count", "scan_emit", "sort", "ranges", "rasterize", "frame"]
+NSTAGES = 7
+STAGE_NAMES = ["project_count", "depth_sort", "emit", "bin_sort", "ranges", "rasterize", "frame"]
 
 # every entry point include/kt_gs.h declares
 EXPORTED_SYMBOLS = [
@@ -77,6 +77,7 @@ class Stats(C.Structure):
         ("sort_passes", C.c_uint32), ("error_flags", C.c_uint32),
         ("depth_min_bits", C.c_uint32), ("depth_max_bits", C.c_uint32),
         ("status_bytes", C.c_uint32), ("launches", C.c_uint32),
+        ("packed", C.c_uint32), ("idx_bits", C.c_uint32),
     ]
 
     def as_dict(self) -> dict:
@@ -85,15 +86,15 @@ class Stats(C.Structure):
 
 class Counters(C.Structure):
     _fields_ = [("frames", C.c_uint64), ("keys", C.c_uint64), ("key_passes", C.c_uint64),
-                ("visible", C.c_uint64)]
+                ("visible", C.c_uint64), ("sort_bytes", C.c_uint64), ("depth_sort_bytes", C.c_uint64)]
 
     def as_dict(self) -> dict:
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
 assert C.sizeof(Config) == 48
-assert C.sizeof(Stats) == 72
-assert C.sizeof(Counters) == 32
+assert C.sizeof(Stats) == 80
+assert C.sizeof(Counters) == 48
 
 _lib = None
 

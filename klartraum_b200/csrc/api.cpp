@@ -4,7 +4,9 @@
 // (src/vulkan_gaussian_splatting.cpp:13-316): where the node builds a five-element compute
 // sub-graph with Vulkan buffers, this context owns the device buffers of each path (frame in
 // flight) and enqueues the kernels of one frame on a CUDA stream:
-//   init -> K1 project+count -> K2/3 scan+emit -> plan -> K4 sort passes -> K5 ranges -> K6.
+//   init -> K1 project+count -> depth keys -> plan -> depth sort passes (Gaussians)
+//   -> K2/3 scan+emit in depth order -> plan -> bin sort passes (pairs) -> K6;
+//   bin ranges (K5) come from per-bin pair counts right after K1.
 // No host synchronisation happens inside a frame: the key count, the sort plan and the pass
 // skipping live in device memory. After the frame a 2.6 KB control block is copied back;
 // unless KT_GS_FLAG_ASYNC is set the call waits for it and, if the keys did not fit, grows
@@ -45,6 +47,7 @@ using namespace kt;
 namespace {
 
 constexpr uint64_t kMaxKeyCapacity = 0xFFFFF000ull;  // values and ranges are 32-bit
+constexpr uint32_t kDepthPasses = 4;                  // 8-bit passes over <= 31 depth bits
 
 struct PathWs {
     uint64_t n_alloc = 0;
@@ -53,13 +56,15 @@ struct PathWs {
     uint32_t* counts = nullptr;
     uint2* rect = nullptr;
     uint32_t* depth = nullptr;
-    unsigned long long* offsets = nullptr;
+    unsigned long long* gsort[2] = {nullptr, nullptr};  // Gaussians by depth
     unsigned long long* scan_status = nullptr;
-    unsigned long long* keys[2] = {nullptr, nullptr};
-    uint32_t* vals[2] = {nullptr, nullptr};
+    unsigned long long* keys[2] = {nullptr, nullptr};   // (bin, Gaussian) pairs
     unsigned long long* sort_status = nullptr;
+    uint64_t status_words = 0;
+    int* bin_diff = nullptr;  // (tiles_y + 1) x (tiles_x + 1) difference table, zero between frames
     uint2* ranges = nullptr;
     FrameCtl* ctl = nullptr;
+    FrameCtl* ctl_depth = nullptr;
     FrameCtl* host_ctl = nullptr;  // pinned copy of the last frame's control block
     uint32_t scan_epoch = 0;
     uint32_t sort_epoch = 0;
@@ -76,11 +81,6 @@ struct PathWs {
     bool timed = false;
     bool have_frame = false;
     uint64_t frame_n = 0;
-    // debug copies of the unsorted keys
-    unsigned long long* dbg_keys = nullptr;
-    uint32_t* dbg_vals = nullptr;
-    uint64_t dbg_count = 0;
-    uint64_t dbg_cap = 0;
     // device image for kt_gs_render_host
     uchar4* img = nullptr;
     // device copy of caller-supplied projected records
@@ -172,9 +172,9 @@ GridParams make_grid(const kt_gs_config& c) {
 uint32_t ntiles(const kt_gs_ctx* c) { return c->gp.tiles_x * c->gp.tiles_y; }
 
 void free_path(PathWs& w) {
-    dfree(w.rec); dfree(w.counts); dfree(w.rect); dfree(w.depth); dfree(w.offsets);
-    dfree(w.scan_status); dfree(w.keys[0]); dfree(w.keys[1]); dfree(w.vals[0]); dfree(w.vals[1]);
-    dfree(w.sort_status); dfree(w.ranges); dfree(w.ctl); dfree(w.dbg_keys); dfree(w.dbg_vals);
+    dfree(w.rec); dfree(w.counts); dfree(w.rect); dfree(w.depth); dfree(w.gsort[0]); dfree(w.gsort[1]);
+    dfree(w.scan_status); dfree(w.keys[0]); dfree(w.keys[1]);
+    dfree(w.sort_status); dfree(w.ranges); dfree(w.ctl); dfree(w.ctl_depth); dfree(w.bin_diff);
     dfree(w.img); dfree(w.g2d);
     if (w.host_ctl) cudaFreeHost(w.host_ctl);
     w.host_ctl = nullptr;
@@ -193,9 +193,14 @@ kt_status ensure_path_base(kt_gs_ctx* c, PathWs& w) {
     if (!w.ctl) {
         KT_TRY_CUDA(c, cudaMalloc(&w.ctl, sizeof(FrameCtl)));
         KT_TRY_CUDA(c, cudaMemset(w.ctl, 0, sizeof(FrameCtl)));
+        KT_TRY_CUDA(c, cudaMalloc(&w.ctl_depth, sizeof(FrameCtl)));
+        KT_TRY_CUDA(c, cudaMemset(w.ctl_depth, 0, sizeof(FrameCtl)));
         KT_TRY_CUDA(c, cudaMallocHost(&w.host_ctl, sizeof(FrameCtl)));
         std::memset(w.host_ctl, 0, sizeof(FrameCtl));
         KT_TRY_CUDA(c, cudaMalloc(&w.ranges, sizeof(uint2) * std::max(1u, ntiles(c))));
+        const size_t cells = (size_t)(c->gp.tiles_x + 1) * (c->gp.tiles_y + 1);
+        KT_TRY_CUDA(c, cudaMalloc(&w.bin_diff, sizeof(int) * cells));
+        KT_TRY_CUDA(c, cudaMemset(w.bin_diff, 0, sizeof(int) * cells));
         KT_TRY_CUDA(c, cudaEventCreateWithFlags(&w.done_ev, cudaEventDisableTiming));
         for (auto& set : w.ring)
             for (auto& e : set) KT_TRY_CUDA(c, cudaEventCreate(&e));
@@ -205,9 +210,22 @@ kt_status ensure_path_base(kt_gs_ctx* c, PathWs& w) {
     return KT_OK;
 }
 
+// Look-back status words shared by the depth sort (n elements) and the pair sort (cap).
+kt_status ensure_status(kt_gs_ctx* c, PathWs& w) {
+    const uint64_t need = sort_status_words(std::max<uint64_t>(w.cap, w.n_alloc));
+    if (need <= w.status_words) return KT_OK;
+    dfree(w.sort_status);
+    w.status_words = 0;
+    KT_TRY_CUDA(c, cudaMalloc(&w.sort_status, sizeof(unsigned long long) * need));
+    KT_TRY_CUDA(c, cudaMemset(w.sort_status, 0, sizeof(unsigned long long) * need));
+    w.sort_epoch = 0;
+    w.status_words = need;
+    return KT_OK;
+}
+
 kt_status ensure_n(kt_gs_ctx* c, PathWs& w, uint64_t n) {
     if (n <= w.n_alloc) return KT_OK;
-    dfree(w.rec); dfree(w.counts); dfree(w.rect); dfree(w.depth); dfree(w.offsets);
+    dfree(w.rec); dfree(w.counts); dfree(w.rect); dfree(w.depth); dfree(w.gsort[0]); dfree(w.gsort[1]);
     dfree(w.scan_status);
     w.n_alloc = 0;
     const uint64_t m = std::max<uint64_t>(n, 1);
@@ -215,13 +233,14 @@ kt_status ensure_n(kt_gs_ctx* c, PathWs& w, uint64_t n) {
     KT_TRY_CUDA(c, cudaMalloc(&w.counts, sizeof(uint32_t) * m));
     KT_TRY_CUDA(c, cudaMalloc(&w.rect, sizeof(uint2) * m));
     KT_TRY_CUDA(c, cudaMalloc(&w.depth, sizeof(uint32_t) * m));
-    KT_TRY_CUDA(c, cudaMalloc(&w.offsets, sizeof(unsigned long long) * m));
+    KT_TRY_CUDA(c, cudaMalloc(&w.gsort[0], sizeof(unsigned long long) * m));
+    KT_TRY_CUDA(c, cudaMalloc(&w.gsort[1], sizeof(unsigned long long) * m));
     const uint64_t chunks = (m + kScanChunk - 1) / kScanChunk;
     KT_TRY_CUDA(c, cudaMalloc(&w.scan_status, sizeof(unsigned long long) * chunks));
     KT_TRY_CUDA(c, cudaMemset(w.scan_status, 0, sizeof(unsigned long long) * chunks));
     w.scan_epoch = 0;
     w.n_alloc = m;
-    return KT_OK;
+    return ensure_status(c, w);
 }
 
 kt_status ensure_cap(kt_gs_ctx* c, PathWs& w, uint64_t cap) {
@@ -230,18 +249,11 @@ kt_status ensure_cap(kt_gs_ctx* c, PathWs& w, uint64_t cap) {
         return fail(c, KT_ERR_CAPACITY, "key count " + std::to_string(cap) +
                                             " exceeds the 32-bit index range of the key buffers");
     cap = std::min<uint64_t>(((cap + kSortTile - 1) / kSortTile) * kSortTile, kMaxKeyCapacity);
-    dfree(w.keys[0]); dfree(w.keys[1]); dfree(w.vals[0]); dfree(w.vals[1]); dfree(w.sort_status);
+    dfree(w.keys[0]); dfree(w.keys[1]);
     w.cap = 0;
-    for (int b = 0; b < 2; ++b) {
-        KT_TRY_CUDA(c, cudaMalloc(&w.keys[b], sizeof(unsigned long long) * cap));
-        KT_TRY_CUDA(c, cudaMalloc(&w.vals[b], sizeof(uint32_t) * cap));
-    }
-    const size_t words = sort_status_words(cap);
-    KT_TRY_CUDA(c, cudaMalloc(&w.sort_status, sizeof(unsigned long long) * words));
-    KT_TRY_CUDA(c, cudaMemset(w.sort_status, 0, sizeof(unsigned long long) * words));
-    w.sort_epoch = 0;
+    for (int b = 0; b < 2; ++b) KT_TRY_CUDA(c, cudaMalloc(&w.keys[b], sizeof(unsigned long long) * cap));
     w.cap = cap;
-    return KT_OK;
+    return ensure_status(c, w);
 }
 
 FrameBufs frame_bufs(const PathWs& w) {
@@ -250,15 +262,15 @@ FrameBufs frame_bufs(const PathWs& w) {
     fb.counts = w.counts;
     fb.rect = w.rect;
     fb.depth = w.depth;
-    fb.offsets = w.offsets;
+    fb.gsort[0] = w.gsort[0];
+    fb.gsort[1] = w.gsort[1];
     fb.keys[0] = w.keys[0];
     fb.keys[1] = w.keys[1];
-    fb.vals[0] = w.vals[0];
-    fb.vals[1] = w.vals[1];
     fb.ranges = w.ranges;
     fb.scan_status = w.scan_status;
     fb.sort_status = w.sort_status;
     fb.ctl = w.ctl;
+    fb.ctl_depth = w.ctl_depth;
     fb.key_capacity = w.cap;
     return fb;
 }
@@ -272,14 +284,15 @@ constexpr size_t kCtlHeaderBytes = offsetof(FrameCtl, hist);
 kt_status drain_slot(kt_gs_ctx* c, PathWs& w, int slot) {
     if (!w.ring_used[slot]) return KT_OK;
     cudaEvent_t* ev = w.ring[slot];
-    KT_TRY_CUDA(c, cudaEventSynchronize(ev[5]));
+    constexpr int L = KT_GS_NSTAGES - 1;  // events 0..L bracket the stages
+    KT_TRY_CUDA(c, cudaEventSynchronize(ev[L]));
     float ms = 0.0f;
-    for (int i = 0; i < 5; ++i) {
+    for (int i = 0; i < L; ++i) {
         KT_TRY_CUDA(c, cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
         w.stage_sum[i] += ms;
     }
-    KT_TRY_CUDA(c, cudaEventElapsedTime(&ms, ev[0], ev[5]));
-    w.stage_sum[5] += ms;
+    KT_TRY_CUDA(c, cudaEventElapsedTime(&ms, ev[0], ev[L]));
+    w.stage_sum[L] += ms;
     w.timed_frames += 1;
     w.ring_used[slot] = false;
     return KT_OK;
@@ -310,23 +323,24 @@ kt_status enqueue_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* ca
                                        stream));
         w.scan_epoch = 1;
     }
-    if (w.sort_epoch + c->max_passes + 1 > kEpochMax) {
-        KT_TRY_CUDA(c, cudaMemsetAsync(w.sort_status, 0,
-                                       sizeof(unsigned long long) * sort_status_words(w.cap), stream));
+    const uint32_t epochs = kDepthPasses + c->max_passes;
+    if (w.sort_epoch + epochs + 1 > kEpochMax) {
+        KT_TRY_CUDA(c, cudaMemsetAsync(w.sort_status, 0, sizeof(unsigned long long) * w.status_words, stream));
         w.sort_epoch = 0;
     }
     const uint32_t sort_epoch0 = w.sort_epoch + 1;
-    w.sort_epoch += c->max_passes;
+    w.sort_epoch += epochs;
 
     FrameBufs fb = frame_bufs(w);
-    SortIO io{};
+    SortIO io{};  // pairs by bin
     io.keys[0] = w.keys[0];
     io.keys[1] = w.keys[1];
-    io.vals[0] = w.vals[0];
-    io.vals[1] = w.vals[1];
+    SortIO io_depth{};  // Gaussians by depth
+    io_depth.keys[0] = w.gsort[0];
+    io_depth.keys[1] = w.gsort[1];
 
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[0], stream));
-    KT_TRY_CUDA(c, launch_frame_init(w.ctl, w.ranges, ntiles(c), stream));
+    KT_TRY_CUDA(c, launch_frame_init(w.ctl, w.ctl_depth, w.ranges, ntiles(c), stream));
     if (src == Source::Scene) {
         SceneDev sc{c->pos, c->rot, c->scale, c->sh, c->nplanes, c->deg, c->n};
         KT_TRY_CUDA(c, launch_project_count(sc, *cam, c->gp, fb, stream));
@@ -334,37 +348,27 @@ kt_status enqueue_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* ca
         KT_TRY_CUDA(c, launch_load_projected(w.g2d, n, c->gp, fb, stream));
     }
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[1], stream));
-    KT_TRY_CUDA(c, launch_scan_emit(fb, c->gp, n, w.scan_epoch, c->max_passes, stream));
+    // pairs per bin -> bin ranges and the bin sort's histograms (independent of depth order)
+    KT_TRY_CUDA(c, launch_bin_counts(fb, c->gp, n, w.bin_diff, c->max_passes, stream));
+    // Gaussians by depth (stable: ties keep index order), then the pairs emitted in that order
+    KT_TRY_CUDA(c, launch_depth_keys(fb, n, stream));
+    KT_TRY_CUDA(c, launch_plan(w.ctl_depth, n, kDepthPasses, 0, stream));
+    for (uint32_t p = 0; p < kDepthPasses; ++p)
+        KT_TRY_CUDA(c, launch_sort_pass(io_depth, w.ctl_depth, w.sort_status, p, sort_epoch0 + p, n, true, stream));
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[2], stream));
-    KT_TRY_CUDA(c, launch_plan(w.ctl, w.cap, c->max_passes, 0, stream));
-    if (c->cfg.flags & KT_GS_FLAG_KEEP_UNSORTED) {
-        // debug path: read K now and keep a copy of the emitted pairs
-        unsigned long long k = 0;
-        KT_TRY_CUDA(c, cudaMemcpyAsync(&k, &w.ctl->num_keys, sizeof(k), cudaMemcpyDeviceToHost, stream));
-        KT_TRY_CUDA(c, cudaStreamSynchronize(stream));
-        w.dbg_count = 0;
-        if (k <= w.cap) {
-            if (k > w.dbg_cap) {
-                dfree(w.dbg_keys);
-                dfree(w.dbg_vals);
-                w.dbg_cap = 0;
-                KT_TRY_CUDA(c, cudaMalloc(&w.dbg_keys, sizeof(unsigned long long) * std::max<uint64_t>(k, 1)));
-                KT_TRY_CUDA(c, cudaMalloc(&w.dbg_vals, sizeof(uint32_t) * std::max<uint64_t>(k, 1)));
-                w.dbg_cap = std::max<uint64_t>(k, 1);
-            }
-            KT_TRY_CUDA(c, cudaMemcpyAsync(w.dbg_keys, w.keys[0], k * 8, cudaMemcpyDeviceToDevice, stream));
-            KT_TRY_CUDA(c, cudaMemcpyAsync(w.dbg_vals, w.vals[0], k * 4, cudaMemcpyDeviceToDevice, stream));
-            w.dbg_count = k;
-        }
-    }
-    for (uint32_t p = 0; p < c->max_passes; ++p)
-        KT_TRY_CUDA(c, launch_sort_pass(io, w.ctl, w.sort_status, p, sort_epoch0 + p, w.cap, stream));
+    KT_TRY_CUDA(c, launch_scan_emit(fb, c->gp, n, w.scan_epoch, c->max_passes, stream));
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[3], stream));
-    KT_TRY_CUDA(c, launch_ranges(io, w.ctl, w.ranges, w.totals, stream));
+    // pairs by bin (stable: depth order within a bin survives)
+    KT_TRY_CUDA(c, launch_plan(w.ctl, w.cap, c->max_passes, 0, stream));
+    for (uint32_t p = 0; p < c->max_passes; ++p)
+        KT_TRY_CUDA(c, launch_sort_pass(io, w.ctl, w.sort_status, p, sort_epoch0 + kDepthPasses + p, w.cap,
+                                        true, stream));
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[4], stream));
+    KT_TRY_CUDA(c, launch_frame_totals(w.ctl, w.ctl_depth, w.totals, stream));
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[5], stream));
     KT_TRY_CUDA(c, launch_rasterize(w.rec, io, w.ranges, w.ctl, c->gp, img,
                                     (c->cfg.flags & KT_GS_FLAG_EXIT_PER_ELEMENT) != 0, stream));
-    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[5], stream));
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[6], stream));
     KT_TRY_CUDA(c, cudaMemcpyAsync(w.host_ctl, w.ctl, kCtlHeaderBytes, cudaMemcpyDeviceToHost, stream));
     KT_TRY_CUDA(c, cudaEventRecord(w.done_ev, stream));
     w.have_frame = true;
@@ -465,16 +469,6 @@ kt_status upload_scene(kt_gs_ctx* c, const kt_gaussian3d* src, bool src_on_devic
     return KT_OK;
 }
 
-// compact key (bin << dbits | depth - dmin) -> reference key (bin << 32 | depth)
-void expand_keys(unsigned long long* k, uint64_t count, uint32_t dbits, uint32_t dmin) {
-    const unsigned long long m = dbits >= 64 ? ~0ull : ((1ull << dbits) - 1ull);
-    for (uint64_t i = 0; i < count; ++i) {
-        const unsigned long long bin = dbits >= 64 ? 0ull : (k[i] >> dbits);
-        const uint32_t depth = (uint32_t)((k[i] & m) + dmin);
-        k[i] = (bin << 32) | depth;
-    }
-}
-
 }  // namespace
 
 // ======================================================================= C ABI
@@ -532,7 +526,7 @@ kt_status kt_gs_create(const kt_gs_config* cfg, int device, kt_gs_ctx** out) {
     c->cfg = *cfg;
     c->device = device;
     c->gp = make_grid(*cfg);
-    c->max_passes = (c->gp.tile_bits + 32 + 7) / 8;
+    c->max_passes = std::max<uint32_t>(1, (c->gp.tile_bits + 7) / 8);  // passes over the bin bits
     c->paths.resize(cfg->num_paths);
     *out = c;
     return KT_OK;
@@ -673,7 +667,9 @@ kt_status kt_gs_frame_stats(kt_gs_ctx* c, uint32_t path, kt_gs_stats* out) {
     out->depth_min_bits = h.depth_min;
     out->depth_max_bits = h.depth_max;
     out->status_bytes = (uint32_t)kCtlHeaderBytes;
-    out->launches = 6 + c->max_passes;
+    out->launches = 9 + kDepthPasses + c->max_passes;
+    out->packed = h.packed;
+    out->idx_bits = h.idx_bits;
     return KT_OK;
 }
 
@@ -691,6 +687,8 @@ kt_status kt_gs_counters_take(kt_gs_ctx* c, uint32_t path, kt_gs_counters* out) 
     out->keys = t.keys;
     out->key_passes = t.key_passes;
     out->visible = t.visible;
+    out->sort_bytes = t.sort_bytes;
+    out->depth_sort_bytes = t.depth_sort_bytes;
     // reset the counters; the sticky error bits stay until kt_gs_sync reports them
     KT_TRY_CUDA(c, cudaMemset(w.totals, 0, offsetof(FrameTotals, sticky_errors)));
     return KT_OK;
@@ -715,25 +713,25 @@ kt_status kt_gs_debug_dump(kt_gs_ctx* c, uint32_t path, kt_gs_stage stage, void*
     const uint64_t n = w.frame_n;
     const uint64_t K = h.num_keys;
     const bool sorted_ok = h.plan_ok != 0;
+    const uint32_t ibits = h.idx_bits;
+    const unsigned long long imask = (1ull << ibits) - 1ull;
+    const uint32_t tx = c->gp.tiles_x;
+    const bool is_keys = stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_KEYS_UNSORTED;
+    const bool is_vals = stage == KT_GS_STAGE_VALUES_SORTED || stage == KT_GS_STAGE_VALUES_UNSORTED;
     uint64_t need = 0;
-    const void* src = nullptr;
     switch (stage) {
         case KT_GS_STAGE_PROJECTED: need = n * sizeof(kt_gaussian2d); break;
-        case KT_GS_STAGE_TILE_COUNTS: need = n * 4; src = w.counts; break;
-        case KT_GS_STAGE_OFFSETS: need = n * 8; src = w.offsets; break;
+        case KT_GS_STAGE_TILE_COUNTS: need = n * 4; break;
+        case KT_GS_STAGE_OFFSETS: need = n * 8; break;
         case KT_GS_STAGE_KEYS_UNSORTED:
-            if (!w.dbg_keys && K) return fail(c, KT_ERR_STATE, "unsorted keys need KT_GS_FLAG_KEEP_UNSORTED");
-            need = w.dbg_count * 8; src = w.dbg_keys; break;
         case KT_GS_STAGE_VALUES_UNSORTED:
-            if (!w.dbg_vals && K) return fail(c, KT_ERR_STATE, "unsorted values need KT_GS_FLAG_KEEP_UNSORTED");
-            need = w.dbg_count * 4; src = w.dbg_vals; break;
         case KT_GS_STAGE_KEYS_SORTED:
-            if (!sorted_ok) return fail(c, KT_ERR_STATE, "the last frame was not sorted");
-            need = K * 8; src = w.keys[h.final_buf]; break;
         case KT_GS_STAGE_VALUES_SORTED:
-            if (!sorted_ok) return fail(c, KT_ERR_STATE, "the last frame was not sorted");
-            need = K * 4; src = w.vals[h.final_buf]; break;
-        case KT_GS_STAGE_TILE_RANGES: need = (uint64_t)ntiles(c) * 8; src = w.ranges; break;
+            if ((stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_VALUES_SORTED) && !sorted_ok)
+                return fail(c, KT_ERR_STATE, "the last frame was not sorted");
+            need = K * (is_keys ? 8 : 4);
+            break;
+        case KT_GS_STAGE_TILE_RANGES: need = (uint64_t)ntiles(c) * 8; break;
         default: return fail(c, KT_ERR_ARG, "unknown stage");
     }
     if (!dst) {
@@ -741,9 +739,14 @@ kt_status kt_gs_debug_dump(kt_gs_ctx* c, uint32_t path, kt_gs_stage stage, void*
         return KT_OK;
     }
     if (bytes < need) return fail(c, KT_ERR_ARG, "buffer too small: need " + std::to_string(need) + " bytes");
+    auto fetch = [&](const void* d, size_t nbytes, void* out) -> kt_status {
+        if (nbytes) KT_TRY_CUDA(c, cudaMemcpy(out, d, nbytes, cudaMemcpyDeviceToHost));
+        return KT_OK;
+    };
+    kt_status st = KT_OK;
     if (stage == KT_GS_STAGE_PROJECTED) {
         std::vector<float4> rec(3 * n);
-        if (n) KT_TRY_CUDA(c, cudaMemcpy(rec.data(), w.rec, sizeof(float4) * 3 * n, cudaMemcpyDeviceToHost));
+        if ((st = fetch(w.rec, sizeof(float4) * 3 * n, rec.data())) != KT_OK) return st;
         kt_gaussian2d* o = (kt_gaussian2d*)dst;
         for (uint64_t i = 0; i < n; ++i) {
             const float4 a = rec[3 * i], b = rec[3 * i + 1], cc = rec[3 * i + 2];
@@ -760,10 +763,55 @@ kt_status kt_gs_debug_dump(kt_gs_ctx* c, uint32_t path, kt_gs_stage stage, void*
             o[i].color[2] = cc.z;
             o[i].alpha = a.z;
         }
-    } else if (need) {
-        KT_TRY_CUDA(c, cudaMemcpy(dst, src, need, cudaMemcpyDeviceToHost));
-        if (stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_KEYS_UNSORTED)
-            expand_keys((unsigned long long*)dst, need / 8, h.depth_bits, h.depth_min);
+    } else if (stage == KT_GS_STAGE_TILE_COUNTS) {
+        if ((st = fetch(w.counts, n * 4, dst)) != KT_OK) return st;
+    } else if (stage == KT_GS_STAGE_TILE_RANGES) {
+        if ((st = fetch(w.ranges, need, dst)) != KT_OK) return st;
+    } else if (stage == KT_GS_STAGE_OFFSETS) {
+        // the reference algorithm's scan is in Gaussian index order; the renderer scans in depth
+        // order, so this dump is the index-order exclusive scan of the device's counts
+        std::vector<uint32_t> cnt(n);
+        if ((st = fetch(w.counts, n * 4, cnt.data())) != KT_OK) return st;
+        uint64_t* o = (uint64_t*)dst;
+        uint64_t run = 0;
+        for (uint64_t i = 0; i < n; ++i) {
+            o[i] = run;
+            run += cnt[i];
+        }
+    } else if (stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_VALUES_SORTED) {
+        std::vector<unsigned long long> e(K);
+        if ((st = fetch(w.keys[h.final_buf], K * 8, e.data())) != KT_OK) return st;
+        if (is_vals) {
+            uint32_t* v = (uint32_t*)dst;
+            for (uint64_t i = 0; i < K; ++i) v[i] = (uint32_t)(e[i] & imask);
+        } else {
+            std::vector<uint32_t> depth(n);
+            if ((st = fetch(w.depth, n * 4, depth.data())) != KT_OK) return st;
+            unsigned long long* k = (unsigned long long*)dst;
+            for (uint64_t i = 0; i < K; ++i)
+                k[i] = ((e[i] >> ibits) << 32) | depth[e[i] & imask];  // bin << 32 | depth bits
+        }
+    } else {
+        // pairs as the reference's binning would list them without its atomic reordering:
+        // Gaussians in index order, bins ascending; rebuilt from the device's rectangles
+        std::vector<uint32_t> cnt(n), depth(n);
+        std::vector<uint2> rect(n);
+        if ((st = fetch(w.counts, n * 4, cnt.data())) != KT_OK) return st;
+        if ((st = fetch(w.rect, n * 8, rect.data())) != KT_OK) return st;
+        if ((st = fetch(w.depth, n * 4, depth.data())) != KT_OK) return st;
+        uint64_t o = 0;
+        for (uint64_t g = 0; g < n && o < K; ++g) {
+            if (!cnt[g]) continue;
+            const uint32_t x0 = rect[g].x & 0xFFFFu, x1 = rect[g].x >> 16;
+            const uint32_t y0 = rect[g].y & 0xFFFFu, y1 = rect[g].y >> 16;
+            for (uint32_t y = y0; y < y1; ++y)
+                for (uint32_t x = x0; x < x1 && o < K; ++x, ++o) {
+                    if (is_keys)
+                        ((unsigned long long*)dst)[o] = ((unsigned long long)(y * tx + x) << 32) | depth[g];
+                    else
+                        ((uint32_t*)dst)[o] = (uint32_t)g;
+                }
+        }
     }
     if (written) *written = need;
     return KT_OK;
@@ -777,9 +825,10 @@ kt_status kt_gs_stage_times(kt_gs_ctx* c, uint32_t path, float ms[KT_GS_NSTAGES]
     KT_TRY_CUDA(c, cudaSetDevice(c->device));
     KT_TRY_CUDA(c, cudaEventSynchronize(w.done_ev));
     cudaEvent_t* ev = w.ring[w.ring_last];
-    KT_TRY_CUDA(c, cudaEventSynchronize(ev[5]));
-    for (int i = 0; i < 5; ++i) KT_TRY_CUDA(c, cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]));
-    KT_TRY_CUDA(c, cudaEventElapsedTime(&ms[5], ev[0], ev[5]));
+    constexpr int L = KT_GS_NSTAGES - 1;
+    KT_TRY_CUDA(c, cudaEventSynchronize(ev[L]));
+    for (int i = 0; i < L; ++i) KT_TRY_CUDA(c, cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]));
+    KT_TRY_CUDA(c, cudaEventElapsedTime(&ms[L], ev[0], ev[L]));
     return KT_OK;
 }
 
@@ -846,7 +895,7 @@ kt_status kt_gs_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* vals_i
     io.vals[1] = alt_v;
     io.vals[2] = vals_out;
     for (uint32_t p = 0; p < max_passes; ++p)
-        if (launch_sort_pass(io, ctl, status, p, p + 1, n, s) != cudaSuccess) return KT_ERR_CUDA;
+        if (launch_sort_pass(io, ctl, status, p, p + 1, n, false, s) != cudaSuccess) return KT_ERR_CUDA;
     return KT_OK;
 }
 

@@ -1,15 +1,14 @@
-// K2+K3: exclusive scan of the per-Gaussian bin counts (decoupled look-back) fused with the
-// emission of one (key, value) pair per overlapped bin; plus the per-frame reset, the sort
-// plan and the bin-range search (K5).
+// Binning: depth keys of the Gaussians, the exclusive scan of the per-Gaussian bin counts in
+// depth order (decoupled look-back) fused with the emission of one element per (bin, Gaussian)
+// pair; plus the per-frame reset, the sort plan and the bin-range search (K5).
 //
-// Replaces the atomicAdd duplication of shaders/gsplat/gsplat_binning.comp:112-159 (whose
-// order is nondeterministic and capped at 2N) with count -> scan -> emit, which is exact and
-// deterministic: Gaussians in index order, bins in ascending bin index per Gaussian.
-//
-// Keys are compact: (bin << depth_bits) | (depth - depth_min), where depth is
-// floatBitsToUint(z) ^ 0x80000000 (gsplat_radix_sort_include.glsl:51-63) and depth_min /
-// depth_bits come from the frame's range of depths. Subtracting the minimum is monotone, so
-// the order is exactly the order of the reference key bin<<32 | depth, with fewer sort passes.
+// The reference duplicates each projected Gaussian once per overlapped bin with atomicAdd
+// (shaders/gsplat/gsplat_binning.comp:112-159; order nondeterministic, capped at 2N) and then
+// sorts the copies by the 48-bit key bin<<32 | depth, depth = floatBitsToUint(z) ^ 0x80000000
+// (gsplat_radix_sort_include.glsl:51-63). Every copy carries its Gaussian's depth, so the same
+// order is reached by sorting the N Gaussians by depth first (stable, ties by index), emitting
+// the pairs in that order, and then sorting the pairs stably by bin alone: 2 passes over the
+// pairs instead of 5. Depths enter as depth - depth_min of the frame (monotone, fewer bits).
 #include "kt_common.cuh"
 #include "kt_kernels.h"
 
@@ -92,44 +91,95 @@ __device__ uint64_t lookback_warp(unsigned long long* status, uint32_t idx, uint
     return excl;
 }
 
-__global__ void k_frame_init(FrameCtl* ctl, uint2* ranges, uint32_t ntiles) {
+__global__ void k_frame_init(FrameCtl* ctl, FrameCtl* ctl_depth, uint2* ranges, uint32_t ntiles) {
     const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
     if (blockIdx.x == 0) {
         uint32_t* w = reinterpret_cast<uint32_t*>(ctl);
+        uint32_t* wd = reinterpret_cast<uint32_t*>(ctl_depth);
         const uint32_t nw = sizeof(FrameCtl) / 4;
-        for (uint32_t i = threadIdx.x; i < nw; i += blockDim.x) w[i] = 0u;
+        for (uint32_t i = threadIdx.x; i < nw; i += blockDim.x) {
+            w[i] = 0u;
+            wd[i] = 0u;
+        }
         __syncthreads();
         if (threadIdx.x == 0) ctl->depth_min = 0xFFFFFFFFu;
     }
     for (uint32_t t = tid; t < ntiles; t += gridDim.x * blockDim.x) ranges[t] = make_uint2(0u, 0u);
 }
 
+// Depth key of every Gaussian, (depth - depth_min) << idx_bits | index, with the digit
+// histograms of the depth sort. Gaussians that touch no bin take the largest depth; they
+// emit nothing, so where they land does not matter.
+__global__ void __launch_bounds__(256) k_depth_keys(FrameBufs fb, uint64_t n) {
+    __shared__ uint32_t s_hist[4][256];
+    const FrameCtl* ctl = fb.ctl;
+    FrameCtl* cd = fb.ctl_depth;
+    for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) (&s_hist[0][0])[i] = 0u;
+    __syncthreads();
+    const uint32_t dmin = ctl->depth_min, dmax = ctl->depth_max;
+    const bool any = dmax >= dmin;
+    const uint32_t dtop = any ? dmax - dmin : 0u;
+    const uint32_t dbits = bits_for(dtop);
+    const uint32_t ibits = bits_for(n - 1);
+    const uint32_t npass = (dbits + 7) / 8;
+    unsigned long long* out = fb.gsort[0];
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const int lane = threadIdx.x & 31;
+    const uint64_t n_up = (n + 31) & ~31ull;  // whole warps iterate together
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_up; i += stride) {
+        const bool live = i < n;
+        const uint32_t dk = live ? (fb.counts[i] != 0u ? fb.depth[i] - dmin : dtop) : 0u;
+        if (live) out[i] = ((unsigned long long)dk << ibits) | i;
+        for (uint32_t p = 0; p < npass; ++p) {
+            // lanes with the same digit add once (the top digits of nearby depths collide)
+            const uint32_t d = live ? (dk >> (8 * p)) & 255u : 256u;
+            const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
+            if (live && lane == __ffs(peers) - 1) atomicAdd(&s_hist[p][d], (uint32_t)__popc(peers));
+        }
+    }
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < npass * 256; i += blockDim.x) {
+        const uint32_t v = (&s_hist[0][0])[i];
+        if (v) atomicAdd(&(&cd->hist[0][0])[i], v);
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        cd->num_keys = n;
+        cd->key_bits = dbits;
+        cd->idx_bits = ibits;
+        cd->packed = 1u;
+    }
+}
+
 __global__ void __launch_bounds__(kScanThreads) k_scan_emit(FrameBufs fb, GridParams gp, uint64_t n,
                                                             uint32_t epoch, uint32_t max_passes) {
     __shared__ uint32_t s_off[kScanChunk + 1];
     __shared__ uint2 s_rect[kScanChunk];
-    __shared__ uint32_t s_depth[kScanChunk];
-    __shared__ uint32_t s_hist[kMaxPasses][256];
+    __shared__ uint32_t s_gid[kScanChunk];
     __shared__ uint32_t s_warp[8];
     __shared__ uint32_t s_chunk;
     __shared__ unsigned long long s_base;
 
     FrameCtl* ctl = fb.ctl;
+    const FrameCtl* cd = fb.ctl_depth;
     const int tid = threadIdx.x;
     if (tid == 0) s_chunk = atomicAdd(&ctl->scan_ticket, 1u);
-    for (int i = tid; i < kMaxPasses * 256; i += kScanThreads) (&s_hist[0][0])[i] = 0u;
     __syncthreads();
     const uint32_t chunk = s_chunk;
     const uint64_t nchunks = (n + kScanChunk - 1) / kScanChunk;
     const uint64_t c0 = (uint64_t)chunk * kScanChunk;
+    // Gaussians in depth order: the sorted depth keys carry the index in their low bits
+    const unsigned long long* order = io_select(fb.gsort, cd->final_buf);
+    const uint32_t ibits = cd->idx_bits;
+    const unsigned long long imask = (1ull << ibits) - 1ull;
 
-    // counts of this thread's 8 consecutive Gaussians
-    uint32_t c[kScanItems];
+    // counts of this thread's 8 consecutive positions in depth order
+    uint32_t c[kScanItems], gid[kScanItems];
     uint32_t sum = 0;
 #pragma unroll
     for (int j = 0; j < kScanItems; ++j) {
-        const uint64_t g = c0 + (uint64_t)tid * kScanItems + j;
-        c[j] = g < n ? fb.counts[g] : 0u;
+        const uint64_t q = c0 + (uint64_t)tid * kScanItems + j;
+        gid[j] = q < n ? (uint32_t)(order[q] & imask) : 0u;
+        c[j] = q < n ? fb.counts[gid[j]] : 0u;
         sum += c[j];
     }
     uint32_t total;
@@ -139,11 +189,10 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_emit(FrameBufs fb, GridPa
 #pragma unroll
         for (int j = 0; j < kScanItems; ++j) {
             const int l = tid * kScanItems + j;
-            const uint64_t g = c0 + l;
             s_off[l] = run;
             if (c[j] != 0u) {
-                s_rect[l] = fb.rect[g];
-                s_depth[l] = fb.depth[g];
+                s_rect[l] = fb.rect[gid[j]];
+                s_gid[l] = gid[j];
             }
             run += c[j];
         }
@@ -156,54 +205,162 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_emit(FrameBufs fb, GridPa
     __syncthreads();
     const uint64_t base = s_base;
 
-#pragma unroll
-    for (int j = 0; j < kScanItems; ++j) {
-        const int l = tid * kScanItems + j;
-        const uint64_t g = c0 + l;
-        if (g < n) fb.offsets[g] = base + s_off[l];
-    }
-
-    // every CTA derives the same key layout from the frame's depth range
-    const uint32_t dmin = ctl->depth_min, dmax = ctl->depth_max;
-    const uint32_t dbits = dmax >= dmin ? bits_for((uint64_t)(dmax - dmin)) : 0u;
-    const uint32_t key_bits = gp.tile_bits + dbits;
-    uint32_t npasses = (key_bits + 7) / 8;
-    if (npasses > max_passes) npasses = max_passes;
+    // pairs: bin << idx_bits | index; the sort by bin is stable, so depth order survives
+    // (the digit histograms of that sort come from k_bin_finalize)
+    const uint32_t key_bits = gp.tile_bits;
     const bool fits = base + total <= fb.key_capacity;
     unsigned long long* keys = fb.keys[0];
-    uint32_t* vals = fb.vals[0];
 
-    for (uint32_t s = tid; s < total; s += kScanThreads) {
-        // last Gaussian whose local offset is <= s (zero-count Gaussians share offsets)
-        int lo = 0, hi = kScanChunk;
-        while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (s_off[mid] <= s) lo = mid; else hi = mid;
+    // Emission: warp w walks its 256 positions in order; the lanes write one Gaussian's bins
+    // (row-major over its rectangle) as one coalesced run.
+    const int lane = tid & 31, warp = tid >> 5;
+    for (int q0 = warp * (kScanChunk / 8); q0 < (warp + 1) * (kScanChunk / 8); q0 += 32) {
+        const int q = q0 + lane;
+        uint32_t todo = __ballot_sync(0xFFFFFFFFu, s_off[q + 1] != s_off[q]);
+        while (todo) {
+            const int l = q0 + __ffs(todo) - 1;
+            todo &= todo - 1u;
+            const uint32_t off = s_off[l], cnt = s_off[l + 1] - off;
+            const uint2 r = s_rect[l];
+            const uint32_t gid = s_gid[l];
+            const uint32_t x0 = r.x & 0xFFFFu, x1 = r.x >> 16, y0 = r.y & 0xFFFFu;
+            const uint32_t w = x1 - x0;
+            const float inv_w = 1.0f / (float)w;
+            for (uint32_t j = lane; j < cnt; j += 32) {
+                uint32_t dy = (uint32_t)((float)j * inv_w);  // j / w, then corrected exactly
+                if (dy * w > j) --dy;
+                if ((dy + 1) * w <= j) ++dy;
+                const uint32_t tile = (y0 + dy) * gp.tiles_x + x0 + (j - dy * w);
+                if (fits) keys[base + off + j] = ((unsigned long long)tile << ibits) | gid;
+            }
         }
-        const uint32_t j = s - s_off[lo];
-        const uint2 r = s_rect[lo];
-        const uint32_t x0 = r.x & 0xFFFFu, x1 = r.x >> 16, y0 = r.y & 0xFFFFu;
-        const uint32_t w = x1 - x0;
-        const uint32_t dy = j / w;
-        const uint32_t tx = x0 + (j - dy * w), ty = y0 + dy;
-        const uint64_t tile = (uint64_t)ty * gp.tiles_x + tx;
-        const unsigned long long key = (tile << dbits) | (uint64_t)(s_depth[lo] - dmin);
-        if (fits) {
-            keys[base + s] = key;
-            vals[base + s] = (uint32_t)(c0 + lo);
-        }
-        for (uint32_t p = 0; p < npasses; ++p) atomicAdd(&s_hist[p][(key >> (8 * p)) & 255u], 1u);
-    }
-    __syncthreads();
-    for (uint32_t i = tid; i < npasses * 256; i += kScanThreads) {
-        const uint32_t v = (&s_hist[0][0])[i];
-        if (v) atomicAdd(&(&ctl->hist[0][0])[i], v);
     }
     if (tid == 0 && (uint64_t)chunk == nchunks - 1) {
+        const uint32_t dmin = ctl->depth_min, dmax = ctl->depth_max;
         ctl->num_keys = base + total;
-        ctl->depth_bits = dbits;
+        ctl->depth_bits = dmax >= dmin ? bits_for((uint64_t)(dmax - dmin)) : 0u;
         ctl->key_bits = key_bits;
+        ctl->packed = 1u;
+        ctl->idx_bits = ibits;
     }
+}
+
+// Per-bin pair counts from the Gaussians' bin rectangles: +1/-1 at the four corners of each
+// rectangle in a (tiles_y + 1) x (tiles_x + 1) difference table, accumulated per CTA in shared
+// memory when it fits (4 atomics per Gaussian instead of one per pair).
+__global__ void __launch_bounds__(512) k_bin_diff(FrameBufs fb, GridParams gp, uint64_t n, int* gdiff,
+                                                  int use_smem) {
+    extern __shared__ int s_diff[];
+    const uint32_t W1 = gp.tiles_x + 1;
+    const uint32_t cells = W1 * (gp.tiles_y + 1);
+    int* table = use_smem ? s_diff : gdiff;
+    if (use_smem) {
+        for (uint32_t i = threadIdx.x; i < cells; i += blockDim.x) s_diff[i] = 0;
+        __syncthreads();
+    }
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        if (fb.counts[i] == 0u) continue;
+        const uint2 r = fb.rect[i];
+        const uint32_t x0 = r.x & 0xFFFFu, x1 = r.x >> 16, y0 = r.y & 0xFFFFu, y1 = r.y >> 16;
+        atomicAdd(&table[y0 * W1 + x0], 1);
+        atomicAdd(&table[y0 * W1 + x1], -1);
+        atomicAdd(&table[y1 * W1 + x0], -1);
+        atomicAdd(&table[y1 * W1 + x1], 1);
+    }
+    if (use_smem) {
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < cells; i += blockDim.x)
+            if (s_diff[i] != 0) atomicAdd(&gdiff[i], s_diff[i]);
+    }
+}
+
+// One CTA of 1024 threads: 2D prefix sums of the difference table (in place) give the pairs per
+// bin; their exclusive scan gives every bin's range {start, end} in the sorted pair list (empty
+// bins stay {0, 0}, as the reference's zeroed StartAndEnd buffer), and their digits give the
+// histograms of the bin sort. The table is left zeroed for the next frame.
+__global__ void __launch_bounds__(1024) k_bin_finalize(FrameBufs fb, GridParams gp, int* gdiff,
+                                                       uint32_t max_passes) {
+    __shared__ uint32_t s_hist[kMaxPasses][256];
+    __shared__ uint32_t s_warp[32];
+    __shared__ unsigned long long s_carry;
+    const uint32_t tx = gp.tiles_x, ty = gp.tiles_y, W1 = tx + 1;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < kMaxPasses * 256; i += blockDim.x) (&s_hist[0][0])[i] = 0u;
+    // prefix along x, one warp per row
+    for (uint32_t row = warp; row < ty; row += 32) {
+        int carry = 0;
+        for (uint32_t x0 = 0; x0 < tx; x0 += 32) {
+            const uint32_t x = x0 + lane;
+            int v = x < tx ? gdiff[row * W1 + x] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xFFFFFFFFu, v, o);
+                if (lane >= o) v += y;
+            }
+            if (x < tx) gdiff[row * W1 + x] = v + carry;
+            carry += __shfl_sync(0xFFFFFFFFu, v, 31);
+        }
+    }
+    __syncthreads();
+    // prefix along y, one warp per column: the pairs of bin (row, x)
+    for (uint32_t x = warp; x < tx; x += 32) {
+        int carry = 0;
+        for (uint32_t y0 = 0; y0 < ty; y0 += 32) {
+            const uint32_t y = y0 + lane;
+            int v = y < ty ? gdiff[y * W1 + x] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xFFFFFFFFu, v, o);
+                if (lane >= o) v += t;
+            }
+            if (y < ty) gdiff[y * W1 + x] = v + carry;
+            carry += __shfl_sync(0xFFFFFFFFu, v, 31);
+        }
+    }
+    __syncthreads();
+    // exclusive scan over bins in row-major order, 1024 bins per round
+    uint32_t npasses = (gp.tile_bits + 7) / 8;
+    if (npasses > max_passes) npasses = max_passes;
+    const uint32_t nbins = tx * ty;
+    if (tid == 0) s_carry = 0ull;
+    __syncthreads();
+    for (uint32_t b0 = 0; b0 < nbins; b0 += 1024) {
+        const uint32_t b = b0 + tid;
+        const uint32_t by = b / tx, bx = b - by * tx;
+        const uint32_t cnt = b < nbins ? (uint32_t)gdiff[by * W1 + bx] : 0u;
+        uint32_t x = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, x, o);
+            if (lane >= o) x += t;
+        }
+        if (lane == 31) s_warp[warp] = x;
+        __syncthreads();
+        if (warp == 0) {
+            uint32_t w = s_warp[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, w, o);
+                if (lane >= o) w += t;
+            }
+            s_warp[lane] = w;
+        }
+        __syncthreads();
+        const unsigned long long start = s_carry + (warp ? s_warp[warp - 1] : 0u) + x - cnt;
+        if (b < nbins) {
+            fb.ranges[b] = cnt ? make_uint2((uint32_t)start, (uint32_t)(start + cnt)) : make_uint2(0u, 0u);
+            for (uint32_t p = 0; p < npasses; ++p)
+                if (cnt) atomicAdd(&s_hist[p][(b >> (8 * p)) & 255u], cnt);
+        }
+        __syncthreads();
+        if (tid == 0) s_carry += s_warp[31];
+        __syncthreads();
+    }
+    // clear the table for the next frame (every cell, including the padding row and column)
+    const uint32_t cells = W1 * (ty + 1);
+    for (uint32_t i = tid; i < cells; i += blockDim.x) gdiff[i] = 0;
+    for (uint32_t i = tid; i < npasses * 256; i += blockDim.x) (&fb.ctl->hist[0][0])[i] = (&s_hist[0][0])[i];
 }
 
 // One CTA of 256 threads: which passes move data, their bucket bases and buffer order.
@@ -264,44 +421,60 @@ __global__ void __launch_bounds__(256) k_plan(FrameCtl* ctl, uint64_t capacity, 
     }
 }
 
-__global__ void k_ranges(SortIO io, const FrameCtl* ctl, uint2* ranges, FrameTotals* totals) {
-    // every earlier kernel of the frame has finished: fold its error bits and sizes into the
-    // running totals
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-        if (ctl->error_flags) atomicOr(&totals->sticky_errors, ctl->error_flags);
-        if (ctl->plan_ok) {
-            totals->frames += 1ull;
-            totals->keys += ctl->num_keys;
-            totals->key_passes += ctl->num_keys * (unsigned long long)ctl->passes_run;
-            totals->visible += ctl->num_visible;
-        }
-    }
-    if (!ctl->plan_ok) return;
-    const uint64_t K = ctl->num_keys;
-    const uint32_t dbits = ctl->depth_bits;
-    const unsigned long long* keys = io_keys(io, ctl->final_buf);
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < K; i += stride) {
-        const uint32_t t = (uint32_t)(keys[i] >> dbits);
-        if (i == K - 1) {  // gsplat_bin_bounds.comp:44-52
-            ranges[t].y = (uint32_t)(i + 1);
-        } else {
-            const uint32_t tn = (uint32_t)(keys[i + 1] >> dbits);
-            if (t != tn) {  // comp:64-70
-                ranges[t].y = (uint32_t)(i + 1);
-                ranges[tn].x = (uint32_t)(i + 1);
-            }
-        }
+// After the last sort pass: fold the frame's error bits and sizes into the running totals
+// (kt_gs_counters, kt_gs_sync).
+__global__ void k_frame_totals(const FrameCtl* ctl, const FrameCtl* ctl_depth, FrameTotals* totals) {
+    if (ctl->error_flags) atomicOr(&totals->sticky_errors, ctl->error_flags);
+    if (ctl->plan_ok) {
+        totals->frames += 1ull;
+        totals->keys += ctl->num_keys;
+        totals->key_passes += ctl->num_keys * (unsigned long long)ctl->passes_run;
+        totals->visible += ctl->num_visible;
+        totals->sort_bytes += ctl->num_keys * (unsigned long long)ctl->passes_run * 16ull;
+        totals->depth_sort_bytes += ctl_depth->num_keys * (unsigned long long)ctl_depth->passes_run * 16ull;
     }
 }
 
 }  // namespace
 
-cudaError_t launch_frame_init(FrameCtl* ctl, uint2* ranges, uint32_t ntiles, cudaStream_t stream) {
+cudaError_t launch_frame_init(FrameCtl* ctl, FrameCtl* ctl_depth, uint2* ranges, uint32_t ntiles,
+                              cudaStream_t stream) {
     unsigned blocks = (ntiles + 255) / 256;
     if (blocks < 1) blocks = 1;
     if (blocks > 1024) blocks = 1024;
-    k_frame_init<<<blocks, 256, 0, stream>>>(ctl, ranges, ntiles);
+    k_frame_init<<<blocks, 256, 0, stream>>>(ctl, ctl_depth, ranges, ntiles);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bin_counts(const FrameBufs& fb, const GridParams& gp, uint64_t n, int* gdiff,
+                              uint32_t max_passes, cudaStream_t stream) {
+    const size_t cells = (size_t)(gp.tiles_x + 1) * (gp.tiles_y + 1);
+    const size_t smem = cells * sizeof(int);
+    const bool use_smem = smem <= 96 * 1024;
+    static bool attr_set[128] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (use_smem && dev >= 0 && dev < 128 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(k_bin_diff, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    if (n > 0) {
+        uint64_t blocks = (n + 511) / 512;
+        const uint64_t cap = (uint64_t)device_sm_count() * (use_smem ? 2 : 8);
+        if (blocks > cap) blocks = cap;
+        k_bin_diff<<<(unsigned)blocks, 512, use_smem ? smem : 0, stream>>>(fb, gp, n, gdiff, use_smem ? 1 : 0);
+    }
+    k_bin_finalize<<<1, 1024, 0, stream>>>(fb, gp, gdiff, max_passes);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_depth_keys(const FrameBufs& fb, uint64_t n, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    uint64_t blocks = (n + 255) / 256;
+    const uint64_t cap = (uint64_t)device_sm_count() * 8;
+    if (blocks > cap) blocks = cap;
+    k_depth_keys<<<(unsigned)blocks, 256, 0, stream>>>(fb, n);
     return cudaGetLastError();
 }
 
@@ -319,9 +492,9 @@ cudaError_t launch_plan(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes, i
     return cudaGetLastError();
 }
 
-cudaError_t launch_ranges(const SortIO& io, const FrameCtl* ctl, uint2* ranges, FrameTotals* totals,
-                          cudaStream_t stream) {
-    k_ranges<<<device_sm_count() * 8, 256, 0, stream>>>(io, ctl, ranges, totals);
+cudaError_t launch_frame_totals(const FrameCtl* ctl, const FrameCtl* ctl_depth, FrameTotals* totals,
+                                cudaStream_t stream) {
+    k_frame_totals<<<1, 1, 0, stream>>>(ctl, ctl_depth, totals);
     return cudaGetLastError();
 }
 

@@ -8,8 +8,8 @@
 //                        degree d interleaved per coefficient (R,G,B), DC first
 //   per path       rec   float4[3N] (px, py, alpha, z) (covInv 00,01,10,11) (r, g, b, 0)
 //                  counts u32[N], rect u32x2[N] (x0|x1<<16, y0|y1<<16), depth u32[N],
-//                  offsets u64[N], keys u64[2][cap], vals u32[2][cap],
-//                  ranges u32x2[tiles], look-back status words, FrameCtl.
+//                  gsort u64[2][N] (Gaussians by depth), keys u64[2][cap] (pairs by bin),
+//                  ranges u32x2[tiles], look-back status words, two FrameCtl blocks.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -49,6 +49,8 @@ struct FrameCtl {
     unsigned int key_bits;
     unsigned int passes_run;
     unsigned int final_buf;           // which key/value buffer holds the sorted data
+    unsigned int packed;              // 1: elements are (key << idx_bits) | index, no value array
+    unsigned int idx_bits;            // bits of the index field of a packed element (0 unpacked)
     unsigned int pass_ticket[kMaxPasses];
     unsigned int pass_run[kMaxPasses];
     unsigned int pass_src[kMaxPasses];
@@ -64,6 +66,8 @@ struct FrameTotals {
     unsigned long long keys;
     unsigned long long key_passes;
     unsigned long long visible;
+    unsigned long long sort_bytes;
+    unsigned long long depth_sort_bytes;
     unsigned int sticky_errors;  // error bits of every frame since the last sync
     unsigned int pad;
 };
@@ -104,13 +108,13 @@ struct FrameBufs {
     uint32_t* counts;
     uint2* rect;
     uint32_t* depth;
-    unsigned long long* offsets;
-    unsigned long long* keys[2];
-    uint32_t* vals[2];
+    unsigned long long* gsort[2];  // Gaussians by depth: (depth - min) << idx_bits | index
+    unsigned long long* keys[2];   // (bin, Gaussian) pairs: bin << idx_bits | index
     uint2* ranges;
     unsigned long long* scan_status;
     unsigned long long* sort_status;
-    FrameCtl* ctl;
+    FrameCtl* ctl;                 // the frame, and the sort of the pairs by bin
+    FrameCtl* ctl_depth;           // the sort of the Gaussians by depth
     uint64_t key_capacity;
 };
 
@@ -124,8 +128,74 @@ __device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned 
     asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
+// Look-back status words: relaxed, device-scope (coherent at L2) loads and stores.
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 // SM count of the current device (cached per device).
 int device_sm_count();
+
+// ---- mbarrier / bulk-copy helpers (sm_90+ PTX; no cluster multicast anywhere)
+#ifdef __CUDACC__
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Order this thread's earlier generic-proxy shared-memory accesses before later async-proxy
+// (bulk copy) accesses to the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// Global -> shared bulk copy (16-B aligned addresses, size a multiple of 16), completing on `bar`.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
+                                              unsigned long long* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for phase `parity` of `bar`; false if it did not complete within `limit` polls.
+__device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+#endif  // __CUDACC__
 
 __host__ __device__ inline uint32_t bits_for(uint64_t v) {
     uint32_t b = 0;

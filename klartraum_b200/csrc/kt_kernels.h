@@ -20,6 +20,9 @@ __device__ __forceinline__ unsigned long long* io_keys(const SortIO& io, uint32_
 __device__ __forceinline__ uint32_t* io_vals(const SortIO& io, uint32_t i) {
     return i == 0 ? io.vals[0] : (i == 1 ? io.vals[1] : io.vals[2]);
 }
+__device__ __forceinline__ const unsigned long long* io_select(unsigned long long* const (&b)[2], uint32_t i) {
+    return i == 0 ? b[0] : b[1];
+}
 
 constexpr int kScanChunk = 2048;  // Gaussians per scan/emit CTA
 constexpr int kSortTile = 4096;   // keys per onesweep CTA iteration
@@ -34,20 +37,28 @@ cudaError_t launch_pack_scene(const float* d_aos, uint64_t n, float4* pos, float
                               cudaStream_t stream);
 
 // binning.cu
-cudaError_t launch_frame_init(FrameCtl* ctl, uint2* ranges, uint32_t ntiles, cudaStream_t stream);
+cudaError_t launch_frame_init(FrameCtl* ctl, FrameCtl* ctl_depth, uint2* ranges, uint32_t ntiles,
+                              cudaStream_t stream);
+cudaError_t launch_depth_keys(const FrameBufs& fb, uint64_t n, cudaStream_t stream);
+// per-bin pair counts (2D difference table `gdiff`, zero on entry and on exit) -> bin ranges and
+// the digit histograms of the bin sort
+cudaError_t launch_bin_counts(const FrameBufs& fb, const GridParams& gp, uint64_t n, int* gdiff,
+                              uint32_t max_passes, cudaStream_t stream);
 cudaError_t launch_scan_emit(const FrameBufs& fb, const GridParams& gp, uint64_t n, uint32_t epoch,
                              uint32_t max_passes, cudaStream_t stream);
 // mode 0: ping-pong between io.keys[0] and [1]; mode 1: [0] -> ... -> [2] via [1]
 cudaError_t launch_plan(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes, int mode,
                         cudaStream_t stream);
-cudaError_t launch_ranges(const SortIO& io, const FrameCtl* ctl, uint2* ranges, FrameTotals* totals,
-                          cudaStream_t stream);
+cudaError_t launch_frame_totals(const FrameCtl* ctl, const FrameCtl* ctl_depth, FrameTotals* totals,
+                                cudaStream_t stream);
 
 // sort.cu
 cudaError_t launch_key_histogram(const unsigned long long* keys, uint64_t n, uint32_t key_bits,
                                  FrameCtl* ctl, cudaStream_t stream);
+// packed: launch the variant for (key << idx_bits | index) elements; the variant that does not
+// match the frame's layout (FrameCtl::packed) returns at once.
 cudaError_t launch_sort_pass(const SortIO& io, FrameCtl* ctl, unsigned long long* status,
-                             uint32_t pass, uint32_t epoch, uint64_t max_keys,
+                             uint32_t pass, uint32_t epoch, uint64_t max_keys, bool packed,
                              cudaStream_t stream);
 size_t sort_status_words(uint64_t max_keys);
 

@@ -21,18 +21,32 @@ namespace {
 constexpr int kRasterThreads = 256;
 constexpr int kBatch = 256;
 
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // One blend step: a = exp(-0.5 * dot(d, covInv d)) * alpha; C += color * a * T; T *= 1 - a.
-// `cq` is covInv pre-multiplied by -0.5 * log2(e) so that the exponential is one exp2.
-__device__ __forceinline__ void blend(float fx, float fy, const float4& p, const float4& cq, const float4& col,
+// `q` = (A, B, C, alpha) with A = covInv[0][0] * k, B = (covInv[0][1] + covInv[1][0]) * k,
+// C = covInv[1][1] * k and k = -0.5 * log2(e), so the exponent is one quadratic form and the
+// exponential one exp2. T *= 1 - a is evaluated as T -= a * T.
+__device__ __forceinline__ void blend(float fx, float fy, float2 mean, const float4& q, const float4& col,
                                       float& C0, float& C1, float& C2, float& T) {
-    const float dx = fx - p.x, dy = fy - p.y;
-    const float sx = cq.x * dx + cq.z * dy;
-    const float sy = cq.y * dx + cq.w * dy;
-    const float a = exp2f(dx * sx + dy * sy) * p.z;
-    C0 += col.x * a * T;
-    C1 += col.y * a * T;
-    C2 += col.z * a * T;
-    T *= (1.0f - a);
+    const float dx = fx - mean.x, dy = fy - mean.y;
+    const float t = fmaf(q.y, dy, q.x * dx);
+    const float power = fmaf(q.z * dy, dy, dx * t);
+    const float a = ex2_approx(power) * q.w;
+    const float w = a * T;
+    C0 = fmaf(col.x, w, C0);
+    C1 = fmaf(col.y, w, C1);
+    C2 = fmaf(col.z, w, C2);
+    T -= w;
+}
+
+__device__ __forceinline__ float4 quad_form(float4 cov, float alpha) {
+    const float k = -0.5f * 1.44269504088896340736f;  // -0.5 * log2(e)
+    return make_float4(cov.x * k, (cov.y + cov.z) * k, cov.w * k, alpha);
 }
 
 template <bool PER_ELEM>
@@ -40,9 +54,9 @@ __global__ void __launch_bounds__(kRasterThreads)
 k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__ ranges,
             const FrameCtl* __restrict__ ctl, GridParams gp, uchar4* __restrict__ img,
             uint32_t ypix0) {
-    __shared__ float4 s_pos[kBatch];  // px, py, alpha, z
-    __shared__ float4 s_cov[kBatch];  // covInv * (-0.5 log2 e)
-    __shared__ float4 s_col[kBatch];  // r, g, b
+    __shared__ float2 s_mean[kBatch];  // px, py
+    __shared__ float4 s_q[kBatch];     // quadratic form, alpha
+    __shared__ float4 s_col[kBatch];   // r, g, b
     if (!ctl->plan_ok) return;
 
     const int tid = threadIdx.x;
@@ -53,9 +67,15 @@ k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__
     const uint2 r = ranges[bin];
     const uint32_t start = r.x, end = r.y;
     const uint32_t preend = start + ((end - start) / 64) * 64;
+    // sorted Gaussian indices: the low idx_bits of packed elements, or the value array
+    const bool packed = ctl->packed != 0;
+    const unsigned long long* __restrict__ elems = io_keys(io, ctl->final_buf);
     const uint32_t* __restrict__ vals = io_vals(io, ctl->final_buf);
+    const unsigned long long imask = (1ull << ctl->idx_bits) - 1ull;
+    auto index_at = [&](uint32_t i) -> uint32_t {
+        return packed ? (uint32_t)(elems[i] & imask) : vals[i];
+    };
     const float tmin = (float)(1.0 - 0.9999);
-    const float kq = -0.5f * 1.44269504088896340736f;  // -0.5 * log2(e)
     const float fx = (float)px, fy = (float)py;
 
     float C0 = 0.0f, C1 = 0.0f, C2 = 0.0f, T = 1.0f;
@@ -69,27 +89,37 @@ k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__
         if (__syncthreads_and(done || wait_tail)) break;
         const uint32_t nb = min((uint32_t)kBatch, end - b);
         if ((uint32_t)tid < nb) {
-            const uint32_t idx = vals[b + tid];
-            const float4 c = rec[3 * (uint64_t)idx + 1];
-            s_pos[tid] = rec[3 * (uint64_t)idx + 0];
-            s_cov[tid] = make_float4(c.x * kq, c.y * kq, c.z * kq, c.w * kq);
+            const uint32_t idx = index_at(b + tid);
+            const float4 p = rec[3 * (uint64_t)idx + 0];
+            s_mean[tid] = make_float2(p.x, p.y);
+            s_q[tid] = quad_form(rec[3 * (uint64_t)idx + 1], p.z);
             s_col[tid] = rec[3 * (uint64_t)idx + 2];
         }
         __syncthreads();
         if (done || wait_tail) continue;
-        for (uint32_t jj = 0; jj < nb; ++jj) {
-            const uint32_t pos = b + jj;
-            blend(fx, fy, s_pos[jj], s_cov[jj], s_col[jj], C0, C1, C2, T);
-            if (PER_ELEM) {
+        if (PER_ELEM) {
+            for (uint32_t jj = 0; jj < nb; ++jj) {
+                blend(fx, fy, s_mean[jj], s_q[jj], s_col[jj], C0, C1, C2, T);
                 if (T <= tmin) { done = true; break; }
-            } else if (pos < preend) {
-                if (((pos + 1 - start) & 63u) == 0u && T <= tmin) {
+            }
+            continue;
+        }
+        // 64-element blocks counted from `start` (batches start 256 apart, so blocks align)
+        for (uint32_t j0 = 0; j0 < nb; j0 += 64) {
+            if (b + j0 < preend) {  // a whole 64-batch of the reference: test once at its end
+#pragma unroll 8
+                for (uint32_t jj = j0; jj < j0 + 64; ++jj)
+                    blend(fx, fy, s_mean[jj], s_q[jj], s_col[jj], C0, C1, C2, T);
+                if (T <= tmin) {
                     wait_tail = preend < end;
                     done = !wait_tail;
                     break;
                 }
-            } else if (T <= tmin) {
-                done = true;
+            } else {  // the tail: test after every element
+                for (uint32_t jj = j0; jj < nb; ++jj) {
+                    blend(fx, fy, s_mean[jj], s_q[jj], s_col[jj], C0, C1, C2, T);
+                    if (T <= tmin) { done = true; break; }
+                }
                 break;
             }
         }
@@ -97,9 +127,9 @@ k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__
     if (wait_tail) {
         // the tail loop from `preend`: one element unless that element raised T again
         for (uint32_t i = preend; i < end; ++i) {
-            const uint32_t idx = vals[i];
-            const float4 c = rec[3 * (uint64_t)idx + 1];
-            blend(fx, fy, rec[3 * (uint64_t)idx + 0], make_float4(c.x * kq, c.y * kq, c.z * kq, c.w * kq),
+            const uint32_t idx = index_at(i);
+            const float4 p = rec[3 * (uint64_t)idx + 0];
+            blend(fx, fy, make_float2(p.x, p.y), quad_form(rec[3 * (uint64_t)idx + 1], p.z),
                   rec[3 * (uint64_t)idx + 2], C0, C1, C2, T);
             if (T <= tmin) break;
         }

@@ -1,20 +1,21 @@
-// K4: onesweep LSD radix sort of (u64 key, u32 value) pairs, 8-bit digits.
+// K4: onesweep LSD radix sort, 8-bit digits, one kernel per digit.
 //
-// Replaces the reference's 12-pass 4-bit sort, whose prefix sum runs on one workgroup and
-// whose scatter walks 128 elements per thread serially
-// (shaders/gsplat/gsplat_radix_sort_{histogram,hist_prefix_sum,hist_scatter}.comp). Same
-// result: a stable sort by key. One kernel per digit:
-//   * a CTA takes the next 4096-key tile by ticket (so earlier tiles always have an owner),
-//   * ranks its keys per warp with __match_any_sync (warp-level multisplit), stable in
-//     position order,
-//   * publishes its per-digit counts and looks back over earlier tiles' counts (decoupled
-//     look-back, bounded waits) for its global digit offsets,
-//   * stages the keys in shared memory in digit order and writes them out in coalesced runs.
-// Digit histograms of all passes come from the emission kernel (render path) or
-// k_key_histogram (standalone operator); a pass whose keys all share one digit is skipped.
-//
-// Roofline: HBM bound, 24 B moved per key per executed pass (read + write of 8 B key and
-// 4 B value).
+// Replaces the reference's 12-pass 4-bit sort, whose prefix sum runs on one workgroup and whose
+// scatter walks 128 elements per thread serially
+// (shaders/gsplat/gsplat_radix_sort_{histogram,hist_prefix_sum,hist_scatter}.comp). Same result:
+// a stable sort by key. Per pass, a persistent CTA
+//   * takes 4096-element tiles by ticket, so every earlier tile always has a running owner,
+//   * prefetches its next tile into shared memory with a TMA bulk copy (cp.async.bulk, completion
+//     on an mbarrier; no multicast) while it ranks the current one,
+//   * ranks keys per warp with __match_any_sync (warp multisplit), stable in position order,
+//   * publishes per-digit tile counts and looks back over earlier tiles' counts (decoupled
+//     look-back, 4 predecessors per round trip, bounded waits) for its global digit offsets,
+//   * stages the tile in digit order in the input buffer it has finished reading and writes it
+//     out in coalesced runs.
+// Elements are either packed u64 words (key << idx_bits | index: 16 B moved per element per pass,
+// ties already ordered by the index bits) or u64 keys with a separate u32 value array (24 B).
+// Digit histograms of every pass come from the emission kernel (render path) or from
+// k_key_histogram (standalone operator); passes whose keys share one digit are skipped.
 #include "kt_common.cuh"
 #include "kt_kernels.h"
 
@@ -23,17 +24,21 @@ namespace {
 
 constexpr int kSortThreads = 256;
 constexpr int kSortWarps = kSortThreads / 32;
-constexpr int kSortItems = kSortTile / kSortThreads;  // 16 keys per thread
-constexpr int kWarpKeys = kSortItems * 32;            // 512 consecutive keys per warp
+constexpr int kSortItems = kSortTile / kSortThreads;  // 16 elements per thread
+constexpr int kWarpKeys = kSortItems * 32;            // 512 consecutive elements per warp
+constexpr uint32_t kBarSpinLimit = 1u << 22;
 
+template <bool PACKED>
 struct SortSmem {
-    unsigned long long keys[kSortTile];
-    uint32_t vals[kSortTile];
-    uint32_t whist[kSortWarps][256];
-    uint32_t lstart[256];
-    unsigned long long gbase[256];
+    unsigned long long keys[2][kSortTile];                 // input tiles; the current one is
+    uint32_t vals[PACKED ? 1 : 2][PACKED ? 4 : kSortTile];  //   reused as the staging buffer
+    uint16_t whist[kSortWarps][256];                       // per-warp digit counts, then prefixes
+    uint32_t tcount[256];                                  // the tile's digit counts (early)
+    uint32_t lstart[256];                                  // tile-local digit starts
+    unsigned long long gbase[256];                         // global start of each digit's run
     uint32_t warp_tot[kSortWarps];
-    uint32_t tile;
+    uint32_t tile[2];
+    unsigned long long bar[2];                             // one mbarrier per input buffer
 };
 
 __device__ __forceinline__ uint32_t lanemask_lt() {
@@ -42,15 +47,63 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
     return m;
 }
 
-__global__ void __launch_bounds__(kSortThreads, 2)
+// Issue the bulk copy of a full tile into buffer `b` (thread 0 only).
+template <bool PACKED>
+__device__ __forceinline__ void issue_tile(SortSmem<PACKED>& sm, int b, uint64_t tbase,
+                                           const unsigned long long* src_k, const uint32_t* src_v) {
+    fence_proxy_async_smem();
+    const uint32_t kbytes = kSortTile * 8, vbytes = PACKED ? 0u : kSortTile * 4;
+    mbar_arrive_expect_tx(&sm.bar[b], kbytes + vbytes);
+    bulk_copy_g2s(sm.keys[b], src_k + tbase, kbytes, &sm.bar[b]);
+    if (!PACKED) bulk_copy_g2s(sm.vals[b], src_v + tbase, vbytes, &sm.bar[b]);
+}
+
+constexpr int kLookbackWindow = 16;  // predecessors read per round trip
+
+// Decoupled look-back for one digit: sum of this digit's counts over all earlier tiles.
+__device__ __forceinline__ uint64_t lookback_digit(const unsigned long long* status, uint32_t tile,
+                                                   uint32_t digit, uint32_t epoch, FrameCtl* ctl) {
+    uint64_t excl = 0;
+    int64_t j = (int64_t)tile - 1;
+    uint32_t spins = 0;
+    while (j >= 0) {
+        uint64_t w[kLookbackWindow];
+#pragma unroll
+        for (int q = 0; q < kLookbackWindow; ++q)
+            w[q] = (j - q >= 0) ? ld_relaxed_u64(status + (uint64_t)(j - q) * 256 + digit) : 0ull;
+        int used = 0;
+        bool incl = false;
+#pragma unroll
+        for (int q = 0; q < kLookbackWindow; ++q) {
+            if (incl || used != q || j - q < 0) continue;
+            if (status_epoch(w[q]) != epoch || status_flag(w[q]) == 0) continue;
+            excl += status_value(w[q]);
+            incl = status_flag(w[q]) == kFlagInclusive;
+            used = q + 1;
+        }
+        if (incl) break;
+        if (used == 0) {
+            if (++spins > kSpinLimit) {
+                atomicOr(&ctl->error_flags, kErrTimeout);
+                break;
+            }
+            if (spins > 64) __nanosleep(32);
+        }
+        j -= used;
+    }
+    return excl;
+}
+
+template <bool PACKED>
+__global__ void __launch_bounds__(kSortThreads, PACKED ? 3 : 2)
 k_sort_pass(SortIO io, FrameCtl* ctl, unsigned long long* status, uint32_t pass, uint32_t epoch) {
-    if (!ctl->plan_ok || !ctl->pass_run[pass]) return;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    SortSmem& sm = *reinterpret_cast<SortSmem*>(smem_raw);
+    if (!ctl->plan_ok || !ctl->pass_run[pass] || (ctl->packed != 0) != PACKED) return;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    SortSmem<PACKED>& sm = *reinterpret_cast<SortSmem<PACKED>*>(smem_raw);
 
     const uint64_t K = ctl->num_keys;
     const uint32_t ntiles = (uint32_t)((K + kSortTile - 1) / kSortTile);
-    const uint32_t shift = 8 * pass;
+    const uint32_t shift = (PACKED ? ctl->idx_bits : 0u) + 8 * pass;
     const uint32_t mask = ctl->pass_mask[pass];
     const unsigned long long* __restrict__ src_k = io_keys(io, ctl->pass_src[pass]);
     const uint32_t* __restrict__ src_v = io_vals(io, ctl->pass_src[pass]);
@@ -59,81 +112,107 @@ k_sort_pass(SortIO io, FrameCtl* ctl, unsigned long long* status, uint32_t pass,
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t lt = lanemask_lt();
     const uint32_t bucket_base = ctl->base[pass][tid];
+    unsigned int* ticket = &ctl->pass_ticket[pass];
+    // tiles that can be bulk-copied: whole 4096-element tiles of 16-B aligned arrays
+    const bool aligned = ((reinterpret_cast<uintptr_t>(src_k) | (PACKED ? 0 : reinterpret_cast<uintptr_t>(src_v))) & 15u) == 0;
+    const uint32_t full_tiles = aligned ? (uint32_t)(K / kSortTile) : 0u;
+
+    if (tid == 0) {
+        mbar_init(&sm.bar[0], 1);
+        mbar_init(&sm.bar[1], 1);
+        fence_mbar_init();
+        const uint32_t t0 = atomicAdd(ticket, 1u);
+        sm.tile[0] = t0;
+        if (t0 < full_tiles) issue_tile<PACKED>(sm, 0, (uint64_t)t0 * kSortTile, src_k, src_v);
+    }
+    uint32_t phase = 0u;  // bit b: parity of buffer b's next mbarrier phase
+    int cur = 0;
+    bool failed = false;
 
     for (;;) {
-        if (tid == 0) sm.tile = atomicAdd(&ctl->pass_ticket[pass], 1u);
-#pragma unroll
-        for (int w = 0; w < kSortWarps; ++w) sm.whist[w][tid] = 0u;
-        __syncthreads();
-        const uint32_t tile = sm.tile;
-        if (tile >= ntiles) break;
-        const uint64_t tbase = (uint64_t)tile * kSortTile;
-
-        // ---- load and rank within the warp (positions warp*512 + j*32 + lane)
-        unsigned long long k[kSortItems];
-        uint32_t v[kSortItems];
-        uint32_t rank[kSortItems];
-        const uint64_t wbase = tbase + (uint64_t)warp * kWarpKeys + lane;
-#pragma unroll
-        for (int j = 0; j < kSortItems; ++j) {
-            const uint64_t idx = wbase + (uint64_t)j * 32;
-            const bool valid = idx < K;
-            k[j] = valid ? src_k[idx] : 0ull;
-            v[j] = valid ? src_v[idx] : 0u;
+        __syncthreads();  // previous tile fully written out; sm.tile[cur] visible
+        const uint32_t tile = sm.tile[cur];
+        if (tile >= ntiles || failed) {
+            // after a timed-out wait, let the prefetch already issued land before leaving
+            if (failed && tile < full_tiles) mbar_wait_bounded(&sm.bar[cur], (phase >> cur) & 1u, kBarSpinLimit);
+            break;
         }
+        const uint64_t tbase = (uint64_t)tile * kSortTile;
+#pragma unroll
+        for (int w = 0; w < kSortWarps; ++w) sm.whist[w][tid] = 0;
+        sm.tcount[tid] = 0u;
+        if (tid == 0) {
+            const uint32_t tn = atomicAdd(ticket, 1u);
+            sm.tile[cur ^ 1] = tn;
+            if (tn < full_tiles) issue_tile<PACKED>(sm, cur ^ 1, (uint64_t)tn * kSortTile, src_k, src_v);
+        }
+        bool timed_out = false;
+        if (tile < full_tiles) {
+            const uint32_t par = (phase >> cur) & 1u;
+            if (!mbar_wait_bounded(&sm.bar[cur], par, kBarSpinLimit)) {
+                timed_out = true;
+                if (!mbar_wait_bounded(&sm.bar[cur], par, kBarSpinLimit)) atomicOr(&ctl->error_flags, kErrTimeout);
+            }
+            phase ^= 1u << cur;
+        } else {  // the partial last tile, or unaligned arrays: plain loads
+            for (uint32_t i = tid; i < (uint32_t)min((uint64_t)kSortTile, K - tbase); i += kSortThreads) {
+                sm.keys[cur][i] = src_k[tbase + i];
+                if (!PACKED) sm.vals[cur][i] = src_v[tbase + i];
+            }
+        }
+        if (__syncthreads_or(timed_out)) {
+            if (tid == 0) atomicOr(&ctl->error_flags, kErrTimeout);
+            failed = true;
+        }
+
+        const uint32_t wpos = warp * kWarpKeys + lane;
+        const uint32_t rest = K > tbase + wpos ? (uint32_t)min((K - tbase - wpos + 31) / 32, (uint64_t)kSortItems) : 0u;
+        const uint32_t valid_items = rest;  // this thread's elements that exist
+        // ---- early counts: the tile's digit histogram, published before ranking so that later
+        //      tiles' look-backs find it (and soon this tile's inclusive prefix) sooner
+#pragma unroll
+        for (int j = 0; j < kSortItems; ++j)
+            if ((uint32_t)j < valid_items) atomicAdd(&sm.tcount[(uint32_t)(sm.keys[cur][wpos + j * 32] >> shift) & mask], 1u);
+        __syncthreads();
+        const uint32_t cnt = sm.tcount[tid];
+        unsigned long long* st = status + (uint64_t)tile * 256 + tid;
+        st_relaxed_u64(st, pack_status(epoch, tile == 0 ? kFlagInclusive : kFlagAggregate, cnt));
+
+        // ---- rank within the warp (positions warp*512 + j*32 + lane)
+        uint16_t rank[kSortItems];
 #pragma unroll
         for (int j = 0; j < kSortItems; ++j) {
-            const uint64_t idx = wbase + (uint64_t)j * 32;
-            const bool valid = idx < K;
-            const uint32_t d = valid ? (uint32_t)(k[j] >> shift) & mask : 256u + lane;
+            const bool valid = (uint32_t)j < valid_items;
+            const uint32_t d = valid ? (uint32_t)(sm.keys[cur][wpos + j * 32] >> shift) & mask : 256u + lane;
             const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
             const int leader = __ffs(peers) - 1;
             uint32_t b = 0;
             if (valid && lane == leader) {
                 b = sm.whist[warp][d];
-                sm.whist[warp][d] = b + __popc(peers);
+                sm.whist[warp][d] = (uint16_t)(b + __popc(peers));
             }
             b = __shfl_sync(0xFFFFFFFFu, b, leader);
-            rank[j] = b + __popc(peers & lt);
+            rank[j] = (uint16_t)(b + __popc(peers & lt));
             __syncwarp();
         }
         __syncthreads();
 
-        // ---- per digit (thread tid = digit): prefix over warps, tile count
-        uint32_t cnt = 0;
+        // ---- per digit (thread = digit): prefix over warps, then the look-back
+        {
+            uint32_t run = 0;
 #pragma unroll
-        for (int w = 0; w < kSortWarps; ++w) {
-            const uint32_t t = sm.whist[w][tid];
-            sm.whist[w][tid] = cnt;
-            cnt += t;
+            for (int w = 0; w < kSortWarps; ++w) {
+                const uint32_t t = sm.whist[w][tid];
+                sm.whist[w][tid] = (uint16_t)run;
+                run += t;
+            }
         }
-
-        // ---- decoupled look-back for this digit
-        unsigned long long* st = status + (uint64_t)tile * 256 + tid;
-        st_volatile_u64(st, pack_status(epoch, tile == 0 ? kFlagInclusive : kFlagAggregate, cnt));
         uint64_t excl = 0;
         if (tile > 0) {
-            int64_t j = (int64_t)tile - 1;
-            uint32_t spins = 0;
-            while (j >= 0) {
-                const uint64_t w = ld_volatile_u64(status + (uint64_t)j * 256 + tid);
-                if (status_epoch(w) != epoch || status_flag(w) == 0) {
-                    if (++spins > kSpinLimit) {
-                        atomicOr(&ctl->error_flags, kErrTimeout);
-                        break;
-                    }
-                    __nanosleep(32);
-                    continue;
-                }
-                excl += status_value(w);
-                if (status_flag(w) == kFlagInclusive) break;
-                --j;
-            }
-            st_volatile_u64(st, pack_status(epoch, kFlagInclusive, excl + cnt));
+            excl = lookback_digit(status, tile, tid, epoch, ctl);
+            st_relaxed_u64(st, pack_status(epoch, kFlagInclusive, excl + cnt));
         }
         sm.gbase[tid] = (unsigned long long)bucket_base + excl;
-
-        // ---- tile-local digit starts: exclusive scan of cnt over digits
         {
             uint32_t x = cnt;
 #pragma unroll
@@ -150,15 +229,23 @@ k_sort_pass(SortIO io, FrameCtl* ctl, unsigned long long* status, uint32_t pass,
         }
         __syncthreads();
 
-        // ---- stage in digit order
+        // ---- stage in digit order: read this thread's elements, then reuse the buffer
+        unsigned long long k[kSortItems];
+        uint32_t v[PACKED ? 1 : kSortItems];
 #pragma unroll
         for (int j = 0; j < kSortItems; ++j) {
-            const uint64_t idx = wbase + (uint64_t)j * 32;
-            if (idx < K) {
+            k[j] = sm.keys[cur][wpos + j * 32];
+            if (!PACKED) v[PACKED ? 0 : j] = sm.vals[cur][wpos + j * 32];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < kSortItems; ++j) {
+            const uint32_t p = wpos + j * 32;
+            if (tbase + p < K) {
                 const uint32_t d = (uint32_t)(k[j] >> shift) & mask;
                 const uint32_t pos = sm.lstart[d] + sm.whist[warp][d] + rank[j];
-                sm.keys[pos] = k[j];
-                sm.vals[pos] = v[j];
+                sm.keys[cur][pos] = k[j];
+                if (!PACKED) sm.vals[cur][pos] = v[PACKED ? 0 : j];
             }
         }
         __syncthreads();
@@ -166,18 +253,19 @@ k_sort_pass(SortIO io, FrameCtl* ctl, unsigned long long* status, uint32_t pass,
         // ---- coalesced write-out
         const uint32_t tn = (uint32_t)min((uint64_t)kSortTile, K - tbase);
         for (uint32_t i = tid; i < tn; i += kSortThreads) {
-            const unsigned long long key = sm.keys[i];
+            const unsigned long long key = sm.keys[cur][i];
             const uint32_t d = (uint32_t)(key >> shift) & mask;
             const uint64_t g = sm.gbase[d] + (i - sm.lstart[d]);
             dst_k[g] = key;
-            dst_v[g] = sm.vals[i];
+            if (!PACKED) dst_v[g] = sm.vals[cur][i];
         }
-        __syncthreads();
+        fence_proxy_async_smem();  // this buffer is the target of a later bulk copy
+        cur ^= 1;
     }
 }
 
-// Digit histograms of caller-supplied keys (standalone operator). Also records K and the
-// key width for the plan.
+// Digit histograms of caller-supplied keys (standalone operator). Also records K and the key
+// width for the plan.
 __global__ void __launch_bounds__(256) k_key_histogram(const unsigned long long* __restrict__ keys,
                                                        uint64_t n, uint32_t key_bits, FrameCtl* ctl) {
     __shared__ uint32_t s_hist[kMaxPasses][256];
@@ -204,6 +292,31 @@ __global__ void __launch_bounds__(256) k_key_histogram(const unsigned long long*
     }
 }
 
+template <bool PACKED>
+cudaError_t launch_pass(const SortIO& io, FrameCtl* ctl, unsigned long long* status, uint32_t pass,
+                        uint32_t epoch, uint64_t max_keys, cudaStream_t stream) {
+    static int per_sm[128] = {0};  // resident CTAs per SM, per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const size_t smem = sizeof(SortSmem<PACKED>);
+    if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+    if (per_sm[dev] == 0) {
+        cudaError_t e = cudaFuncSetAttribute(k_sort_pass<PACKED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+        int n = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_sort_pass<PACKED>, kSortThreads, smem);
+        if (e != cudaSuccess) return e;
+        per_sm[dev] = n > 0 ? n : 1;
+    }
+    const uint64_t tiles = (max_keys + kSortTile - 1) / kSortTile;
+    uint64_t grid = (uint64_t)device_sm_count() * per_sm[dev];  // persistent: all resident
+    if (tiles < grid) grid = tiles;
+    if (grid < 1) grid = 1;
+    k_sort_pass<PACKED><<<(unsigned)grid, kSortThreads, smem, stream>>>(io, ctl, status, pass, epoch);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 size_t sort_status_words(uint64_t max_keys) {
@@ -221,24 +334,10 @@ cudaError_t launch_key_histogram(const unsigned long long* keys, uint64_t n, uin
 }
 
 cudaError_t launch_sort_pass(const SortIO& io, FrameCtl* ctl, unsigned long long* status,
-                             uint32_t pass, uint32_t epoch, uint64_t max_keys,
+                             uint32_t pass, uint32_t epoch, uint64_t max_keys, bool packed,
                              cudaStream_t stream) {
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const size_t smem = sizeof(SortSmem);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(k_sort_pass, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-        attr_set[dev] = true;
-    }
-    const uint64_t tiles = (max_keys + kSortTile - 1) / kSortTile;
-    uint64_t grid = (uint64_t)device_sm_count() * 2;  // persistent: every CTA resident
-    if (tiles < grid) grid = tiles;
-    if (grid < 1) grid = 1;
-    k_sort_pass<<<(unsigned)grid, kSortThreads, smem, stream>>>(io, ctl, status, pass, epoch);
-    return cudaGetLastError();
+    return packed ? launch_pass<true>(io, ctl, status, pass, epoch, max_keys, stream)
+                  : launch_pass<false>(io, ctl, status, pass, epoch, max_keys, stream);
 }
 
 }  // namespace kt

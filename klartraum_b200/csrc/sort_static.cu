@@ -87,6 +87,6 @@ extern "C" kt_status kt_gs_radix_sort_pairs_static(const uint64_t* keys_in, cons
     io.vals[1] = alt_v;
     io.vals[2] = vals_out;
     for (uint32_t p = 0; p < max_passes; ++p)
-        if (launch_sort_pass(io, ctl, status, p, p + 1, n, s) != cudaSuccess) return KT_ERR_CUDA;
+        if (launch_sort_pass(io, ctl, status, p, p + 1, n, false, s) != cudaSuccess) return KT_ERR_CUDA;
     return KT_OK;
 }

@@ -52,7 +52,7 @@ def test_record_sizes_match_header():
     assert GAUSSIAN3D_DTYPE.itemsize == 236
     assert GAUSSIAN2D_DTYPE.itemsize == 48
     assert CAMERA_DTYPE.itemsize == 192
-    assert C.sizeof(N.Config) == 48 and C.sizeof(N.Stats) == 72
+    assert C.sizeof(N.Config) == 48 and C.sizeof(N.Stats) == 80
 
 
 def test_invalid_configs_are_rejected_before_touching_a_device():

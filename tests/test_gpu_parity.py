@@ -312,6 +312,7 @@ def test_counters_accumulate_frames_and_keys():
     st = r.stats()
     assert c["frames"] == 20 and c["keys"] == 20 * st["num_keys"]
     assert c["key_passes"] == 20 * st["num_keys"] * st["sort_passes"]
+    assert c["sort_bytes"] == c["key_passes"] * (16 if st["packed"] else 24)
     ms, frames = r.stage_times_total()
-    assert frames == 20 and ms["frame"] > 0 and ms["sort"] > 0
+    assert frames == 20 and ms["frame"] > 0 and ms["bin_sort"] > 0
     assert r.counters()["frames"] == 0
