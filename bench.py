@@ -9,7 +9,10 @@ scaling). Inputs are larger than L2: 240 MB of scene planes and ~390 MB of key b
 frame, so no L2 flush is needed between frames.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --mode bands [--workload large_6m]   # one 4K frame split over the GPUs
 
+``--mode bands`` splits every frame into bin-row bands, one per rank, balanced on per-row pair
+counts, and all-gathers the strips each step (strong scaling).
 ``--impl reference`` times the CPU restatement of the reference algorithm (the oracle, C +
 OpenMP on all host cores) on the same workload; under torchrun only rank 0 runs it.
 Prints one JSON line (rank 0).
@@ -46,6 +49,11 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=None, help="steps of the host-buffer pass (default: steps/4)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--small", action="store_true", help="tiny frame for profiler captures")
+    p.add_argument("--mode", choices=["views", "bands"], default="views",
+                   help="views: one view per GPU per step (default); bands: one frame split into bin-row bands "
+                        "over the GPUs, strips all-gathered every step")
+    p.add_argument("--workload", default=None, help="scene of scenes.WORKLOADS (default: single_1m for views, "
+                                                    "large_6m for bands)")
     return p.parse_args()
 
 
@@ -163,6 +171,55 @@ def run_reference(args, w, cfg_block):
 
 # ------------------------------------------------------------------- our arm
 
+def stage_report(w, cnt, st, stage_ms, timed_frames, nplanes):
+    """Per-stage time, algorithmic bytes and HBM fraction over a timed region, and the roofline
+    entry of the dominant HBM-bound stage."""
+    from klartraum_b200 import native as N
+
+    peak, peak_kind = load_peaks()
+    frames = max(timed_frames, 1)
+    K_avg = cnt["keys"] / max(cnt["frames"], 1)
+    passes_avg = cnt["key_passes"] / max(cnt["keys"], 1)
+    nf = max(cnt["frames"], 1)
+    tiles = st["tiles_x"] * st["tiles_y"]
+    table = st["place_chunks"] * tiles * 4  # pairs per (chunk, bin), u32
+    per_frame_bytes = {
+        # scene planes read; record 48 + count 4 + rect 8 + depth 4 written
+        "project_count": w.n * (16 * (3 + nplanes) + 64),
+        # depth keys (counts + depths read, 8-B keys written) and the depth sort passes (16 B per
+        # Gaussian per pass)
+        "depth_sort": w.n * (4 + 4 + 8) + cnt["depth_sort_bytes"] / nf,
+        # depth order, count and bin rectangle read per Gaussian; the (chunk, bin) table written
+        "pair_count": w.n * (8 + 4 + 8) + table,
+        # the table read, rewritten as its prefix over chunks; bin ranges written
+        "bin_ranges": 2 * table + tiles * 8,
+        # depth order, count and rectangle per Gaussian, the table and bin starts read; 8 B per
+        # pair written once, at its place in bin order
+        "pair_place": w.n * (8 + 4 + 8) + table + tiles * 8 + cnt["sort_bytes"] / nf,
+    }
+    stages = {}
+    for name in N.STAGE_NAMES[:-1]:
+        avg = stage_ms[name] / frames
+        d = {"ms": avg, "share": stage_ms[name] / max(stage_ms["frame"], 1e-12)}
+        if name in per_frame_bytes:
+            gbs = per_frame_bytes[name] / (avg / 1000.0) / 1e9 if avg > 0 else 0.0
+            d.update({"bytes": per_frame_bytes[name], "gbs": gbs, "frac": gbs / peak})
+        stages[name] = d
+    dominant = max(stages, key=lambda k: stages[k]["ms"])
+    dom = stages[dominant]
+    if "bytes" in dom:
+        roofline = {"kernel": dominant, "bound": "hbm", "achieved": dom["gbs"], "peak": peak, "unit": "GB/s",
+                    "frac": dom["frac"], "traffic": None, "peak_source": peak_kind,
+                    "bytes_per_launch": dom["bytes"]}
+    else:
+        hb = max((k for k in stages if "bytes" in stages[k]), key=lambda k: stages[k]["ms"])
+        roofline = {"kernel": hb, "bound": "hbm", "achieved": stages[hb]["gbs"], "peak": peak, "unit": "GB/s",
+                    "frac": stages[hb]["frac"], "traffic": None, "peak_source": peak_kind,
+                    "bytes_per_launch": stages[hb]["bytes"],
+                    "note": f"{dominant} (issue bound, not HBM) takes the most time; this is the top HBM-bound stage"}
+    return stages, roofline, K_avg, passes_avg
+
+
 def load_peaks() -> tuple[float, str]:
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -185,14 +242,23 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     if args.small:
         w = type(w)(**{**w.__dict__, "n": 20000, "width": 640, "height": 360})
-    g3d = make_scene(w)
     cams = orbit_views(N_VIEWS, w.distance, w.width, w.height, fovy_deg=w.fovy_deg)
 
     def view_of(s):
         return (s * world + rank) % N_VIEWS
 
     r = Renderer(w.width, w.height, bin_size=16, sh_degree=w.sh_degree, device=local_rank, flags=N.FLAG_TIMING)
-    r.set_gaussians(g3d)
+    if world > 1:
+        # the scene is made once (rank 0) and broadcast over NCCL; records land in device memory
+        from klartraum_b200.multigpu import broadcast_scene
+
+        scene_dev, n_rec = broadcast_scene(make_scene(w) if rank == 0 else None, dist, rank, dev)
+        torch.cuda.synchronize()
+        r.set_gaussians_device(scene_dev.data_ptr(), n_rec)
+        torch.cuda.synchronize()
+        del scene_dev
+    else:
+        r.set_gaussians(make_scene(w))
     nplanes = (3 * (w.sh_degree + 1) ** 2 + 3) // 4
     bg = torch.zeros((w.height, w.width, 4), dtype=torch.uint8, device=dev)
     bg[..., 3] = 255
@@ -242,43 +308,7 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     fps = world * args.steps / (ms_max / 1000.0)
 
     # ---- per-stage bandwidth over the timed region
-    peak, peak_kind = load_peaks()
-    frames = max(timed_frames, 1)
-    K_avg = cnt["keys"] / max(cnt["frames"], 1)
-    passes_avg = cnt["key_passes"] / max(cnt["keys"], 1)
-    nf = max(cnt["frames"], 1)
-    per_frame_bytes = {
-        # scene planes read; record 48 + count 4 + rect 8 + depth 4 written
-        "project_count": w.n * (16 * (3 + nplanes) + 64),
-        # depth keys (counts + depths read, 8-B keys written) and the depth sort passes (16 B per
-        # Gaussian per pass)
-        "depth_sort": w.n * (4 + 4 + 8) + cnt["depth_sort_bytes"] / nf,
-        # scan/emit: order, counts and rects gathered per Gaussian; 8 B written per pair
-        "emit": w.n * (8 + 4 + 8) + K_avg * 8,
-        # per executed pass of the pair sort: 8-B element read and written
-        "bin_sort": cnt["sort_bytes"] / nf,
-        "ranges": K_avg * 8 + st["tiles_x"] * st["tiles_y"] * 8,
-    }
-    stages = {}
-    for name in N.STAGE_NAMES[:-1]:
-        avg = stage_ms[name] / frames
-        d = {"ms": avg, "share": stage_ms[name] / max(stage_ms["frame"], 1e-12)}
-        if name in per_frame_bytes:
-            gbs = per_frame_bytes[name] / (avg / 1000.0) / 1e9 if avg > 0 else 0.0
-            d.update({"bytes": per_frame_bytes[name], "gbs": gbs, "frac": gbs / peak})
-        stages[name] = d
-    dominant = max(stages, key=lambda k: stages[k]["ms"])
-    dom = stages[dominant]
-    if "bytes" in dom:
-        roofline = {"kernel": dominant, "bound": "hbm", "achieved": dom["gbs"], "peak": peak, "unit": "GB/s",
-                    "frac": dom["frac"], "traffic": None, "peak_source": peak_kind,
-                    "bytes_per_launch": dom["bytes"]}
-    else:
-        hb = max((k for k in stages if "bytes" in stages[k]), key=lambda k: stages[k]["ms"])
-        roofline = {"kernel": hb, "bound": "hbm", "achieved": stages[hb]["gbs"], "peak": peak, "unit": "GB/s",
-                    "frac": stages[hb]["frac"], "traffic": None, "peak_source": peak_kind,
-                    "bytes_per_launch": stages[hb]["bytes"],
-                    "note": f"{dominant} (issue bound, not HBM) takes the most time; this is the top HBM-bound stage"}
+    stages, roofline, K_avg, passes_avg = stage_report(w, cnt, st, stage_ms, timed_frames, nplanes)
 
     # ---- end to end through the public API with host buffers
     r.set_flags(0)
@@ -309,7 +339,7 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg_block,
         "gaussians_per_s": fps * w.n, "keys_per_frame": K_avg, "sort_passes_per_frame": passes_avg,
-        "sort_layout": "Gaussians by depth, then (bin | index) pairs by bin; packed u64 elements",
+        "sort_layout": "Gaussians radix-sorted by depth; (bin | index) pairs placed in bin order by a counting sort over (chunk of depth order, bin); packed u64 elements",
         "stages": stages, "roofline": roofline,
         "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": img_bytes + 192,
                 "d2h_bytes_per_step": img_bytes + st["status_bytes"], "steps": e2e_steps,
@@ -319,6 +349,158 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     }
     if world == 1 and rank == 0 and not args.no_cpu_baseline and not args.small:
         line["cpu_baseline"] = cpu_baseline(w, cams)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    r.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_bands(args, w, rank, world, local_rank):
+    """One frame split into bin-row bands over the ranks (strong scaling). Every rank projects
+    the whole scene but bins, sorts and draws only its band; the strips are all-gathered over
+    NCCL every step, so every rank ends the step holding the full frame. Bands are balanced once
+    on the per-row pair counts of view 0 (each rank's rows summed with one all_reduce)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from klartraum_b200 import Renderer, make_scene, native as N, orbit_views
+    from klartraum_b200.multigpu import StripGather, band_pixel_rows, band_rows, broadcast_scene, row_pair_counts
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if args.small:
+        w = type(w)(**{**w.__dict__, "n": 20000, "width": 640, "height": 360})
+    cams = orbit_views(N_VIEWS, w.distance, w.width, w.height, fovy_deg=w.fovy_deg)
+    tx, ty = (w.width + 15) // 16, (w.height + 15) // 16
+    if world > 1:
+        scene_dev, n_rec = broadcast_scene(make_scene(w) if rank == 0 else None, dist, rank, dev)
+        torch.cuda.synchronize()
+        scene_host = None
+    else:
+        scene_dev, scene_host = None, make_scene(w)
+
+    def renderer(band):
+        r = Renderer(w.width, w.height, bin_size=16, sh_degree=w.sh_degree, device=local_rank,
+                     flags=N.FLAG_TIMING, tile_rows=band)
+        if scene_dev is not None:
+            r.set_gaussians_device(scene_dev.data_ptr(), n_rec)
+            torch.cuda.synchronize()
+        else:
+            r.set_gaussians(scene_host)
+        return r
+
+    bg = torch.zeros((w.height, w.width, 4), dtype=torch.uint8, device=dev)
+    bg[..., 3] = 255
+    img = bg.clone()
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+
+    # balance: equal bands render view 0, their per-row pair counts are summed over the ranks
+    bands = band_rows(ty, world)
+    r = renderer(bands[rank])
+    r.render(cams[0], img, stream=sptr)
+    torch.cuda.synchronize()
+    rows = torch.from_numpy(row_pair_counts(r.dump(N.STAGE_TILE_RANGES), tx, ty)).to(dev)
+    r.close()
+    if world > 1:
+        dist.all_reduce(rows)
+    bands = band_rows(ty, world, rows.cpu().numpy())
+    r = renderer(bands[rank])
+    del scene_dev
+    px = [band_pixel_rows(b, 16, w.height) for b in bands]
+    gather = StripGather(px, w.width, w.height, dist, rank, dev) if world > 1 else (lambda x: x)
+
+    def frame(s):
+        img.copy_(bg)
+        r.render(cams[s % N_VIEWS], img, stream=sptr)
+        return gather(img)
+
+    for s in range(max(args.warmup, 3)):
+        frame(s)
+    for v in sorted({s % N_VIEWS for s in range(args.steps)}):
+        r.render(cams[v], img, stream=sptr)  # checked frames size the key buffers for every view
+    torch.cuda.synchronize()
+    r.stage_times_total()
+    r.counters()
+
+    r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC)
+    clock = ClockSampler(local_rank)
+    clock.start()
+    time.sleep(0.5)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize()
+    t_wall0 = time.time()
+    ev0.record(stream)
+    for s in range(args.steps):
+        frame(s)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    r.sync()
+    clocks = clock.summary(t_wall0, t_wall1)
+    t = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    fps = args.steps / (ms_max / 1000.0)
+    stage_ms, timed_frames = r.stage_times_total()
+    cnt = r.counters()
+    st = r.stats()
+    nplanes = (3 * (w.sh_degree + 1) ** 2 + 3) // 4
+    stages, roofline, K_avg, passes_avg = stage_report(w, cnt, st, stage_ms, timed_frames, nplanes)
+
+    # end to end: camera from host through the API, band render, strip gather, frame to host
+    r.set_flags(0)
+    e2e_steps = args.e2e_steps or max(10, args.steps // 4)
+    host = torch.empty((w.height, w.width, 4), dtype=torch.uint8, pin_memory=True)
+    for s in range(3):
+        host.copy_(frame(s), non_blocking=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(e2e_steps):
+        out = frame(s)
+        if rank == 0:
+            host.copy_(out, non_blocking=True)
+        stream.synchronize()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_fps = e2e_steps / (float(te.item()) / 1000.0)
+    clock.stop()
+    img_bytes = w.width * w.height * 4
+    line = {
+        "metric": f"frames/s, {w.n:,}-splat SH{w.sh_degree} {w.width}x{w.height} split into bin-row bands",
+        "value": fps, "unit": "frames/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{w.name}: {w.n:,} Gaussians SH{w.sh_degree} {w.width}x{w.height}, 16x16-px bins, "
+                               f"{N_VIEWS}-view orbit, one frame per step split into {world} bin-row bands",
+                   "bands": bands, "parallelism": f"bands{world}: projection replicated, binning/sort/splat per band, "
+                                                  "strips all-gathered (NCCL) every step",
+                   "l2": "inputs larger than L2; no flush", "seed": w.seed},
+        "keys_per_frame_this_rank": K_avg, "sort_passes_per_frame": passes_avg, "stages_rank0": stages,
+        "roofline": roofline,
+        "gather_bytes_per_step": gather.bytes_per_frame if world > 1 else 0,
+        "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": 192 * world,
+                "d2h_bytes_per_step": img_bytes, "steps": e2e_steps,
+                "api": "kt_gs_render (camera from host) + strip all_gather + frame copied to pinned host on rank 0"},
+        "gpu_launches": st["launches"] * args.steps * world, "gpu_launches_per_step": st["launches"] * world,
+        "clocks": clocks,
+    }
     if rank == 0:
         print(json.dumps(line), flush=True)
     r.close()
@@ -353,7 +535,7 @@ def main():
     args = parse()
     from klartraum_b200.scenes import WORKLOADS
 
-    w = WORKLOADS[WORKLOAD]
+    w = WORKLOADS[args.workload or (WORKLOAD if args.mode == "views" else "large_6m")]
     cfg_block = workload_config(w)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -362,7 +544,10 @@ def main():
         if rank == 0:
             run_reference(args, w, cfg_block)
         return
-    run_ours(args, w, cfg_block, rank, world, local_rank)
+    if args.mode == "bands":
+        run_bands(args, w, rank, world, local_rank)
+    else:
+        run_ours(args, w, cfg_block, rank, world, local_rank)
 
 
 if __name__ == "__main__":

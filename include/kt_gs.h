@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define KT_GS_ABI_VERSION 1
+#define KT_GS_ABI_VERSION 2
 
 typedef enum kt_status {
     KT_OK = 0,
@@ -124,14 +124,16 @@ typedef struct kt_gs_stats {
     uint32_t tiles_y;
     uint32_t key_bits;       /* significant bits of the compact sort key (bin bits + depth bits) */
     uint32_t depth_bits;     /* bits of the depth field after subtracting the frame's minimum */
-    uint32_t sort_passes;    /* 8-bit LSD passes that moved data (the rest were skipped) */
+    uint32_t sort_passes;    /* passes over the pairs: 0, they are placed in bin order directly */
     uint32_t error_flags;    /* device error bits: 1 = capacity, 2 = look-back timeout */
     uint32_t depth_min_bits; /* smallest (floatBitsToUint(z) ^ 0x80000000) over binned Gaussians */
     uint32_t depth_max_bits;
     uint32_t status_bytes;   /* bytes of frame status copied device->host after every frame */
     uint32_t launches;       /* kernels launched per frame */
-    uint32_t packed;         /* 1: the sort moved (key << idx_bits | index) words, 0: keys + values */
+    uint32_t packed;         /* 1: pairs are (bin << idx_bits | index) words */
     uint32_t idx_bits;       /* index bits of a packed element */
+    uint32_t place_chunks;   /* chunks of depth order the pair placement split the Gaussians into */
+    uint32_t place_bands;    /* bands of bin rows of the pair placement */
 } kt_gs_stats;
 
 /* Totals accumulated on the device over every frame rendered on a path since the last
@@ -139,9 +141,9 @@ typedef struct kt_gs_stats {
 typedef struct kt_gs_counters {
     uint64_t frames;      /* frames whose sort plan ran */
     uint64_t keys;        /* sum of K */
-    uint64_t key_passes;  /* sum of K * (executed sort passes) */
+    uint64_t key_passes;  /* sum of K * (passes over the pairs; 0 with direct placement) */
     uint64_t visible;     /* sum of Gaussians with a non-zero tile count */
-    uint64_t sort_bytes;  /* sum of bytes the executed passes of the pair sort read and wrote */
+    uint64_t sort_bytes;  /* sum of bytes of pairs written in bin order (8 per pair) */
     uint64_t depth_sort_bytes; /* same for the depth sort of the Gaussians */
 } kt_gs_counters;
 
@@ -165,8 +167,9 @@ typedef enum kt_gs_stage {
 
 /* Stage timers (KT_GS_FLAG_TIMING), in the order the stages run. */
 #define KT_GS_NSTAGES 7
-/* 0 projection+count, 1 depth keys + depth sort of the Gaussians, 2 scan/emit of the (bin,
- * Gaussian) pairs, 3 sort of the pairs by bin, 4 bin ranges, 5 rasterise, 6 whole frame */
+/* 0 projection+count, 1 pairs per bin -> bin ranges and pair-sort histograms, 2 depth keys +
+ * depth sort of the Gaussians, 3 scan/emit of the (bin, Gaussian) pairs, 4 sort of the pairs by
+ * bin (+ frame counters), 5 rasterise, 6 whole frame */
 
 typedef struct kt_gs_ctx kt_gs_ctx;
 

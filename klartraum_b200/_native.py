@@ -36,7 +36,7 @@ STAGE_KEYS_SORTED = 5
 STAGE_VALUES_SORTED = 6
 STAGE_TILE_RANGES = 7
 NSTAGES = 7
-STAGE_NAMES = ["project_count", "depth_sort", "emit", "bin_sort", "ranges", "rasterize", "frame"]
+STAGE_NAMES = ["project_count", "depth_sort", "pair_count", "bin_ranges", "pair_place", "rasterize", "frame"]
 
 # every entry point include/kt_gs.h declares
 EXPORTED_SYMBOLS = [
@@ -78,6 +78,7 @@ class Stats(C.Structure):
         ("depth_min_bits", C.c_uint32), ("depth_max_bits", C.c_uint32),
         ("status_bytes", C.c_uint32), ("launches", C.c_uint32),
         ("packed", C.c_uint32), ("idx_bits", C.c_uint32),
+        ("place_chunks", C.c_uint32), ("place_bands", C.c_uint32),
     ]
 
     def as_dict(self) -> dict:
@@ -93,7 +94,7 @@ class Counters(C.Structure):
 
 
 assert C.sizeof(Config) == 48
-assert C.sizeof(Stats) == 80
+assert C.sizeof(Stats) == 88
 assert C.sizeof(Counters) == 48
 
 _lib = None

@@ -31,6 +31,7 @@ COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler",
 SOURCES = {
     "project.cu": ["-fmad=false", "-prec-div=true", "-prec-sqrt=true", "-ftz=false"],
     "binning.cu": [],
+    "place.cu": [],
     "sort.cu": [],
     "raster.cu": [],
     "sort_static.cu": [],

@@ -5,10 +5,10 @@
 // sub-graph with Vulkan buffers, this context owns the device buffers of each path (frame in
 // flight) and enqueues the kernels of one frame on a CUDA stream:
 //   init -> K1 project+count -> depth keys -> plan -> depth sort passes (Gaussians)
-//   -> K2/3 scan+emit in depth order -> plan -> bin sort passes (pairs) -> K6;
-//   bin ranges (K5) come from per-bin pair counts right after K1.
-// No host synchronisation happens inside a frame: the key count, the sort plan and the pass
-// skipping live in device memory. After the frame a 2.6 KB control block is copied back;
+//   -> pair counts per (chunk of depth order, bin) -> prefix over chunks, bin ranges (K5)
+//   -> pair placement by bin (K2-K4 without a pair sort) -> totals -> K6.
+// No host synchronisation happens inside a frame: the key count, the capacity check and the
+// depth-sort plan live in device memory. After the frame a 2.6 KB control block is copied back;
 // unless KT_GS_FLAG_ASYNC is set the call waits for it and, if the keys did not fit, grows
 // the key buffers and renders again (nothing was drawn in that case).
 #include <cuda_runtime.h>
@@ -55,18 +55,19 @@ struct PathWs {
     float4* rec = nullptr;
     uint32_t* counts = nullptr;
     uint2* rect = nullptr;
+    uint2* srect = nullptr;  // rect in depth order
     uint32_t* depth = nullptr;
     unsigned long long* gsort[2] = {nullptr, nullptr};  // Gaussians by depth
-    unsigned long long* scan_status = nullptr;
-    unsigned long long* keys[2] = {nullptr, nullptr};   // (bin, Gaussian) pairs
+    uint32_t* pairs = nullptr;  // Gaussian of every (bin, Gaussian) pair, in bin order
     unsigned long long* sort_status = nullptr;
+    uint32_t* sort_table = nullptr;  // per-range digit table of reduce-then-scan passes
     uint64_t status_words = 0;
-    int* bin_diff = nullptr;  // (tiles_y + 1) x (tiles_x + 1) difference table, zero between frames
+    uint32_t* pair_table = nullptr;  // pairs per (chunk, bin), then their prefix over chunks
+    uint64_t pair_table_words = 0;
     uint2* ranges = nullptr;
     FrameCtl* ctl = nullptr;
     FrameCtl* ctl_depth = nullptr;
     FrameCtl* host_ctl = nullptr;  // pinned copy of the last frame's control block
-    uint32_t scan_epoch = 0;
     uint32_t sort_epoch = 0;
     cudaEvent_t done_ev = nullptr;
     // stage timers: a ring of event sets, one set per timed frame, drained into sums
@@ -109,7 +110,6 @@ struct kt_gs_ctx {
     uint64_t n = 0;
     bool has_scene = false;
     GridParams gp{};
-    uint32_t max_passes = 0;
     std::vector<PathWs> paths;
 };
 
@@ -172,9 +172,10 @@ GridParams make_grid(const kt_gs_config& c) {
 uint32_t ntiles(const kt_gs_ctx* c) { return c->gp.tiles_x * c->gp.tiles_y; }
 
 void free_path(PathWs& w) {
-    dfree(w.rec); dfree(w.counts); dfree(w.rect); dfree(w.depth); dfree(w.gsort[0]); dfree(w.gsort[1]);
-    dfree(w.scan_status); dfree(w.keys[0]); dfree(w.keys[1]);
-    dfree(w.sort_status); dfree(w.ranges); dfree(w.ctl); dfree(w.ctl_depth); dfree(w.bin_diff);
+    dfree(w.rec); dfree(w.counts); dfree(w.rect); dfree(w.srect); dfree(w.depth); dfree(w.gsort[0]);
+    dfree(w.gsort[1]);
+    dfree(w.pairs); dfree(w.pair_table);
+    dfree(w.sort_status); dfree(w.sort_table); dfree(w.ranges); dfree(w.ctl); dfree(w.ctl_depth);
     dfree(w.img); dfree(w.g2d);
     if (w.host_ctl) cudaFreeHost(w.host_ctl);
     w.host_ctl = nullptr;
@@ -186,7 +187,7 @@ void free_path(PathWs& w) {
             e = nullptr;
         }
     dfree(w.totals);
-    w.n_alloc = w.cap = 0;
+    w.n_alloc = w.cap = w.pair_table_words = 0;
 }
 
 kt_status ensure_path_base(kt_gs_ctx* c, PathWs& w) {
@@ -198,9 +199,6 @@ kt_status ensure_path_base(kt_gs_ctx* c, PathWs& w) {
         KT_TRY_CUDA(c, cudaMallocHost(&w.host_ctl, sizeof(FrameCtl)));
         std::memset(w.host_ctl, 0, sizeof(FrameCtl));
         KT_TRY_CUDA(c, cudaMalloc(&w.ranges, sizeof(uint2) * std::max(1u, ntiles(c))));
-        const size_t cells = (size_t)(c->gp.tiles_x + 1) * (c->gp.tiles_y + 1);
-        KT_TRY_CUDA(c, cudaMalloc(&w.bin_diff, sizeof(int) * cells));
-        KT_TRY_CUDA(c, cudaMemset(w.bin_diff, 0, sizeof(int) * cells));
         KT_TRY_CUDA(c, cudaEventCreateWithFlags(&w.done_ev, cudaEventDisableTiming));
         for (auto& set : w.ring)
             for (auto& e : set) KT_TRY_CUDA(c, cudaEventCreate(&e));
@@ -210,12 +208,16 @@ kt_status ensure_path_base(kt_gs_ctx* c, PathWs& w) {
     return KT_OK;
 }
 
-// Look-back status words shared by the depth sort (n elements) and the pair sort (cap).
+// Look-back status words of the depth sort (n elements), and its reduce-then-scan table when it
+// spans more than one wave of CTAs.
 kt_status ensure_status(kt_gs_ctx* c, PathWs& w) {
-    const uint64_t need = sort_status_words(std::max<uint64_t>(w.cap, w.n_alloc));
+    const uint64_t need = sort_status_words(w.n_alloc);
     if (need <= w.status_words) return KT_OK;
     dfree(w.sort_status);
+    dfree(w.sort_table);
     w.status_words = 0;
+    const size_t table = sort_table_words(w.n_alloc);
+    KT_TRY_CUDA(c, cudaMalloc(&w.sort_table, sizeof(uint32_t) * table));
     KT_TRY_CUDA(c, cudaMalloc(&w.sort_status, sizeof(unsigned long long) * need));
     KT_TRY_CUDA(c, cudaMemset(w.sort_status, 0, sizeof(unsigned long long) * need));
     w.sort_epoch = 0;
@@ -225,20 +227,17 @@ kt_status ensure_status(kt_gs_ctx* c, PathWs& w) {
 
 kt_status ensure_n(kt_gs_ctx* c, PathWs& w, uint64_t n) {
     if (n <= w.n_alloc) return KT_OK;
-    dfree(w.rec); dfree(w.counts); dfree(w.rect); dfree(w.depth); dfree(w.gsort[0]); dfree(w.gsort[1]);
-    dfree(w.scan_status);
+    dfree(w.rec); dfree(w.counts); dfree(w.rect); dfree(w.srect); dfree(w.depth); dfree(w.gsort[0]);
+    dfree(w.gsort[1]);
     w.n_alloc = 0;
     const uint64_t m = std::max<uint64_t>(n, 1);
     KT_TRY_CUDA(c, cudaMalloc(&w.rec, sizeof(float4) * 3 * m));
     KT_TRY_CUDA(c, cudaMalloc(&w.counts, sizeof(uint32_t) * m));
     KT_TRY_CUDA(c, cudaMalloc(&w.rect, sizeof(uint2) * m));
+    KT_TRY_CUDA(c, cudaMalloc(&w.srect, sizeof(uint2) * m));
     KT_TRY_CUDA(c, cudaMalloc(&w.depth, sizeof(uint32_t) * m));
     KT_TRY_CUDA(c, cudaMalloc(&w.gsort[0], sizeof(unsigned long long) * m));
     KT_TRY_CUDA(c, cudaMalloc(&w.gsort[1], sizeof(unsigned long long) * m));
-    const uint64_t chunks = (m + kScanChunk - 1) / kScanChunk;
-    KT_TRY_CUDA(c, cudaMalloc(&w.scan_status, sizeof(unsigned long long) * chunks));
-    KT_TRY_CUDA(c, cudaMemset(w.scan_status, 0, sizeof(unsigned long long) * chunks));
-    w.scan_epoch = 0;
     w.n_alloc = m;
     return ensure_status(c, w);
 }
@@ -249,11 +248,11 @@ kt_status ensure_cap(kt_gs_ctx* c, PathWs& w, uint64_t cap) {
         return fail(c, KT_ERR_CAPACITY, "key count " + std::to_string(cap) +
                                             " exceeds the 32-bit index range of the key buffers");
     cap = std::min<uint64_t>(((cap + kSortTile - 1) / kSortTile) * kSortTile, kMaxKeyCapacity);
-    dfree(w.keys[0]); dfree(w.keys[1]);
+    dfree(w.pairs);
     w.cap = 0;
-    for (int b = 0; b < 2; ++b) KT_TRY_CUDA(c, cudaMalloc(&w.keys[b], sizeof(unsigned long long) * cap));
+    KT_TRY_CUDA(c, cudaMalloc(&w.pairs, sizeof(uint32_t) * cap));
     w.cap = cap;
-    return ensure_status(c, w);
+    return KT_OK;
 }
 
 FrameBufs frame_bufs(const PathWs& w) {
@@ -261,13 +260,12 @@ FrameBufs frame_bufs(const PathWs& w) {
     fb.rec = w.rec;
     fb.counts = w.counts;
     fb.rect = w.rect;
+    fb.srect = w.srect;
     fb.depth = w.depth;
     fb.gsort[0] = w.gsort[0];
     fb.gsort[1] = w.gsort[1];
-    fb.keys[0] = w.keys[0];
-    fb.keys[1] = w.keys[1];
+    fb.pairs = w.pairs;
     fb.ranges = w.ranges;
-    fb.scan_status = w.scan_status;
     fb.sort_status = w.sort_status;
     fb.ctl = w.ctl;
     fb.ctl_depth = w.ctl_depth;
@@ -316,25 +314,26 @@ kt_status enqueue_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* ca
         w.ring_last = slot;
         w.ring_next = (slot + 1) % PathWs::kRing;
     }
-    // look-back epochs; a wrap clears the status words
-    if (++w.scan_epoch > kEpochMax) {
-        KT_TRY_CUDA(c, cudaMemsetAsync(w.scan_status, 0,
-                                       sizeof(unsigned long long) * ((w.n_alloc + kScanChunk - 1) / kScanChunk),
-                                       stream));
-        w.scan_epoch = 1;
+    // work split of the pair placement, and its table
+    PlaceGeom pg{};
+    KT_TRY_CUDA(c, place_geometry(c->gp, n, &pg));
+    if (pg.table_words > w.pair_table_words) {
+        dfree(w.pair_table);
+        w.pair_table_words = 0;
+        KT_TRY_CUDA(c, cudaMalloc(&w.pair_table, sizeof(uint32_t) * pg.table_words));
+        w.pair_table_words = pg.table_words;
     }
-    const uint32_t epochs = kDepthPasses + c->max_passes;
-    if (w.sort_epoch + epochs + 1 > kEpochMax) {
+    // look-back epochs of the depth sort; a wrap clears the status words
+    if (w.sort_epoch + kDepthPasses + 1 > kEpochMax) {
         KT_TRY_CUDA(c, cudaMemsetAsync(w.sort_status, 0, sizeof(unsigned long long) * w.status_words, stream));
         w.sort_epoch = 0;
     }
     const uint32_t sort_epoch0 = w.sort_epoch + 1;
-    w.sort_epoch += epochs;
+    w.sort_epoch += kDepthPasses;
 
     FrameBufs fb = frame_bufs(w);
-    SortIO io{};  // pairs by bin
-    io.keys[0] = w.keys[0];
-    io.keys[1] = w.keys[1];
+    SortIO io{};  // pairs by bin, as the rasteriser reads them: Gaussian indices
+    io.vals[0] = w.pairs;
     SortIO io_depth{};  // Gaussians by depth
     io_depth.keys[0] = w.gsort[0];
     io_depth.keys[1] = w.gsort[1];
@@ -348,22 +347,20 @@ kt_status enqueue_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* ca
         KT_TRY_CUDA(c, launch_load_projected(w.g2d, n, c->gp, fb, stream));
     }
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[1], stream));
-    // pairs per bin -> bin ranges and the bin sort's histograms (independent of depth order)
-    KT_TRY_CUDA(c, launch_bin_counts(fb, c->gp, n, w.bin_diff, c->max_passes, stream));
-    // Gaussians by depth (stable: ties keep index order), then the pairs emitted in that order
+    // Gaussians by depth (stable: ties keep index order)
     KT_TRY_CUDA(c, launch_depth_keys(fb, n, stream));
     KT_TRY_CUDA(c, launch_plan(w.ctl_depth, n, kDepthPasses, 0, stream));
     for (uint32_t p = 0; p < kDepthPasses; ++p)
-        KT_TRY_CUDA(c, launch_sort_pass(io_depth, w.ctl_depth, w.sort_status, p, sort_epoch0 + p, n, true, stream));
-    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[2], stream));
-    KT_TRY_CUDA(c, launch_scan_emit(fb, c->gp, n, w.scan_epoch, c->max_passes, stream));
-    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[3], stream));
-    // pairs by bin (stable: depth order within a bin survives)
-    KT_TRY_CUDA(c, launch_plan(w.ctl, w.cap, c->max_passes, 0, stream));
-    for (uint32_t p = 0; p < c->max_passes; ++p)
-        KT_TRY_CUDA(c, launch_sort_pass(io, w.ctl, w.sort_status, p, sort_epoch0 + kDepthPasses + p, w.cap,
+        KT_TRY_CUDA(c, launch_sort_pass(io_depth, w.ctl_depth, w.sort_status, w.sort_table, p, sort_epoch0 + p, n,
                                         true, stream));
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[2], stream));
+    // pairs per (chunk of depth order, bin); their prefix over chunks and the bin ranges
+    KT_TRY_CUDA(c, launch_pair_count(fb, c->gp, pg, n, w.pair_table, stream));
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[3], stream));
+    KT_TRY_CUDA(c, launch_pair_ranges(fb, c->gp, pg, n, w.pair_table, stream));
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[4], stream));
+    // every pair at its place in bin order (depth order within a bin)
+    KT_TRY_CUDA(c, launch_pair_place(fb, c->gp, pg, n, w.pair_table, stream));
     KT_TRY_CUDA(c, launch_frame_totals(w.ctl, w.ctl_depth, w.totals, stream));
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[5], stream));
     KT_TRY_CUDA(c, launch_rasterize(w.rec, io, w.ranges, w.ctl, c->gp, img,
@@ -381,7 +378,7 @@ kt_status check_frame(kt_gs_ctx* c, PathWs& w) {
     if (!w.have_frame) return KT_OK;
     KT_TRY_CUDA(c, cudaEventSynchronize(w.done_ev));
     const uint32_t e = w.host_ctl->error_flags;
-    if (e & kErrTimeout) return fail(c, KT_ERR_TIMEOUT, "a decoupled look-back wait timed out");
+    if (e & kErrTimeout) return fail(c, KT_ERR_TIMEOUT, "a bounded device wait of the depth sort timed out");
     if (e & kErrCapacity)
         return fail(c, KT_ERR_CAPACITY, "frame needs " + std::to_string(w.host_ctl->num_keys) +
                                             " keys, capacity is " + std::to_string(w.cap));
@@ -526,7 +523,6 @@ kt_status kt_gs_create(const kt_gs_config* cfg, int device, kt_gs_ctx** out) {
     c->cfg = *cfg;
     c->device = device;
     c->gp = make_grid(*cfg);
-    c->max_passes = std::max<uint32_t>(1, (c->gp.tile_bits + 7) / 8);  // passes over the bin bits
     c->paths.resize(cfg->num_paths);
     *out = c;
     return KT_OK;
@@ -667,9 +663,17 @@ kt_status kt_gs_frame_stats(kt_gs_ctx* c, uint32_t path, kt_gs_stats* out) {
     out->depth_min_bits = h.depth_min;
     out->depth_max_bits = h.depth_max;
     out->status_bytes = (uint32_t)kCtlHeaderBytes;
-    out->launches = 9 + kDepthPasses + c->max_passes;
+    // init, project, depth keys, plan, the depth passes, pair count, pair scan, bin ranges,
+    // placement, totals, rasterise
+    out->launches = 10 + kDepthPasses * sort_pass_launches(w.frame_n, true);
     out->packed = h.packed;
     out->idx_bits = h.idx_bits;
+    PlaceGeom pg{};
+    if (place_geometry(c->gp, w.frame_n, &pg) == cudaSuccess) {
+        out->place_chunks = pg.nchunks;
+        out->place_bands = pg.nbands;
+    }
+    out->launches += 1;  // the gather of the rectangles into depth order
     return KT_OK;
 }
 
@@ -713,8 +717,6 @@ kt_status kt_gs_debug_dump(kt_gs_ctx* c, uint32_t path, kt_gs_stage stage, void*
     const uint64_t n = w.frame_n;
     const uint64_t K = h.num_keys;
     const bool sorted_ok = h.plan_ok != 0;
-    const uint32_t ibits = h.idx_bits;
-    const unsigned long long imask = (1ull << ibits) - 1ull;
     const uint32_t tx = c->gp.tiles_x;
     const bool is_keys = stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_KEYS_UNSORTED;
     const bool is_vals = stage == KT_GS_STAGE_VALUES_SORTED || stage == KT_GS_STAGE_VALUES_UNSORTED;
@@ -779,17 +781,19 @@ kt_status kt_gs_debug_dump(kt_gs_ctx* c, uint32_t path, kt_gs_stage stage, void*
             run += cnt[i];
         }
     } else if (stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_VALUES_SORTED) {
-        std::vector<unsigned long long> e(K);
-        if ((st = fetch(w.keys[h.final_buf], K * 8, e.data())) != KT_OK) return st;
         if (is_vals) {
-            uint32_t* v = (uint32_t*)dst;
-            for (uint64_t i = 0; i < K; ++i) v[i] = (uint32_t)(e[i] & imask);
+            if ((st = fetch(w.pairs, K * 4, dst)) != KT_OK) return st;
         } else {
-            std::vector<uint32_t> depth(n);
+            // bin << 32 | depth bits, the bin of each pair read off the bin ranges
+            std::vector<uint32_t> g(K), depth(n);
+            std::vector<uint2> rng(ntiles(c));
+            if ((st = fetch(w.pairs, K * 4, g.data())) != KT_OK) return st;
             if ((st = fetch(w.depth, n * 4, depth.data())) != KT_OK) return st;
+            if ((st = fetch(w.ranges, rng.size() * 8, rng.data())) != KT_OK) return st;
             unsigned long long* k = (unsigned long long*)dst;
-            for (uint64_t i = 0; i < K; ++i)
-                k[i] = ((e[i] >> ibits) << 32) | depth[e[i] & imask];  // bin << 32 | depth bits
+            for (uint64_t b = 0; b < rng.size(); ++b)
+                for (uint64_t i = rng[b].x; i < rng[b].y && i < K; ++i)
+                    k[i] = ((unsigned long long)b << 32) | depth[g[i]];
         }
     } else {
         // pairs as the reference's binning would list them without its atomic reordering:
@@ -894,8 +898,11 @@ kt_status kt_gs_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* vals_i
     io.vals[0] = (uint32_t*)vals_in;
     io.vals[1] = alt_v;
     io.vals[2] = vals_out;
+    // Every pass of one call takes the same algorithm (it depends on n only) and the status words
+    // were cleared above, so they can also hold the reduce-then-scan table of a large call.
     for (uint32_t p = 0; p < max_passes; ++p)
-        if (launch_sort_pass(io, ctl, status, p, p + 1, n, false, s) != cudaSuccess) return KT_ERR_CUDA;
+        if (launch_sort_pass(io, ctl, status, (uint32_t*)status, p, p + 1, n, false, s) != cudaSuccess)
+            return KT_ERR_CUDA;
     return KT_OK;
 }
 

@@ -8,8 +8,11 @@
 //                        degree d interleaved per coefficient (R,G,B), DC first
 //   per path       rec   float4[3N] (px, py, alpha, z) (covInv 00,01,10,11) (r, g, b, 0)
 //                  counts u32[N], rect u32x2[N] (x0|x1<<16, y0|y1<<16), depth u32[N],
-//                  gsort u64[2][N] (Gaussians by depth), keys u64[2][cap] (pairs by bin),
-//                  ranges u32x2[tiles], look-back status words, two FrameCtl blocks.
+//                  srect u32x2[N] (rect in depth order),
+//                  gsort u64[2][N] (Gaussians by depth), pairs u32[cap] (the Gaussian of
+//                  every (bin, Gaussian) pair, in bin order; the bin is implied by the ranges),
+//                  ranges u32x2[tiles], pair table u32[chunks][tiles], look-back status
+//                  words of the depth sort, two FrameCtl blocks.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -38,14 +41,14 @@ __host__ __device__ inline uint64_t status_value(uint64_t w) { return w & kValue
 
 // Per-frame control block in device memory, reset by k_frame_init.
 struct FrameCtl {
-    unsigned long long num_keys;      // K, written by the last scan chunk
+    unsigned long long num_keys;      // K: pairs (render path) or keys (sorts)
     unsigned int depth_min;           // min / max of floatBitsToUint(z) ^ 0x80000000
     unsigned int depth_max;           //   over Gaussians with a non-zero tile count
     unsigned int num_visible;         // Gaussians with a non-zero tile count
     unsigned int error_flags;         // kErr*
-    unsigned int scan_ticket;         // chunk ticket of the scan/emit kernel
-    unsigned int plan_ok;             // set by k_plan when the sort may run
-    unsigned int depth_bits;          // set by the emit kernel (all CTAs agree)
+    unsigned int scan_ticket;         // work ticket of the pair placement
+    unsigned int plan_ok;             // the keys fit and the stages after may run
+    unsigned int depth_bits;          // bits of depth_max - depth_min
     unsigned int key_bits;
     unsigned int passes_run;
     unsigned int final_buf;           // which key/value buffer holds the sorted data
@@ -103,15 +106,28 @@ struct SceneDev {
     uint64_t n;
 };
 
+// Work split of the pair placement (place.cu).
+struct PlaceGeom {
+    uint32_t nchunks;         // chunks of consecutive Gaussians in depth order
+    uint32_t chunk_len;       // Gaussians per chunk (the last may be shorter)
+    uint32_t nbands;          // placement bands of bin rows (one warp's cursors each)
+    uint32_t band_rows;       // bin rows per placement band (the last may be shorter)
+    uint32_t ncbands;         // count bands of bin rows (one CTA's difference table each)
+    uint32_t cband_rows;
+    uint32_t count_smem;      // dynamic shared memory of a count CTA
+    uint32_t place_ctas;      // persistent placement CTAs
+    uint64_t table_words;     // u32 words of table[chunk][bin]
+};
+
 struct FrameBufs {
     float4* rec;
     uint32_t* counts;
     uint2* rect;
+    uint2* srect;                  // rect in depth order (empty for Gaussians without bins)
     uint32_t* depth;
     unsigned long long* gsort[2];  // Gaussians by depth: (depth - min) << idx_bits | index
-    unsigned long long* keys[2];   // (bin, Gaussian) pairs: bin << idx_bits | index
+    uint32_t* pairs;               // Gaussian index of every (bin, Gaussian) pair, in bin order
     uint2* ranges;
-    unsigned long long* scan_status;
     unsigned long long* sort_status;
     FrameCtl* ctl;                 // the frame, and the sort of the pairs by bin
     FrameCtl* ctl_depth;           // the sort of the Gaussians by depth
@@ -142,7 +158,7 @@ __device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned l
 // SM count of the current device (cached per device).
 int device_sm_count();
 
-// ---- mbarrier / bulk-copy helpers (sm_90+ PTX; no cluster multicast anywhere)
+// ---- mbarrier / bulk-copy helpers (sm_90+ PTX; every copy has a single destination CTA)
 #ifdef __CUDACC__
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {

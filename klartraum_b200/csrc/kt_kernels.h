@@ -24,8 +24,7 @@ __device__ __forceinline__ const unsigned long long* io_select(unsigned long lon
     return i == 0 ? b[0] : b[1];
 }
 
-constexpr int kScanChunk = 2048;  // Gaussians per scan/emit CTA
-constexpr int kSortTile = 4096;   // keys per onesweep CTA iteration
+constexpr int kSortTile = 4096;   // keys per sort tile
 
 // project.cu (compiled with -fmad=false)
 cudaError_t launch_project_count(const SceneDev& sc, const CamParams& cam, const GridParams& gp,
@@ -40,27 +39,39 @@ cudaError_t launch_pack_scene(const float* d_aos, uint64_t n, float4* pos, float
 cudaError_t launch_frame_init(FrameCtl* ctl, FrameCtl* ctl_depth, uint2* ranges, uint32_t ntiles,
                               cudaStream_t stream);
 cudaError_t launch_depth_keys(const FrameBufs& fb, uint64_t n, cudaStream_t stream);
-// per-bin pair counts (2D difference table `gdiff`, zero on entry and on exit) -> bin ranges and
-// the digit histograms of the bin sort
-cudaError_t launch_bin_counts(const FrameBufs& fb, const GridParams& gp, uint64_t n, int* gdiff,
-                              uint32_t max_passes, cudaStream_t stream);
-cudaError_t launch_scan_emit(const FrameBufs& fb, const GridParams& gp, uint64_t n, uint32_t epoch,
-                             uint32_t max_passes, cudaStream_t stream);
 // mode 0: ping-pong between io.keys[0] and [1]; mode 1: [0] -> ... -> [2] via [1]
 cudaError_t launch_plan(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes, int mode,
                         cudaStream_t stream);
 cudaError_t launch_frame_totals(const FrameCtl* ctl, const FrameCtl* ctl_depth, FrameTotals* totals,
                                 cudaStream_t stream);
 
+// place.cu: pairs by bin from the Gaussians in depth order (counting sort, no pair sort)
+cudaError_t place_geometry(const GridParams& gp, uint64_t n, PlaceGeom* out);
+// table[chunk][bin] <- the chunk's pairs per bin
+cudaError_t launch_pair_count(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
+                              uint32_t* table, cudaStream_t stream);
+// table -> prefix over chunks; bin ranges, K and the capacity check (FrameCtl::plan_ok)
+cudaError_t launch_pair_ranges(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
+                               uint32_t* table, cudaStream_t stream);
+// every pair written at its sorted position in fb.keys[0]
+cudaError_t launch_pair_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
+                              const uint32_t* table, cudaStream_t stream);
+
 // sort.cu
 cudaError_t launch_key_histogram(const unsigned long long* keys, uint64_t n, uint32_t key_bits,
                                  FrameCtl* ctl, cudaStream_t stream);
+// One stable 8-bit pass. Sorts of at most one wave of resident tiles run onesweep on the
+// epoch-tagged look-back words in `status`; larger ones run reduce-then-scan with its per-range
+// digit table in `table` (sort_table_words(max_keys) u32). The two must not overlap when other
+// sorts share `status`: a table value read as a look-back word could carry a live epoch tag.
 // packed: launch the variant for (key << idx_bits | index) elements; the variant that does not
 // match the frame's layout (FrameCtl::packed) returns at once.
-cudaError_t launch_sort_pass(const SortIO& io, FrameCtl* ctl, unsigned long long* status,
+cudaError_t launch_sort_pass(const SortIO& io, FrameCtl* ctl, unsigned long long* status, uint32_t* table,
                              uint32_t pass, uint32_t epoch, uint64_t max_keys, bool packed,
                              cudaStream_t stream);
 size_t sort_status_words(uint64_t max_keys);
+size_t sort_table_words(uint64_t max_keys);
+uint32_t sort_pass_launches(uint64_t max_keys, bool packed);  // kernels one pass launches
 
 // raster.cu
 cudaError_t launch_rasterize(const float4* rec, const SortIO& io, const uint2* ranges,

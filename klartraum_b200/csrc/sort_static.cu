@@ -86,7 +86,10 @@ extern "C" kt_status kt_gs_radix_sort_pairs_static(const uint64_t* keys_in, cons
     io.vals[0] = (uint32_t*)vals_in;
     io.vals[1] = alt_v;
     io.vals[2] = vals_out;
+    // Every pass of one call takes the same algorithm (it depends on n only) and the status words
+    // were cleared above, so they can also hold the reduce-then-scan table of a large call.
     for (uint32_t p = 0; p < max_passes; ++p)
-        if (launch_sort_pass(io, ctl, status, p, p + 1, n, false, s) != cudaSuccess) return KT_ERR_CUDA;
+        if (launch_sort_pass(io, ctl, status, (uint32_t*)status, p, p + 1, n, false, s) != cudaSuccess)
+            return KT_ERR_CUDA;
     return KT_OK;
 }
