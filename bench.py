@@ -189,13 +189,14 @@ def stage_report(w, cnt, st, stage_ms, timed_frames, nplanes):
         # depth keys (counts + depths read, 8-B keys written) and the depth sort passes (16 B per
         # Gaussian per pass)
         "depth_sort": w.n * (4 + 4 + 8) + cnt["depth_sort_bytes"] / nf,
-        # depth order, count and bin rectangle read per Gaussian; the (chunk, bin) table written
-        "pair_count": w.n * (8 + 4 + 8) + table,
-        # the table read, rewritten as its prefix over chunks; bin ranges written
+        # rectangles gathered into depth order (order, count, rectangle read; 8 B written), read
+        # again by the count; the (chunk, bin) table written
+        "pair_count": w.n * (8 + 4 + 8 + 8 + 8) + table,
+        # the table read and rewritten as its prefix over chunks; bin ranges written
         "bin_ranges": 2 * table + tiles * 8,
-        # depth order, count and rectangle per Gaussian, the table and bin starts read; 8 B per
-        # pair written once, at its place in bin order
-        "pair_place": w.n * (8 + 4 + 8) + table + tiles * 8 + cnt["sort_bytes"] / nf,
+        # depth order and rectangle per Gaussian, the table and bin starts read; 4 B per pair
+        # (its Gaussian's index) written once, at its place in bin order
+        "pair_place": w.n * (8 + 8) + table + tiles * 8 + cnt["sort_bytes"] / nf,
     }
     stages = {}
     for name in N.STAGE_NAMES[:-1]:
@@ -339,7 +340,7 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg_block,
         "gaussians_per_s": fps * w.n, "keys_per_frame": K_avg, "sort_passes_per_frame": passes_avg,
-        "sort_layout": "Gaussians radix-sorted by depth; (bin | index) pairs placed in bin order by a counting sort over (chunk of depth order, bin); packed u64 elements",
+        "sort_layout": "Gaussians radix-sorted by depth; (bin | index) pairs placed in bin order by a counting sort over (chunk of depth order, bin); a pair is stored as its u32 Gaussian index",
         "stages": stages, "roofline": roofline,
         "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": img_bytes + 192,
                 "d2h_bytes_per_step": img_bytes + st["status_bytes"], "steps": e2e_steps,

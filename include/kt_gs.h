@@ -143,7 +143,7 @@ typedef struct kt_gs_counters {
     uint64_t keys;        /* sum of K */
     uint64_t key_passes;  /* sum of K * (passes over the pairs; 0 with direct placement) */
     uint64_t visible;     /* sum of Gaussians with a non-zero tile count */
-    uint64_t sort_bytes;  /* sum of bytes of pairs written in bin order (8 per pair) */
+    uint64_t sort_bytes;  /* sum of bytes of pairs written in bin order (4 per pair) */
     uint64_t depth_sort_bytes; /* same for the depth sort of the Gaussians */
 } kt_gs_counters;
 

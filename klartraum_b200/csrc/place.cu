@@ -244,7 +244,13 @@ struct BatchGauss {
     float inv_w;    // 1 / w
 };
 
-__device__ __forceinline__ BatchGauss batch_gauss(uint32_t g, uint2 r, uint32_t by0, uint32_t by1) {
+// (o / w) | (o % w) << 8 for w in 1..32, o in 0..31, in shared memory
+struct DivTable {
+    uint16_t qr[33][32];
+};
+
+__device__ __forceinline__ BatchGauss batch_gauss(uint32_t g, uint2 r, uint32_t by0, uint32_t by1,
+                                                  const DivTable& dt) {
     BatchGauss b{g, 0u, 0u, 0u, 0.0f};
     const uint32_t y0 = max(r.y & 0xFFFFu, by0), y1 = min(r.y >> 16, by1);
     const uint32_t x0 = r.x & 0xFFFFu, x1 = r.x >> 16;
@@ -252,9 +258,19 @@ __device__ __forceinline__ BatchGauss batch_gauss(uint32_t g, uint2 r, uint32_t 
     const uint32_t w = x1 - x0;
     b.xw = x0 | (w << 16);
     b.yc = (y0 - by0) | ((w * (y1 - y0)) << 16);
-    b.inv_w = 1.0f / (float)w;
     uint32_t sy, sx;
-    divmod_small(32u, w, b.inv_w, sy, sx);
+    if (w <= 32u) {  // 32 = 31 + 1
+        const uint32_t d = dt.qr[w][31];
+        sy = d & 0xFFu;
+        sx = (d >> 8) + 1u;
+        if (sx == w) {
+            ++sy;
+            sx = 0u;
+        }
+    } else {
+        b.inv_w = 1.0f / (float)w;
+        divmod_small(32u, w, b.inv_w, sy, sx);
+    }
     b.step = sy | (sx << 16);
     return b;
 }
@@ -266,8 +282,14 @@ __device__ __forceinline__ BatchGauss batch_gauss(uint32_t g, uint2 r, uint32_t 
 __global__ void __launch_bounds__(kPlaceWarps * 32, 1) k_pair_place(FrameBufs fb, GridParams gp, PlaceGeom pg,
                                                                     uint64_t n, const uint32_t* __restrict__ table) {
     extern __shared__ uint32_t s_cur[];  // kBandMaxBins cursors per warp
+    __shared__ DivTable s_div;
     FrameCtl* ctl = fb.ctl;
     if (!ctl->plan_ok) return;
+    for (uint32_t i = threadIdx.x; i < 33 * 32; i += blockDim.x) {
+        const uint32_t w = i >> 5, o = i & 31u;
+        s_div.qr[w][o] = w ? (uint16_t)((o / w) | ((o % w) << 8)) : (uint16_t)0;
+    }
+    __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t* cur = s_cur + (size_t)warp * kBandMaxBins;
     const FrameCtl* cd = fb.ctl_depth;
@@ -298,7 +320,7 @@ __global__ void __launch_bounds__(kPlaceWarps * 32, 1) k_pair_place(FrameBufs fb
             q = qb + 32 + lane;
             const uint2 r1 = q < q1 ? fb.srect[q] : make_uint2(0u, 0u);
             const uint32_t g1 = q < q1 ? (uint32_t)(order[q] & imask) : kNone;
-            const BatchGauss mine = batch_gauss(g0, r0, by0, by1);
+            const BatchGauss mine = batch_gauss(g0, r0, by0, by1, s_div);
             uint32_t todo = __ballot_sync(0xFFFFFFFFu, mine.xw != 0u);
             while (todo) {  // this batch's Gaussians in depth order
                 const int src = __ffs(todo) - 1;
@@ -310,8 +332,14 @@ __global__ void __launch_bounds__(kPlaceWarps * 32, 1) k_pair_place(FrameBufs fb
                 const float inv_w = __shfl_sync(0xFFFFFFFFu, mine.inv_w, src);
                 const uint32_t x0 = xw & 0xFFFFu, w = xw >> 16, ly0 = yc & 0xFFFFu, cnt = yc >> 16;
                 const uint32_t sy = st & 0xFFFFu, sx = st >> 16;
-                uint32_t dy, dx;
-                divmod_small((uint32_t)lane, w, inv_w, dy, dx);  // this lane's first bin
+                uint32_t dy, dx;  // this lane's first bin
+                if (w <= 32u) {
+                    const uint32_t d = s_div.qr[w][lane];
+                    dy = d & 0xFFu;
+                    dx = d >> 8;
+                } else {
+                    divmod_small((uint32_t)lane, w, inv_w, dy, dx);
+                }
                 for (uint32_t j = lane; j < cnt; j += 32) {
                     const uint32_t li = (ly0 + dy) * tx + x0 + dx;
                     const uint32_t pos = cur[li];

@@ -312,7 +312,7 @@ def test_counters_accumulate_frames_and_keys():
     st = r.stats()
     assert c["frames"] == 20 and c["keys"] == 20 * st["num_keys"]
     assert st["sort_passes"] == 0 and c["key_passes"] == 0  # pairs placed in bin order directly
-    assert c["sort_bytes"] == 8 * c["keys"]
+    assert c["sort_bytes"] == 4 * c["keys"]
     ms, frames = r.stage_times_total()
     assert frames == 20 and ms["frame"] > 0 and ms["pair_place"] > 0
     assert r.counters()["frames"] == 0
