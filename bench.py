@@ -146,6 +146,9 @@ def run_reference(args, w, cfg_block):
     cfg = oracle.config(w.width, w.height, bin_size=16, sh_degree=w.sh_degree)
     bg = np.zeros((w.height, w.width, 4), np.uint8)
     bg[..., 3] = 255
+    # all host cores: launchers such as torchrun set OMP_NUM_THREADS=1 for their ranks
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    oracle.set_threads(threads)
     threads = oracle.lib().ko_get_threads()
     for s in range(args.warmup):
         oracle.render_frame_fast(cfg, cams[s % N_VIEWS], g3d, bg)
@@ -170,6 +173,12 @@ def run_reference(args, w, cfg_block):
 
 
 # ------------------------------------------------------------------- our arm
+
+# DRAM bytes (read + write) per launch of a stage's kernel, from the ncu captures summarised in
+# profiles/ (1M SH3 1080p workload): profiles/k_pair_place_single_1m.md,
+# profiles/k_project_count_single_1m.md.
+NCU_TRAFFIC = {"single_1m": {"pair_place": 77.7e6 + 59.9e6, "project_count": 240.0e6 + 46.2e6}}
+
 
 def stage_report(w, cnt, st, stage_ms, timed_frames, nplanes):
     """Per-stage time, algorithmic bytes and HBM fraction over a timed region, and the roofline
@@ -210,12 +219,13 @@ def stage_report(w, cnt, st, stage_ms, timed_frames, nplanes):
     dom = stages[dominant]
     if "bytes" in dom:
         roofline = {"kernel": dominant, "bound": "hbm", "achieved": dom["gbs"], "peak": peak, "unit": "GB/s",
-                    "frac": dom["frac"], "traffic": None, "peak_source": peak_kind,
-                    "bytes_per_launch": dom["bytes"]}
+                    "frac": dom["frac"], "traffic": NCU_TRAFFIC.get(w.name, {}).get(dominant),
+                    "peak_source": peak_kind, "bytes_per_launch": dom["bytes"]}
     else:
         hb = max((k for k in stages if "bytes" in stages[k]), key=lambda k: stages[k]["ms"])
         roofline = {"kernel": hb, "bound": "hbm", "achieved": stages[hb]["gbs"], "peak": peak, "unit": "GB/s",
-                    "frac": stages[hb]["frac"], "traffic": None, "peak_source": peak_kind,
+                    "frac": stages[hb]["frac"], "traffic": NCU_TRAFFIC.get(w.name, {}).get(hb),
+                    "peak_source": peak_kind,
                     "bytes_per_launch": stages[hb]["bytes"],
                     "note": f"{dominant} (issue bound, not HBM) takes the most time; this is the top HBM-bound stage"}
     return stages, roofline, K_avg, passes_avg
@@ -518,6 +528,7 @@ def cpu_baseline(w, cams) -> dict:
     cfg = oracle.config(w.width, w.height, bin_size=16, sh_degree=w.sh_degree)
     bg = np.zeros((w.height, w.width, 4), np.uint8)
     bg[..., 3] = 255
+    oracle.set_threads(len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1))
     oracle.render_frame_fast(cfg, cams[0], g3d, bg)  # warm caches / page in
     frames = 0
     t0 = time.perf_counter()
