@@ -52,6 +52,9 @@ def parse():
     p.add_argument("--mode", choices=["views", "bands"], default="views",
                    help="views: one view per GPU per step (default); bands: one frame split into bin-row bands "
                         "over the GPUs, strips all-gathered every step")
+    p.add_argument("--sorted-keys", action="store_true",
+                   help="bin through the reference-structured path (scan, key emission, radix sort of the "
+                        "pairs, boundary search) instead of placing the pairs in bin order")
     p.add_argument("--workload", default=None, help="scene of scenes.WORKLOADS (default: single_1m for views, "
                                                     "large_6m for bands)")
     return p.parse_args()
@@ -180,10 +183,12 @@ def run_reference(args, w, cfg_block):
 NCU_TRAFFIC = {"single_1m": {"pair_place": 77.7e6 + 59.9e6, "project_count": 240.0e6 + 46.2e6}}
 
 
-def stage_report(w, cnt, st, stage_ms, timed_frames, nplanes):
+def stage_report(w, cnt, st, stage_ms, timed_frames, nplanes, stage_names=None):
     """Per-stage time, algorithmic bytes and HBM fraction over a timed region, and the roofline
     entry of the dominant HBM-bound stage."""
     from klartraum_b200 import native as N
+
+    stage_names = stage_names or N.STAGE_NAMES
 
     peak, peak_kind = load_peaks()
     frames = max(timed_frames, 1)
@@ -206,9 +211,16 @@ def stage_report(w, cnt, st, stage_ms, timed_frames, nplanes):
         # depth order and rectangle per Gaussian, the table and bin starts read; 4 B per pair
         # (its Gaussian's index) written once, at its place in bin order
         "pair_place": w.n * (8 + 8) + table + tiles * 8 + cnt["sort_bytes"] / nf,
+        # reference-structured path: counts, rectangles and depths read, offsets written; 12 B
+        # (key + value) per pair written
+        "scan_emit": w.n * (4 + 8 + 4 + 8) + K_avg * 12,
+        # executed passes of the pair sort: 24 B per pair and pass
+        "key_sort": cnt["sort_bytes"] / nf,
     }
+    if stage_names is not N.STAGE_NAMES:
+        per_frame_bytes["bin_ranges"] = K_avg * 8 + tiles * 8  # boundary search over the sorted keys
     stages = {}
-    for name in N.STAGE_NAMES[:-1]:
+    for name in stage_names[:-1]:
         avg = stage_ms[name] / frames
         d = {"ms": avg, "share": stage_ms[name] / max(stage_ms["frame"], 1e-12)}
         if name in per_frame_bytes:
@@ -258,7 +270,9 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     def view_of(s):
         return (s * world + rank) % N_VIEWS
 
-    r = Renderer(w.width, w.height, bin_size=16, sh_degree=w.sh_degree, device=local_rank, flags=N.FLAG_TIMING)
+    base_flags = N.FLAG_SORTED_KEYS if args.sorted_keys else 0
+    r = Renderer(w.width, w.height, bin_size=16, sh_degree=w.sh_degree, device=local_rank,
+                 flags=N.FLAG_TIMING | base_flags)
     if world > 1:
         # the scene is made once (rank 0) and broadcast over NCCL; records land in device memory
         from klartraum_b200.multigpu import broadcast_scene
@@ -288,7 +302,7 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     r.counters()
 
     # ---- timed region (device-resident inputs): frames enqueued back to back, no host sync
-    r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC)
+    r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC | base_flags)
     clock = ClockSampler(local_rank)
     clock.start()
     time.sleep(0.5)
@@ -319,10 +333,11 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     fps = world * args.steps / (ms_max / 1000.0)
 
     # ---- per-stage bandwidth over the timed region
-    stages, roofline, K_avg, passes_avg = stage_report(w, cnt, st, stage_ms, timed_frames, nplanes)
+    stages, roofline, K_avg, passes_avg = stage_report(w, cnt, st, stage_ms, timed_frames, nplanes,
+                                                       r.stage_names)
 
     # ---- end to end through the public API with host buffers
-    r.set_flags(0)
+    r.set_flags(base_flags)
     e2e_steps = args.e2e_steps or max(10, args.steps // 4)
     host = torch.empty((w.height, w.width, 4), dtype=torch.uint8, pin_memory=True)
     host.copy_(bg.cpu())
@@ -350,7 +365,10 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg_block,
         "gaussians_per_s": fps * w.n, "keys_per_frame": K_avg, "sort_passes_per_frame": passes_avg,
-        "sort_layout": "Gaussians radix-sorted by depth; (bin | index) pairs placed in bin order by a counting sort over (chunk of depth order, bin); a pair is stored as its u32 Gaussian index",
+        "sort_layout": ("reference-structured: index-order scan, (bin << depth_bits | depth, index) pairs, "
+                        "LSD radix sort of the pairs, boundary search" if args.sorted_keys else
+                        "Gaussians radix-sorted by depth; (bin | index) pairs placed in bin order by a counting "
+                        "sort over (chunk of depth order, bin); a pair is stored as its u32 Gaussian index"),
         "stages": stages, "roofline": roofline,
         "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": img_bytes + 192,
                 "d2h_bytes_per_step": img_bytes + st["status_bytes"], "steps": e2e_steps,
@@ -395,9 +413,11 @@ def run_bands(args, w, rank, world, local_rank):
     else:
         scene_dev, scene_host = None, make_scene(w)
 
+    base_flags = N.FLAG_SORTED_KEYS if args.sorted_keys else 0
+
     def renderer(band):
         r = Renderer(w.width, w.height, bin_size=16, sh_degree=w.sh_degree, device=local_rank,
-                     flags=N.FLAG_TIMING, tile_rows=band)
+                     flags=N.FLAG_TIMING | base_flags, tile_rows=band)
         if scene_dev is not None:
             r.set_gaussians_device(scene_dev.data_ptr(), n_rec)
             torch.cuda.synchronize()
@@ -439,7 +459,7 @@ def run_bands(args, w, rank, world, local_rank):
     r.stage_times_total()
     r.counters()
 
-    r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC)
+    r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC | base_flags)
     clock = ClockSampler(local_rank)
     clock.start()
     time.sleep(0.5)
@@ -467,10 +487,11 @@ def run_bands(args, w, rank, world, local_rank):
     cnt = r.counters()
     st = r.stats()
     nplanes = (3 * (w.sh_degree + 1) ** 2 + 3) // 4
-    stages, roofline, K_avg, passes_avg = stage_report(w, cnt, st, stage_ms, timed_frames, nplanes)
+    stages, roofline, K_avg, passes_avg = stage_report(w, cnt, st, stage_ms, timed_frames, nplanes,
+                                                       r.stage_names)
 
     # end to end: camera from host through the API, band render, strip gather, frame to host
-    r.set_flags(0)
+    r.set_flags(base_flags)
     e2e_steps = args.e2e_steps or max(10, args.steps // 4)
     host = torch.empty((w.height, w.width, 4), dtype=torch.uint8, pin_memory=True)
     for s in range(3):
@@ -549,6 +570,7 @@ def main():
 
     w = WORKLOADS[args.workload or (WORKLOAD if args.mode == "views" else "large_6m")]
     cfg_block = workload_config(w)
+    cfg_block["binning"] = "sorted_keys" if args.sorted_keys else "placed"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -96,6 +96,10 @@ typedef struct kt_gaussian2d {
 #define KT_GS_FLAG_KEEP_UNSORTED 0x8u    /* accepted for compatibility; the unsorted dumps are always
                                             available (rebuilt from the device's bin rectangles) */
 #define KT_GS_FLAG_TIMING 0x10u          /* record CUDA events around every stage */
+#define KT_GS_FLAG_SORTED_KEYS 0x20u     /* bin through the reference's stage structure: scan of the
+                                            counts in index order, one (bin << depth_bits | depth, index)
+                                            pair per bin and Gaussian, radix sort of the pairs, boundary
+                                            search for the bin ranges (same image and dumps; slower) */
 
 typedef struct kt_gs_config {
     uint32_t width;          /* screen width in pixels (reference: 512, vulkan_gaussian_splatting.cpp:20) */

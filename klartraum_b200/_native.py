@@ -26,6 +26,7 @@ FLAG_NO_AUTOGROW = 0x2
 FLAG_ASYNC = 0x4
 FLAG_KEEP_UNSORTED = 0x8
 FLAG_TIMING = 0x10
+FLAG_SORTED_KEYS = 0x20
 
 STAGE_PROJECTED = 0
 STAGE_TILE_COUNTS = 1
@@ -37,6 +38,8 @@ STAGE_VALUES_SORTED = 6
 STAGE_TILE_RANGES = 7
 NSTAGES = 7
 STAGE_NAMES = ["project_count", "depth_sort", "pair_count", "bin_ranges", "pair_place", "rasterize", "frame"]
+# the same timer slots when KT_GS_FLAG_SORTED_KEYS selects the reference-structured binning
+STAGE_NAMES_KEYS = ["project_count", "scan_emit", "key_sort", "bin_ranges", "totals", "rasterize", "frame"]
 
 # every entry point include/kt_gs.h declares
 EXPORTED_SYMBOLS = [

@@ -32,6 +32,7 @@ SOURCES = {
     "project.cu": ["-fmad=false", "-prec-div=true", "-prec-sqrt=true", "-ftz=false"],
     "binning.cu": [],
     "place.cu": [],
+    "keys.cu": [],
     "sort.cu": [],
     "raster.cu": [],
     "sort_static.cu": [],

@@ -65,6 +65,18 @@ struct PathWs {
     uint32_t* pair_table = nullptr;  // pairs per (chunk, bin), then their prefix over chunks
     uint64_t pair_table_words = 0;
     uint2* ranges = nullptr;
+    // reference-structured path (KT_GS_FLAG_SORTED_KEYS), allocated on first use
+    unsigned long long* keys[2] = {nullptr, nullptr};  // bin << depth_bits | depth, ping-pong
+    uint32_t* vals[2] = {nullptr, nullptr};            // Gaussian index, ping-pong
+    uint64_t key_cap = 0;
+    unsigned long long* key_status = nullptr;  // look-back words of the pair sort
+    uint32_t* key_table = nullptr;             // reduce-then-scan table of the pair sort
+    uint32_t key_epoch = 0;
+    unsigned long long* offsets = nullptr;      // scan of the counts, index order
+    unsigned long long* scan_status = nullptr;  // look-back words of that scan
+    uint64_t key_n = 0;
+    uint32_t scan_epoch = 0;
+    bool keys_frame = false;  // the path's last frame took the keys path
     FrameCtl* ctl = nullptr;
     FrameCtl* ctl_depth = nullptr;
     FrameCtl* host_ctl = nullptr;  // pinned copy of the last frame's control block
@@ -176,6 +188,9 @@ void free_path(PathWs& w) {
     dfree(w.gsort[1]);
     dfree(w.pairs); dfree(w.pair_table);
     dfree(w.sort_status); dfree(w.sort_table); dfree(w.ranges); dfree(w.ctl); dfree(w.ctl_depth);
+    dfree(w.keys[0]); dfree(w.keys[1]); dfree(w.vals[0]); dfree(w.vals[1]); dfree(w.key_status);
+    dfree(w.key_table); dfree(w.offsets); dfree(w.scan_status);
+    w.key_cap = w.key_n = 0;
     dfree(w.img); dfree(w.g2d);
     if (w.host_ctl) cudaFreeHost(w.host_ctl);
     w.host_ctl = nullptr;
@@ -255,6 +270,39 @@ kt_status ensure_cap(kt_gs_ctx* c, PathWs& w, uint64_t cap) {
     return KT_OK;
 }
 
+// Buffers of the reference-structured path, sized for the path's capacity and n Gaussians.
+kt_status ensure_keys(kt_gs_ctx* c, PathWs& w, uint64_t n) {
+    if (w.key_cap < w.cap) {
+        dfree(w.keys[0]); dfree(w.keys[1]); dfree(w.vals[0]); dfree(w.vals[1]);
+        dfree(w.key_status); dfree(w.key_table);
+        w.key_cap = 0;
+        for (int b = 0; b < 2; ++b) {
+            KT_TRY_CUDA(c, cudaMalloc(&w.keys[b], sizeof(unsigned long long) * w.cap));
+            KT_TRY_CUDA(c, cudaMalloc(&w.vals[b], sizeof(uint32_t) * w.cap));
+        }
+        const size_t words = sort_status_words(w.cap);
+        KT_TRY_CUDA(c, cudaMalloc(&w.key_status, sizeof(unsigned long long) * words));
+        KT_TRY_CUDA(c, cudaMemset(w.key_status, 0, sizeof(unsigned long long) * words));
+        KT_TRY_CUDA(c, cudaMalloc(&w.key_table, sizeof(uint32_t) * sort_table_words(w.cap)));
+        w.key_epoch = 0;
+        w.key_cap = w.cap;
+    }
+    if (w.key_n < n) {
+        dfree(w.offsets); dfree(w.scan_status);
+        w.key_n = 0;
+        const uint64_t chunks = (n + kScanChunk - 1) / kScanChunk;
+        KT_TRY_CUDA(c, cudaMalloc(&w.offsets, sizeof(unsigned long long) * n));
+        KT_TRY_CUDA(c, cudaMalloc(&w.scan_status, sizeof(unsigned long long) * chunks));
+        KT_TRY_CUDA(c, cudaMemset(w.scan_status, 0, sizeof(unsigned long long) * chunks));
+        w.scan_epoch = 0;
+        w.key_n = n;
+    }
+    return KT_OK;
+}
+
+// 8-bit passes the keys path's sort may need: bin bits + up to 32 depth bits
+uint32_t key_passes(const kt_gs_ctx* c) { return (c->gp.tile_bits + 32 + 7) / 8; }
+
 FrameBufs frame_bufs(const PathWs& w) {
     FrameBufs fb;
     fb.rec = w.rec;
@@ -265,6 +313,12 @@ FrameBufs frame_bufs(const PathWs& w) {
     fb.gsort[0] = w.gsort[0];
     fb.gsort[1] = w.gsort[1];
     fb.pairs = w.pairs;
+    fb.offsets = w.offsets;
+    fb.keys[0] = w.keys[0];
+    fb.keys[1] = w.keys[1];
+    fb.vals[0] = w.vals[0];
+    fb.vals[1] = w.vals[1];
+    fb.scan_status = w.scan_status;
     fb.ranges = w.ranges;
     fb.sort_status = w.sort_status;
     fb.ctl = w.ctl;
@@ -297,6 +351,63 @@ kt_status drain_slot(kt_gs_ctx* c, PathWs& w, int slot) {
 }
 
 // Enqueue one frame on `stream`. Does not wait.
+// The reference-structured frame: project -> scan + key emission in index order -> plan ->
+// radix sort of (key, value) pairs -> boundary search for the bin ranges -> rasterise.
+kt_status enqueue_keys_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* cam, uchar4* img,
+                             cudaStream_t stream, cudaEvent_t* ev, uint64_t n) {
+    const bool timed = ev != nullptr;
+    kt_status st = ensure_keys(c, w, std::max<uint64_t>(n, 1));
+    if (st != KT_OK) return st;
+    const uint32_t passes = key_passes(c);
+    if (++w.scan_epoch > kEpochMax) {
+        KT_TRY_CUDA(c, cudaMemsetAsync(w.scan_status, 0,
+                                       sizeof(unsigned long long) * ((w.key_n + kScanChunk - 1) / kScanChunk),
+                                       stream));
+        w.scan_epoch = 1;
+    }
+    if (w.key_epoch + passes + 1 > kEpochMax) {
+        KT_TRY_CUDA(c, cudaMemsetAsync(w.key_status, 0, sizeof(unsigned long long) * sort_status_words(w.key_cap),
+                                       stream));
+        w.key_epoch = 0;
+    }
+    const uint32_t epoch0 = w.key_epoch + 1;
+    w.key_epoch += passes;
+    FrameBufs fb = frame_bufs(w);
+    SortIO io{};
+    io.keys[0] = w.keys[0];
+    io.keys[1] = w.keys[1];
+    io.vals[0] = w.vals[0];
+    io.vals[1] = w.vals[1];
+
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[0], stream));
+    KT_TRY_CUDA(c, launch_frame_init(w.ctl, w.ctl_depth, w.ranges, ntiles(c), stream));
+    if (src == Source::Scene) {
+        SceneDev sc{c->pos, c->rot, c->scale, c->sh, c->nplanes, c->deg, c->n};
+        KT_TRY_CUDA(c, launch_project_count(sc, *cam, c->gp, fb, stream));
+    } else {
+        KT_TRY_CUDA(c, launch_load_projected(w.g2d, n, c->gp, fb, stream));
+    }
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[1], stream));
+    KT_TRY_CUDA(c, launch_key_scan_emit(fb, c->gp, n, w.scan_epoch, passes, stream));
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[2], stream));
+    KT_TRY_CUDA(c, launch_plan(w.ctl, w.cap, passes, 0, stream));
+    for (uint32_t p = 0; p < passes; ++p)
+        KT_TRY_CUDA(c, launch_sort_pass(io, w.ctl, w.key_status, w.key_table, p, epoch0 + p, w.cap, false, stream));
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[3], stream));
+    KT_TRY_CUDA(c, launch_key_ranges(io, w.ctl, w.ranges, w.cap, stream));
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[4], stream));
+    KT_TRY_CUDA(c, launch_frame_totals(w.ctl, w.ctl_depth, w.totals, stream));
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[5], stream));
+    KT_TRY_CUDA(c, launch_rasterize(w.rec, io, w.ranges, w.ctl, c->gp, img,
+                                    (c->cfg.flags & KT_GS_FLAG_EXIT_PER_ELEMENT) != 0, stream));
+    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[6], stream));
+    KT_TRY_CUDA(c, cudaMemcpyAsync(w.host_ctl, w.ctl, kCtlHeaderBytes, cudaMemcpyDeviceToHost, stream));
+    KT_TRY_CUDA(c, cudaEventRecord(w.done_ev, stream));
+    w.have_frame = true;
+    w.frame_n = n;
+    return KT_OK;
+}
+
 kt_status enqueue_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* cam, uchar4* img,
                         cudaStream_t stream) {
     const uint64_t n = src == Source::Scene ? c->n : w.g2d_n;
@@ -314,6 +425,8 @@ kt_status enqueue_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* ca
         w.ring_last = slot;
         w.ring_next = (slot + 1) % PathWs::kRing;
     }
+    w.keys_frame = (c->cfg.flags & KT_GS_FLAG_SORTED_KEYS) != 0;
+    if (w.keys_frame) return enqueue_keys_frame(c, w, src, cam, img, stream, ev, n);
     // work split of the pair placement, and its table
     PlaceGeom pg{};
     KT_TRY_CUDA(c, place_geometry(c->gp, n, &pg));
@@ -664,8 +777,10 @@ kt_status kt_gs_frame_stats(kt_gs_ctx* c, uint32_t path, kt_gs_stats* out) {
     out->depth_max_bits = h.depth_max;
     out->status_bytes = (uint32_t)kCtlHeaderBytes;
     // init, project, depth keys, plan, the depth passes, pair count, pair scan, bin ranges,
-    // placement, totals, rasterise
-    out->launches = 10 + kDepthPasses * sort_pass_launches(w.frame_n, true);
+    // placement, totals, rasterise; or init, project, scan/emit, plan, the key passes, ranges,
+    // totals, rasterise
+    out->launches = w.keys_frame ? 7 + key_passes(c) * sort_pass_launches(w.cap, false)
+                                 : 10 + kDepthPasses * sort_pass_launches(w.frame_n, true);
     out->packed = h.packed;
     out->idx_bits = h.idx_bits;
     PlaceGeom pg{};
@@ -673,7 +788,7 @@ kt_status kt_gs_frame_stats(kt_gs_ctx* c, uint32_t path, kt_gs_stats* out) {
         out->place_chunks = pg.nchunks;
         out->place_bands = pg.nbands;
     }
-    out->launches += 1;  // the gather of the rectangles into depth order
+    if (!w.keys_frame) out->launches += 1;  // the gather of the rectangles into depth order
     return KT_OK;
 }
 
@@ -769,9 +884,11 @@ kt_status kt_gs_debug_dump(kt_gs_ctx* c, uint32_t path, kt_gs_stage stage, void*
         if ((st = fetch(w.counts, n * 4, dst)) != KT_OK) return st;
     } else if (stage == KT_GS_STAGE_TILE_RANGES) {
         if ((st = fetch(w.ranges, need, dst)) != KT_OK) return st;
+    } else if (stage == KT_GS_STAGE_OFFSETS && w.keys_frame) {
+        if ((st = fetch(w.offsets, n * 8, dst)) != KT_OK) return st;
     } else if (stage == KT_GS_STAGE_OFFSETS) {
-        // the reference algorithm's scan is in Gaussian index order; the renderer scans in depth
-        // order, so this dump is the index-order exclusive scan of the device's counts
+        // the reference algorithm's scan is in Gaussian index order; the default path has no
+        // such scan, so this dump is the index-order exclusive scan of the device's counts
         std::vector<uint32_t> cnt(n);
         if ((st = fetch(w.counts, n * 4, cnt.data())) != KT_OK) return st;
         uint64_t* o = (uint64_t*)dst;
@@ -779,6 +896,18 @@ kt_status kt_gs_debug_dump(kt_gs_ctx* c, uint32_t path, kt_gs_stage stage, void*
         for (uint64_t i = 0; i < n; ++i) {
             o[i] = run;
             run += cnt[i];
+        }
+    } else if ((stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_VALUES_SORTED) && w.keys_frame) {
+        if (is_vals) {
+            if ((st = fetch(w.vals[h.final_buf], K * 4, dst)) != KT_OK) return st;
+        } else {
+            // bin << depth_bits | (depth - depth_min)  ->  bin << 32 | depth, the reference's key
+            if ((st = fetch(w.keys[h.final_buf], K * 8, dst)) != KT_OK) return st;
+            unsigned long long* k = (unsigned long long*)dst;
+            const uint32_t db = h.depth_bits;
+            const unsigned long long dm = db ? ((1ull << db) - 1ull) : 0ull;
+            for (uint64_t i = 0; i < K; ++i)
+                k[i] = ((k[i] >> db) << 32) | (unsigned long long)((uint32_t)(k[i] & dm) + h.depth_min);
         }
     } else if (stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_VALUES_SORTED) {
         if (is_vals) {

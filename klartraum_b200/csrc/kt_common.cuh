@@ -127,6 +127,11 @@ struct FrameBufs {
     uint32_t* depth;
     unsigned long long* gsort[2];  // Gaussians by depth: (depth - min) << idx_bits | index
     uint32_t* pairs;               // Gaussian index of every (bin, Gaussian) pair, in bin order
+    // reference-structured path (KT_GS_FLAG_SORTED_KEYS): offsets, keys and values
+    unsigned long long* offsets;   // exclusive scan of the counts, index order
+    unsigned long long* keys[2];   // bin << depth_bits | (depth - depth_min), ping-pong
+    uint32_t* vals[2];             // Gaussian index, ping-pong
+    unsigned long long* scan_status;
     uint2* ranges;
     unsigned long long* sort_status;
     FrameCtl* ctl;                 // the frame, and the sort of the pairs by bin

@@ -25,6 +25,7 @@ __device__ __forceinline__ const unsigned long long* io_select(unsigned long lon
 }
 
 constexpr int kSortTile = 4096;   // keys per sort tile
+constexpr int kScanChunk = 2048;  // Gaussians per scan/emit CTA (keys path)
 
 // project.cu (compiled with -fmad=false)
 cudaError_t launch_project_count(const SceneDev& sc, const CamParams& cam, const GridParams& gp,
@@ -56,6 +57,12 @@ cudaError_t launch_pair_ranges(const FrameBufs& fb, const GridParams& gp, const 
 // every pair written at its sorted position in fb.keys[0]
 cudaError_t launch_pair_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
                               const uint32_t* table, cudaStream_t stream);
+
+// keys.cu: the reference-structured path (scan, key emission, boundary search)
+cudaError_t launch_key_scan_emit(const FrameBufs& fb, const GridParams& gp, uint64_t n, uint32_t epoch,
+                                 uint32_t max_passes, cudaStream_t stream);
+cudaError_t launch_key_ranges(const SortIO& io, const FrameCtl* ctl, uint2* ranges, uint64_t max_keys,
+                              cudaStream_t stream);
 
 // sort.cu
 cudaError_t launch_key_histogram(const unsigned long long* keys, uint64_t n, uint32_t key_bits,

@@ -42,6 +42,7 @@ class Renderer:
         if tile_rows is not None:
             cfg.tile_row_begin, cfg.tile_row_end = tile_rows
         self.config = cfg
+        self._flags = flags
         ctx = C.c_void_p()
         N.check(self._lib.kt_gs_create(C.byref(cfg), device, C.byref(ctx)))
         self._ctx = ctx
@@ -121,6 +122,12 @@ class Renderer:
     def set_flags(self, flags: int) -> None:
         self._check(self._lib.kt_gs_set_flags(self._ctx, flags))
         self.config.flags = flags
+        self._flags = flags
+
+    @property
+    def stage_names(self) -> list:
+        """Names of the stage timer slots for the binning path the flags select."""
+        return N.STAGE_NAMES_KEYS if self._flags & N.FLAG_SORTED_KEYS else N.STAGE_NAMES
 
     def counters(self, path: int = 0) -> dict:
         """Frame totals accumulated on the device since the previous call (then reset)."""
@@ -140,14 +147,14 @@ class Renderer:
     def stage_times(self, path: int = 0) -> dict:
         ms = (C.c_float * N.NSTAGES)()
         self._check(self._lib.kt_gs_stage_times(self._ctx, path, ms))
-        return dict(zip(N.STAGE_NAMES, list(ms)))
+        return dict(zip(self.stage_names, list(ms)))
 
     def stage_times_total(self, path: int = 0) -> tuple[dict, int]:
         """Summed stage milliseconds of all timed frames since the last call, and their count."""
         ms = (C.c_double * N.NSTAGES)()
         frames = C.c_uint64(0)
         self._check(self._lib.kt_gs_stage_times_total(self._ctx, path, ms, C.byref(frames)))
-        return dict(zip(N.STAGE_NAMES, list(ms))), frames.value
+        return dict(zip(self.stage_names, list(ms))), frames.value
 
     _STAGE_DTYPES = {
         N.STAGE_PROJECTED: GAUSSIAN2D_DTYPE,

@@ -58,8 +58,14 @@ def run_case(name, wname, n, wh, bin_size, sh, flags, rows, bg_kind, dist):
     return r, out, ref, bg
 
 
+@pytest.mark.parametrize("keys", [False, True], ids=["placed", "sorted_keys"])
 @pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
-def test_frame_parity(case):
+def test_frame_parity(case, keys):
+    """Every stage buffer against the oracle, for the default path (pairs placed in bin order)
+    and the reference-structured one (scan, key emission, radix sort, boundary search)."""
+    case = list(case)
+    if keys:
+        case[6] |= N.FLAG_SORTED_KEYS
     r, out, ref, bg = run_case(*case)
     st = r.stats()
     assert st["error_flags"] == 0
@@ -316,3 +322,25 @@ def test_counters_accumulate_frames_and_keys():
     ms, frames = r.stage_times_total()
     assert frames == 20 and ms["frame"] > 0 and ms["pair_place"] > 0
     assert r.counters()["frames"] == 0
+
+
+@pytest.mark.parametrize("wname,n,wh", [("single_1m", 200000, (1280, 720)), ("stress_2m", 20000, (960, 540))])
+def test_sorted_keys_path_draws_the_same_image(wname, n, wh):
+    """The two binning paths order the pairs identically, so their images are identical."""
+    w = WORKLOADS[wname]
+    g3d = make_scene(w, n=n)
+    cam = orbit_camera(w.distance, *wh, fovy_deg=60.0, up="y")
+    bg = background(wh[1], wh[0], "random")
+    imgs, keys = [], []
+    for flags in (0, N.FLAG_SORTED_KEYS):
+        r = Renderer(*wh, bin_size=16, sh_degree=w.sh_degree, flags=flags)
+        r.set_gaussians(g3d)
+        img = device_image(bg)
+        r.render(cam, img)
+        imgs.append(img.cpu().numpy())
+        keys.append((r.dump(N.STAGE_KEYS_SORTED), r.dump(N.STAGE_VALUES_SORTED), r.dump(N.STAGE_TILE_RANGES)))
+        assert r.stats()["sort_passes"] == (0 if flags == 0 else r.stats()["sort_passes"])
+        r.close()
+    assert np.array_equal(imgs[0], imgs[1])
+    for a, b in zip(keys[0], keys[1]):
+        assert np.array_equal(a, b)
