@@ -224,6 +224,15 @@ kt_status kt_gs_set_gaussians_device(kt_gs_ctx* ctx, const kt_gaussian3d* dev, u
 kt_status kt_gs_load_spz(kt_gs_ctx* ctx, const char* path);
 
 /*
+ * Decode an .spz file on the host into Gaussian3D records with loadSPZModel's activations
+ * (the records kt_gs_load_spz uploads). With out == NULL only *count (and *sh_degree) are set;
+ * otherwise capacity must be >= *count. KT_ERR_IO for unreadable or malformed files.
+ * No counterpart in the reference (its loader decodes straight into the node's buffer).
+ */
+kt_status kt_gs_spz_decode(const char* path, kt_gaussian3d* out, uint64_t capacity, uint64_t* count,
+                           uint32_t* sh_degree);
+
+/*
  * Render one frame. `cam` is host memory (the per-path camera UBO, uniformbufferobject.hpp:67-70).
  * `d_rgba8` is a device image of width*height RGBA8 pixels, row-major, row 0 at the top; it
  * is read-modify-written: out = clamp(in + vec4(C,1)*(1-T)) (gsplat_binned_splatting.comp:119-121).

@@ -48,7 +48,7 @@ EXPORTED_SYMBOLS = [
     "kt_gs_set_gaussians_device", "kt_gs_load_spz", "kt_gs_render", "kt_gs_render_host",
     "kt_gs_render_batch", "kt_gs_render_projected", "kt_gs_sync", "kt_gs_frame_stats",
     "kt_gs_debug_dump", "kt_gs_stage_times", "kt_gs_stage_times_total", "kt_gs_radix_sort_pairs",
-    "kt_gs_set_flags", "kt_gs_counters_take",
+    "kt_gs_set_flags", "kt_gs_counters_take", "kt_gs_spz_decode",
 ]
 
 
@@ -127,6 +127,7 @@ def load() -> C.CDLL:
         "kt_gs_set_gaussians": (C.c_int, [vp, vp, u64]),
         "kt_gs_set_gaussians_device": (C.c_int, [vp, vp, u64, vp]),
         "kt_gs_load_spz": (C.c_int, [vp, C.c_char_p]),
+        "kt_gs_spz_decode": (C.c_int, [C.c_char_p, vp, C.c_uint64, C.POINTER(C.c_uint64), C.POINTER(u32)]),
         "kt_gs_render": (C.c_int, [vp, vp, vp, u32, vp]),
         "kt_gs_render_host": (C.c_int, [vp, vp, vp, u32, vp]),
         "kt_gs_render_batch": (C.c_int, [vp, vp, u32, vp, vp]),
@@ -189,3 +190,18 @@ def radix_sort_pairs(keys_in, vals_in, keys_out, vals_out, n: int, key_bits: int
     check(lib.kt_gs_radix_sort_pairs(as_ptr(keys_in), as_ptr(vals_in), as_ptr(keys_out), as_ptr(vals_out),
                                      n, key_bits, as_ptr(temp), C.byref(size), stream or None))
     return size.value
+
+
+def spz_decode(path: str):
+    """Decode an .spz file on the host (kt_gs_spz_decode): (Gaussian3D records, SH degree)."""
+    import numpy as np
+
+    from .types import GAUSSIAN3D_DTYPE
+
+    lib = load()
+    n, deg = C.c_uint64(0), C.c_uint32(0)
+    check(lib.kt_gs_spz_decode(path.encode(), None, 0, C.byref(n), C.byref(deg)))
+    out = np.zeros(n.value, GAUSSIAN3D_DTYPE)
+    if n.value:
+        check(lib.kt_gs_spz_decode(path.encode(), out.ctypes.data, n.value, C.byref(n), C.byref(deg)))
+    return out, deg.value

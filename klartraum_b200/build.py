@@ -37,6 +37,7 @@ SOURCES = {
     "raster.cu": [],
     "sort_static.cu": [],
     "api.cpp": [],
+    "spz.cpp": [],
 }
 
 
@@ -81,7 +82,7 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
         objs = list(ex.map(lambda kv: _compile(kv[0], kv[1] + (extra_info if kv[0].endswith(".cu") else []),
                                                verbose or ptxas_info), SOURCES.items()))
     if _stale(LIB, objs):
-        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB + ".tmp", *objs, "-lcudart_static", "-lrt", "-ldl",
+        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB + ".tmp", *objs, "-lcudart_static", "-lrt", "-ldl", "-lz",
                "-lpthread"]
         if verbose:
             print(" ".join(cmd), flush=True)

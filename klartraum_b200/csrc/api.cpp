@@ -986,9 +986,20 @@ kt_status kt_gs_stage_times_total(kt_gs_ctx* c, uint32_t path, double ms_total[K
 }
 
 kt_status kt_gs_load_spz(kt_gs_ctx* c, const char* path) {
-    if (!c) return KT_ERR_ARG;
-    return fail(c, KT_ERR_IO, std::string("spz loading is not available in this build: ") +
-                                  (path ? path : "(null)"));
+    if (!c || !path) return KT_ERR_ARG;
+    uint64_t n = 0;
+    uint32_t deg = 0;
+    kt_status s = kt_gs_spz_decode(path, nullptr, 0, &n, &deg);
+    if (s != KT_OK) return fail(c, s, std::string("cannot read spz file ") + path);
+    std::vector<kt_gaussian3d> g;
+    try {
+        g.resize(n);
+    } catch (const std::bad_alloc&) {
+        return fail(c, KT_ERR_NOMEM, "no host memory for the spz records");
+    }
+    s = kt_gs_spz_decode(path, g.data(), n, &n, &deg);
+    if (s != KT_OK) return fail(c, s, std::string("cannot decode spz file ") + path);
+    return kt_gs_set_gaussians(c, g.data(), n);
 }
 
 kt_status kt_gs_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* vals_in,
