@@ -12,7 +12,9 @@ frame, so no L2 flush is needed between frames.
     python bench.py --mode bands [--workload large_6m]   # one 4K frame split over the GPUs
 
 ``--mode bands`` splits every frame into bin-row bands, one per rank, balanced on per-row pair
-counts, and all-gathers the strips each step (strong scaling).
+counts, and all-gathers the strips each step (strong scaling). ``--launch`` (default graph)
+replays each frame as a captured CUDA graph; ``--sorted-keys`` bins through the
+reference-structured path.
 ``--impl reference`` times the CPU restatement of the reference algorithm (the oracle, C +
 OpenMP on all host cores) on the same workload; under torchrun only rank 0 runs it.
 Prints one JSON line (rank 0).
@@ -52,6 +54,10 @@ def parse():
     p.add_argument("--mode", choices=["views", "bands"], default="views",
                    help="views: one view per GPU per step (default); bands: one frame split into bin-row bands "
                         "over the GPUs, strips all-gathered every step")
+    p.add_argument("--launch", choices=["graph", "stream"], default="graph",
+                   help="graph (default): each path's frame is captured once as a CUDA graph and replayed with new "
+                        "cameras (KT_GS_FLAG_GRAPH), as the reference re-submits recorded command buffers; stage "
+                        "times then come from a separate stream-launched pass. stream: every kernel launched per frame")
     p.add_argument("--sorted-keys", action="store_true",
                    help="bin through the reference-structured path (scan, key emission, radix sort of the "
                         "pairs, boundary search) instead of placing the pairs in bin order")
@@ -300,9 +306,25 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     torch.cuda.synchronize()
     r.stage_times_total()
     r.counters()
+    stage_pass = None
+    if (args.launch == 'graph'):
+        # stage timers are not recorded by graph replays: take them from a stream-launched pass
+        r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC | base_flags)
+        for s in range(min(args.steps, 200)):
+            r.render(cams[view_of(s)], img, stream=sptr)
+        r.sync()
+        stage_pass = r.stage_times_total()
+        r.counters()
+        run_flags = N.FLAG_GRAPH | N.FLAG_ASYNC | base_flags
+        for s in range(3):  # capture
+            r.set_flags(N.FLAG_GRAPH | base_flags)
+            r.render(cams[view_of(s)], img, stream=sptr)
+        r.counters()
+    else:
+        run_flags = N.FLAG_TIMING | N.FLAG_ASYNC | base_flags
 
     # ---- timed region (device-resident inputs): frames enqueued back to back, no host sync
-    r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC | base_flags)
+    r.set_flags(run_flags)
     clock = ClockSampler(local_rank)
     clock.start()
     time.sleep(0.5)
@@ -323,6 +345,8 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     clocks = clock.summary(t_wall0, t_wall1)
     ms = ev0.elapsed_time(ev1)
     stage_ms, timed_frames = r.stage_times_total()
+    if stage_pass is not None:
+        stage_ms, timed_frames = stage_pass
     cnt = r.counters()
     assert cnt["frames"] == args.steps, cnt
     st = r.stats()
@@ -337,7 +361,7 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
                                                        r.stage_names)
 
     # ---- end to end through the public API with host buffers
-    r.set_flags(base_flags)
+    r.set_flags(base_flags | (N.FLAG_GRAPH if (args.launch == 'graph') else 0))
     e2e_steps = args.e2e_steps or max(10, args.steps // 4)
     host = torch.empty((w.height, w.width, 4), dtype=torch.uint8, pin_memory=True)
     host.copy_(bg.cpu())
@@ -571,6 +595,7 @@ def main():
     w = WORKLOADS[args.workload or (WORKLOAD if args.mode == "views" else "large_6m")]
     cfg_block = workload_config(w)
     cfg_block["binning"] = "sorted_keys" if args.sorted_keys else "placed"
+    cfg_block["launch"] = "cuda_graph" if (args.launch == 'graph') else "stream"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -96,6 +96,12 @@ typedef struct kt_gaussian2d {
 #define KT_GS_FLAG_KEEP_UNSORTED 0x8u    /* accepted for compatibility; the unsorted dumps are always
                                             available (rebuilt from the device's bin rectangles) */
 #define KT_GS_FLAG_TIMING 0x10u          /* record CUDA events around every stage */
+#define KT_GS_FLAG_GRAPH 0x40u          /* replay each path's frame as a captured CUDA graph: the
+                                            kernels of a frame are captured once (again when the image
+                                            pointer, scene, buffers, Gaussian count or flags change)
+                                            and launched with one call; the camera is copied into
+                                            device memory before each replay. Stage timers are not
+                                            recorded in this mode */
 #define KT_GS_FLAG_SORTED_KEYS 0x20u     /* bin through the reference's stage structure: scan of the
                                             counts in index order, one (bin << depth_bits | depth, index)
                                             pair per bin and Gaussian, radix sort of the pairs, boundary

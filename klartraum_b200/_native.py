@@ -27,6 +27,7 @@ FLAG_ASYNC = 0x4
 FLAG_KEEP_UNSORTED = 0x8
 FLAG_TIMING = 0x10
 FLAG_SORTED_KEYS = 0x20
+FLAG_GRAPH = 0x40
 
 STAGE_PROJECTED = 0
 STAGE_TILE_COUNTS = 1

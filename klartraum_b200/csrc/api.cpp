@@ -49,6 +49,21 @@ namespace {
 constexpr uint64_t kMaxKeyCapacity = 0xFFFFF000ull;  // values and ranges are 32-bit
 constexpr uint32_t kDepthPasses = 4;                  // 8-bit passes over <= 31 depth bits
 
+// What a captured frame graph bakes in (kernel arguments and buffer addresses).
+struct GraphKey {
+    const void* img = nullptr;
+    uint64_t n = 0;
+    uint64_t cap = 0;
+    uint32_t flags = 0;
+    int src = 0;
+    uint64_t scene_gen = 0;
+    uint64_t buf_gen = 0;
+    bool operator==(const GraphKey& o) const {
+        return img == o.img && n == o.n && cap == o.cap && flags == o.flags && src == o.src &&
+               scene_gen == o.scene_gen && buf_gen == o.buf_gen;
+    }
+};
+
 struct PathWs {
     uint64_t n_alloc = 0;
     uint64_t cap = 0;
@@ -77,6 +92,12 @@ struct PathWs {
     uint64_t key_n = 0;
     uint32_t scan_epoch = 0;
     bool keys_frame = false;  // the path's last frame took the keys path
+    // frame graph (KT_GS_FLAG_GRAPH)
+    cudaGraphExec_t gexec = nullptr;
+    GraphKey gkey{};
+    CamParams* cam_dev = nullptr;       // camera read by the replayed projection
+    cudaStream_t cap_stream = nullptr;  // capture stream
+    uint64_t buf_gen = 0;               // bumped whenever a buffer of the path is reallocated
     FrameCtl* ctl = nullptr;
     FrameCtl* ctl_depth = nullptr;
     FrameCtl* host_ctl = nullptr;  // pinned copy of the last frame's control block
@@ -122,6 +143,7 @@ struct kt_gs_ctx {
     uint64_t n = 0;
     bool has_scene = false;
     GridParams gp{};
+    uint64_t scene_gen = 0;  // bumped by every scene upload (frame graphs bake the scene's address)
     std::vector<PathWs> paths;
 };
 
@@ -191,6 +213,11 @@ void free_path(PathWs& w) {
     dfree(w.keys[0]); dfree(w.keys[1]); dfree(w.vals[0]); dfree(w.vals[1]); dfree(w.key_status);
     dfree(w.key_table); dfree(w.offsets); dfree(w.scan_status);
     w.key_cap = w.key_n = 0;
+    if (w.gexec) cudaGraphExecDestroy(w.gexec);
+    w.gexec = nullptr;
+    dfree(w.cam_dev);
+    if (w.cap_stream) cudaStreamDestroy(w.cap_stream);
+    w.cap_stream = nullptr;
     dfree(w.img); dfree(w.g2d);
     if (w.host_ctl) cudaFreeHost(w.host_ctl);
     w.host_ctl = nullptr;
@@ -230,6 +257,7 @@ kt_status ensure_status(kt_gs_ctx* c, PathWs& w) {
     if (need <= w.status_words) return KT_OK;
     dfree(w.sort_status);
     dfree(w.sort_table);
+    ++w.buf_gen;
     w.status_words = 0;
     const size_t table = sort_table_words(w.n_alloc);
     KT_TRY_CUDA(c, cudaMalloc(&w.sort_table, sizeof(uint32_t) * table));
@@ -244,6 +272,7 @@ kt_status ensure_n(kt_gs_ctx* c, PathWs& w, uint64_t n) {
     if (n <= w.n_alloc) return KT_OK;
     dfree(w.rec); dfree(w.counts); dfree(w.rect); dfree(w.srect); dfree(w.depth); dfree(w.gsort[0]);
     dfree(w.gsort[1]);
+    ++w.buf_gen;
     w.n_alloc = 0;
     const uint64_t m = std::max<uint64_t>(n, 1);
     KT_TRY_CUDA(c, cudaMalloc(&w.rec, sizeof(float4) * 3 * m));
@@ -264,6 +293,7 @@ kt_status ensure_cap(kt_gs_ctx* c, PathWs& w, uint64_t cap) {
                                             " exceeds the 32-bit index range of the key buffers");
     cap = std::min<uint64_t>(((cap + kSortTile - 1) / kSortTile) * kSortTile, kMaxKeyCapacity);
     dfree(w.pairs);
+    ++w.buf_gen;
     w.cap = 0;
     KT_TRY_CUDA(c, cudaMalloc(&w.pairs, sizeof(uint32_t) * cap));
     w.cap = cap;
@@ -273,6 +303,7 @@ kt_status ensure_cap(kt_gs_ctx* c, PathWs& w, uint64_t cap) {
 // Buffers of the reference-structured path, sized for the path's capacity and n Gaussians.
 kt_status ensure_keys(kt_gs_ctx* c, PathWs& w, uint64_t n) {
     if (w.key_cap < w.cap) {
+        ++w.buf_gen;
         dfree(w.keys[0]); dfree(w.keys[1]); dfree(w.vals[0]); dfree(w.vals[1]);
         dfree(w.key_status); dfree(w.key_table);
         w.key_cap = 0;
@@ -288,6 +319,7 @@ kt_status ensure_keys(kt_gs_ctx* c, PathWs& w, uint64_t n) {
         w.key_cap = w.cap;
     }
     if (w.key_n < n) {
+        ++w.buf_gen;
         dfree(w.offsets); dfree(w.scan_status);
         w.key_n = 0;
         const uint64_t chunks = (n + kScanChunk - 1) / kScanChunk;
@@ -350,64 +382,138 @@ kt_status drain_slot(kt_gs_ctx* c, PathWs& w, int slot) {
     return KT_OK;
 }
 
-// Enqueue one frame on `stream`. Does not wait.
-// The reference-structured frame: project -> scan + key emission in index order -> plan ->
-// radix sort of (key, value) pairs -> boundary search for the bin ranges -> rasterise.
-kt_status enqueue_keys_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* cam, uchar4* img,
-                             cudaStream_t stream, cudaEvent_t* ev, uint64_t n) {
-    const bool timed = ev != nullptr;
-    kt_status st = ensure_keys(c, w, std::max<uint64_t>(n, 1));
-    if (st != KT_OK) return st;
-    const uint32_t passes = key_passes(c);
-    if (++w.scan_epoch > kEpochMax) {
-        KT_TRY_CUDA(c, cudaMemsetAsync(w.scan_status, 0,
-                                       sizeof(unsigned long long) * ((w.key_n + kScanChunk - 1) / kScanChunk),
-                                       stream));
-        w.scan_epoch = 1;
-    }
-    if (w.key_epoch + passes + 1 > kEpochMax) {
-        KT_TRY_CUDA(c, cudaMemsetAsync(w.key_status, 0, sizeof(unsigned long long) * sort_status_words(w.key_cap),
-                                       stream));
-        w.key_epoch = 0;
-    }
-    const uint32_t epoch0 = w.key_epoch + 1;
-    w.key_epoch += passes;
-    FrameBufs fb = frame_bufs(w);
-    SortIO io{};
-    io.keys[0] = w.keys[0];
-    io.keys[1] = w.keys[1];
-    io.vals[0] = w.vals[0];
-    io.vals[1] = w.vals[1];
+// What one frame needs besides its buffers: the placement split and the look-back epochs.
+struct FramePlan {
+    bool keys = false;          // reference-structured binning (KT_GS_FLAG_SORTED_KEYS)
+    PlaceGeom pg{};             // placement split (default path)
+    uint32_t sort_epoch0 = 1;   // depth-sort passes (default path)
+    uint32_t scan_epoch = 1;    // keys path: scan
+    uint32_t key_epoch0 = 1;    // keys path: sort passes
+    bool clear_status = false;  // graph replays clear the look-back words at the frame's start
+};
 
+// Allocations and look-back epochs of a frame. Never called inside a stream capture.
+kt_status prepare_frame(kt_gs_ctx* c, PathWs& w, uint64_t n, bool graph, FramePlan& fp, cudaStream_t stream) {
+    fp.keys = (c->cfg.flags & KT_GS_FLAG_SORTED_KEYS) != 0;
+    fp.clear_status = graph;
+    if (fp.keys) {
+        kt_status st = ensure_keys(c, w, std::max<uint64_t>(n, 1));
+        if (st != KT_OK) return st;
+        if (graph) return KT_OK;  // fixed epochs, words cleared by the graph
+        const uint32_t passes = key_passes(c);
+        if (++w.scan_epoch > kEpochMax) {
+            KT_TRY_CUDA(c, cudaMemsetAsync(w.scan_status, 0,
+                                           sizeof(unsigned long long) * ((w.key_n + kScanChunk - 1) / kScanChunk),
+                                           stream));
+            w.scan_epoch = 1;
+        }
+        if (w.key_epoch + passes + 1 > kEpochMax) {
+            KT_TRY_CUDA(c, cudaMemsetAsync(w.key_status, 0,
+                                           sizeof(unsigned long long) * sort_status_words(w.key_cap), stream));
+            w.key_epoch = 0;
+        }
+        fp.scan_epoch = w.scan_epoch;
+        fp.key_epoch0 = w.key_epoch + 1;
+        w.key_epoch += passes;
+        return KT_OK;
+    }
+    KT_TRY_CUDA(c, place_geometry(c->gp, n, &fp.pg));
+    if (fp.pg.table_words > w.pair_table_words) {
+        dfree(w.pair_table);
+        w.pair_table_words = 0;
+        KT_TRY_CUDA(c, cudaMalloc(&w.pair_table, sizeof(uint32_t) * fp.pg.table_words));
+        w.pair_table_words = fp.pg.table_words;
+        ++w.buf_gen;
+    }
+    if (graph) return KT_OK;
+    if (w.sort_epoch + kDepthPasses + 1 > kEpochMax) {
+        KT_TRY_CUDA(c, cudaMemsetAsync(w.sort_status, 0, sizeof(unsigned long long) * w.status_words, stream));
+        w.sort_epoch = 0;
+    }
+    fp.sort_epoch0 = w.sort_epoch + 1;
+    w.sort_epoch += kDepthPasses;
+    return KT_OK;
+}
+
+// The kernels and copies of one frame on `stream`: no allocation and no host wait, so the
+// sequence can be captured into a CUDA graph. `ev` (may be null) receives the stage events.
+// The camera comes from `cam_dev` (device memory) when it is not null, else from `cam`.
+//   default: init -> K1 -> depth keys -> plan -> depth passes -> rectangles in depth order + pair
+//            counts -> prefix over chunks + bin ranges -> placement + totals -> K6
+//   keys:    init -> K1 -> scan + key emission -> plan + key sort passes -> boundary search ->
+//            totals -> K6
+kt_status record_frame(kt_gs_ctx* c, PathWs& w, Source src, uint64_t n, const CamParams* cam,
+                       const CamParams* cam_dev, uchar4* img, cudaStream_t stream, cudaEvent_t* ev,
+                       const FramePlan& fp) {
+    const bool timed = ev != nullptr;
+    FrameBufs fb = frame_bufs(w);
+    if (fp.clear_status) {
+        if (fp.keys) {
+            KT_TRY_CUDA(c, cudaMemsetAsync(w.scan_status, 0,
+                                           sizeof(unsigned long long) * ((w.key_n + kScanChunk - 1) / kScanChunk),
+                                           stream));
+            KT_TRY_CUDA(c, cudaMemsetAsync(w.key_status, 0,
+                                           sizeof(unsigned long long) * sort_status_words(w.key_cap), stream));
+        } else {
+            KT_TRY_CUDA(c, cudaMemsetAsync(w.sort_status, 0, sizeof(unsigned long long) * w.status_words, stream));
+        }
+    }
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[0], stream));
     KT_TRY_CUDA(c, launch_frame_init(w.ctl, w.ctl_depth, w.ranges, ntiles(c), stream));
     if (src == Source::Scene) {
         SceneDev sc{c->pos, c->rot, c->scale, c->sh, c->nplanes, c->deg, c->n};
-        KT_TRY_CUDA(c, launch_project_count(sc, *cam, c->gp, fb, stream));
+        const CamParams none{};
+        KT_TRY_CUDA(c, launch_project_count(sc, cam ? *cam : none, cam_dev, c->gp, fb, stream));
     } else {
         KT_TRY_CUDA(c, launch_load_projected(w.g2d, n, c->gp, fb, stream));
     }
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[1], stream));
-    KT_TRY_CUDA(c, launch_key_scan_emit(fb, c->gp, n, w.scan_epoch, passes, stream));
-    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[2], stream));
-    KT_TRY_CUDA(c, launch_plan(w.ctl, w.cap, passes, 0, stream));
-    for (uint32_t p = 0; p < passes; ++p)
-        KT_TRY_CUDA(c, launch_sort_pass(io, w.ctl, w.key_status, w.key_table, p, epoch0 + p, w.cap, false, stream));
-    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[3], stream));
-    KT_TRY_CUDA(c, launch_key_ranges(io, w.ctl, w.ranges, w.cap, stream));
-    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[4], stream));
+    SortIO io{};
+    if (fp.keys) {
+        const uint32_t passes = key_passes(c);
+        io.keys[0] = w.keys[0];
+        io.keys[1] = w.keys[1];
+        io.vals[0] = w.vals[0];
+        io.vals[1] = w.vals[1];
+        KT_TRY_CUDA(c, launch_key_scan_emit(fb, c->gp, n, fp.scan_epoch, passes, stream));
+        if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[2], stream));
+        KT_TRY_CUDA(c, launch_plan(w.ctl, w.cap, passes, 0, stream));
+        for (uint32_t p = 0; p < passes; ++p)
+            KT_TRY_CUDA(c, launch_sort_pass(io, w.ctl, w.key_status, w.key_table, p, fp.key_epoch0 + p, w.cap,
+                                            false, stream));
+        if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[3], stream));
+        KT_TRY_CUDA(c, launch_key_ranges(io, w.ctl, w.ranges, w.cap, stream));
+        if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[4], stream));
+    } else {
+        io.vals[0] = w.pairs;  // the rasteriser reads Gaussian indices
+        SortIO io_depth{};
+        io_depth.keys[0] = w.gsort[0];
+        io_depth.keys[1] = w.gsort[1];
+        // Gaussians by depth (stable: ties keep index order)
+        KT_TRY_CUDA(c, launch_depth_keys(fb, n, stream));
+        KT_TRY_CUDA(c, launch_plan(w.ctl_depth, n, kDepthPasses, 0, stream));
+        for (uint32_t p = 0; p < kDepthPasses; ++p)
+            KT_TRY_CUDA(c, launch_sort_pass(io_depth, w.ctl_depth, w.sort_status, w.sort_table, p,
+                                            fp.sort_epoch0 + p, n, true, stream));
+        if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[2], stream));
+        // pairs per (chunk of depth order, bin); their prefix over chunks and the bin ranges
+        KT_TRY_CUDA(c, launch_pair_count(fb, c->gp, fp.pg, n, w.pair_table, stream));
+        if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[3], stream));
+        KT_TRY_CUDA(c, launch_pair_ranges(fb, c->gp, fp.pg, n, w.pair_table, stream));
+        if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[4], stream));
+        // every pair at its place in bin order (depth order within a bin)
+        KT_TRY_CUDA(c, launch_pair_place(fb, c->gp, fp.pg, n, w.pair_table, stream));
+    }
     KT_TRY_CUDA(c, launch_frame_totals(w.ctl, w.ctl_depth, w.totals, stream));
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[5], stream));
     KT_TRY_CUDA(c, launch_rasterize(w.rec, io, w.ranges, w.ctl, c->gp, img,
                                     (c->cfg.flags & KT_GS_FLAG_EXIT_PER_ELEMENT) != 0, stream));
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[6], stream));
     KT_TRY_CUDA(c, cudaMemcpyAsync(w.host_ctl, w.ctl, kCtlHeaderBytes, cudaMemcpyDeviceToHost, stream));
-    KT_TRY_CUDA(c, cudaEventRecord(w.done_ev, stream));
-    w.have_frame = true;
-    w.frame_n = n;
     return KT_OK;
 }
 
+// Enqueue one frame on `stream`. Does not wait.
 kt_status enqueue_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* cam, uchar4* img,
                         cudaStream_t stream) {
     const uint64_t n = src == Source::Scene ? c->n : w.g2d_n;
@@ -425,62 +531,55 @@ kt_status enqueue_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* ca
         w.ring_last = slot;
         w.ring_next = (slot + 1) % PathWs::kRing;
     }
-    w.keys_frame = (c->cfg.flags & KT_GS_FLAG_SORTED_KEYS) != 0;
-    if (w.keys_frame) return enqueue_keys_frame(c, w, src, cam, img, stream, ev, n);
-    // work split of the pair placement, and its table
-    PlaceGeom pg{};
-    KT_TRY_CUDA(c, place_geometry(c->gp, n, &pg));
-    if (pg.table_words > w.pair_table_words) {
-        dfree(w.pair_table);
-        w.pair_table_words = 0;
-        KT_TRY_CUDA(c, cudaMalloc(&w.pair_table, sizeof(uint32_t) * pg.table_words));
-        w.pair_table_words = pg.table_words;
-    }
-    // look-back epochs of the depth sort; a wrap clears the status words
-    if (w.sort_epoch + kDepthPasses + 1 > kEpochMax) {
-        KT_TRY_CUDA(c, cudaMemsetAsync(w.sort_status, 0, sizeof(unsigned long long) * w.status_words, stream));
-        w.sort_epoch = 0;
-    }
-    const uint32_t sort_epoch0 = w.sort_epoch + 1;
-    w.sort_epoch += kDepthPasses;
-
-    FrameBufs fb = frame_bufs(w);
-    SortIO io{};  // pairs by bin, as the rasteriser reads them: Gaussian indices
-    io.vals[0] = w.pairs;
-    SortIO io_depth{};  // Gaussians by depth
-    io_depth.keys[0] = w.gsort[0];
-    io_depth.keys[1] = w.gsort[1];
-
-    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[0], stream));
-    KT_TRY_CUDA(c, launch_frame_init(w.ctl, w.ctl_depth, w.ranges, ntiles(c), stream));
-    if (src == Source::Scene) {
-        SceneDev sc{c->pos, c->rot, c->scale, c->sh, c->nplanes, c->deg, c->n};
-        KT_TRY_CUDA(c, launch_project_count(sc, *cam, c->gp, fb, stream));
-    } else {
-        KT_TRY_CUDA(c, launch_load_projected(w.g2d, n, c->gp, fb, stream));
-    }
-    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[1], stream));
-    // Gaussians by depth (stable: ties keep index order)
-    KT_TRY_CUDA(c, launch_depth_keys(fb, n, stream));
-    KT_TRY_CUDA(c, launch_plan(w.ctl_depth, n, kDepthPasses, 0, stream));
-    for (uint32_t p = 0; p < kDepthPasses; ++p)
-        KT_TRY_CUDA(c, launch_sort_pass(io_depth, w.ctl_depth, w.sort_status, w.sort_table, p, sort_epoch0 + p, n,
-                                        true, stream));
-    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[2], stream));
-    // pairs per (chunk of depth order, bin); their prefix over chunks and the bin ranges
-    KT_TRY_CUDA(c, launch_pair_count(fb, c->gp, pg, n, w.pair_table, stream));
-    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[3], stream));
-    KT_TRY_CUDA(c, launch_pair_ranges(fb, c->gp, pg, n, w.pair_table, stream));
-    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[4], stream));
-    // every pair at its place in bin order (depth order within a bin)
-    KT_TRY_CUDA(c, launch_pair_place(fb, c->gp, pg, n, w.pair_table, stream));
-    KT_TRY_CUDA(c, launch_frame_totals(w.ctl, w.ctl_depth, w.totals, stream));
-    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[5], stream));
-    KT_TRY_CUDA(c, launch_rasterize(w.rec, io, w.ranges, w.ctl, c->gp, img,
-                                    (c->cfg.flags & KT_GS_FLAG_EXIT_PER_ELEMENT) != 0, stream));
-    if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[6], stream));
-    KT_TRY_CUDA(c, cudaMemcpyAsync(w.host_ctl, w.ctl, kCtlHeaderBytes, cudaMemcpyDeviceToHost, stream));
+    FramePlan fp;
+    kt_status s = prepare_frame(c, w, n, false, fp, stream);
+    if (s != KT_OK) return s;
+    w.keys_frame = fp.keys;
+    if ((s = record_frame(c, w, src, n, cam, nullptr, img, stream, ev, fp)) != KT_OK) return s;
     KT_TRY_CUDA(c, cudaEventRecord(w.done_ev, stream));
+    w.have_frame = true;
+    w.frame_n = n;
+    return KT_OK;
+}
+
+// Enqueue one frame as a replay of the path's captured frame graph (KT_GS_FLAG_GRAPH). The graph
+// is captured again when anything baked into it changed: the image pointer, the scene or any
+// buffer of the path, the Gaussian count, the flags or the source. Only the camera changes
+// between replays; it is copied into the path's device camera before the launch.
+kt_status enqueue_graph_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* cam, uchar4* img,
+                              cudaStream_t stream) {
+    const uint64_t n = src == Source::Scene ? c->n : w.g2d_n;
+    FramePlan fp;
+    kt_status s = prepare_frame(c, w, n, true, fp, stream);
+    if (s != KT_OK) return s;
+    if (!w.cam_dev) KT_TRY_CUDA(c, cudaMalloc(&w.cam_dev, sizeof(CamParams)));
+    if (!w.cap_stream) KT_TRY_CUDA(c, cudaStreamCreateWithFlags(&w.cap_stream, cudaStreamNonBlocking));
+    const uint32_t kFlagsBaked = ~(KT_GS_FLAG_ASYNC | KT_GS_FLAG_TIMING | KT_GS_FLAG_NO_AUTOGROW);
+    const GraphKey key{img, n, w.cap, c->cfg.flags & kFlagsBaked, (int)src, c->scene_gen, w.buf_gen};
+    if (!w.gexec || !(key == w.gkey)) {
+        if (w.gexec) cudaGraphExecDestroy(w.gexec);
+        w.gexec = nullptr;
+        KT_TRY_CUDA(c, cudaStreamBeginCapture(w.cap_stream, cudaStreamCaptureModeThreadLocal));
+        const kt_status rs = record_frame(c, w, src, n, nullptr, w.cam_dev, img, w.cap_stream, nullptr, fp);
+        cudaGraph_t g = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(w.cap_stream, &g);  // ends the capture in every case
+        if (rs != KT_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rs;
+        }
+        KT_TRY_CUDA(c, e);
+        const cudaError_t ei = cudaGraphInstantiate(&w.gexec, g, 0);
+        cudaGraphDestroy(g);
+        KT_TRY_CUDA(c, ei);
+        w.gkey = key;
+    }
+    if (cam) {  // pageable source: the copy is staged before the call returns
+        KT_TRY_CUDA(c, cudaMemcpyAsync(w.cam_dev, cam, sizeof(CamParams), cudaMemcpyHostToDevice, stream));
+    }
+    KT_TRY_CUDA(c, cudaGraphLaunch(w.gexec, stream));
+    KT_TRY_CUDA(c, cudaEventRecord(w.done_ev, stream));
+    w.keys_frame = fp.keys;
+    w.timed = false;
     w.have_frame = true;
     w.frame_n = n;
     return KT_OK;
@@ -519,7 +618,9 @@ kt_status render_impl(kt_gs_ctx* c, uint32_t path, Source src, const kt_camera_m
     if (cam) cp = make_cam(cam);
     const bool async = (c->cfg.flags & KT_GS_FLAG_ASYNC) != 0;
     for (int attempt = 0; attempt < 4; ++attempt) {
-        if ((s = enqueue_frame(c, w, src, cam ? &cp : nullptr, img, stream)) != KT_OK) return s;
+        s = (c->cfg.flags & KT_GS_FLAG_GRAPH) ? enqueue_graph_frame(c, w, src, cam ? &cp : nullptr, img, stream)
+                                              : enqueue_frame(c, w, src, cam ? &cp : nullptr, img, stream);
+        if (s != KT_OK) return s;
         if (async) return KT_OK;
         s = check_frame(c, w);
         if (s != KT_OK) {
@@ -554,6 +655,7 @@ kt_status upload_scene(kt_gs_ctx* c, const kt_gaussian3d* src, bool src_on_devic
     KT_TRY_CUDA(c, cudaSetDevice(c->device));
     dfree(c->pos); dfree(c->rot); dfree(c->scale); dfree(c->sh);
     c->has_scene = false;
+    ++c->scene_gen;
     c->n = n;
     c->deg = deg;
     c->nplanes = (uint32_t)((3 * (deg + 1) * (deg + 1) + 3) / 4);
@@ -727,6 +829,7 @@ kt_status kt_gs_render_projected(kt_gs_ctx* c, const kt_gaussian2d* host, uint64
     KT_TRY_CUDA(c, cudaSetDevice(c->device));
     PathWs& w = c->paths[path];
     if (n > w.g2d_n || !w.g2d) {
+        ++w.buf_gen;
         dfree(w.g2d);
         KT_TRY_CUDA(c, cudaMalloc(&w.g2d, sizeof(kt_gaussian2d) * std::max<uint64_t>(n, 1)));
     }

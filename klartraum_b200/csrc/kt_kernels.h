@@ -28,8 +28,9 @@ constexpr int kSortTile = 4096;   // keys per sort tile
 constexpr int kScanChunk = 2048;  // Gaussians per scan/emit CTA (keys path)
 
 // project.cu (compiled with -fmad=false)
-cudaError_t launch_project_count(const SceneDev& sc, const CamParams& cam, const GridParams& gp,
-                                 const FrameBufs& fb, cudaStream_t stream);
+// cam_dev: when not null the kernel reads the camera from device memory (graph replays)
+cudaError_t launch_project_count(const SceneDev& sc, const CamParams& cam, const CamParams* cam_dev,
+                                 const GridParams& gp, const FrameBufs& fb, cudaStream_t stream);
 cudaError_t launch_load_projected(const float* d_g2d, uint64_t n, const GridParams& gp,
                                   const FrameBufs& fb, cudaStream_t stream);
 cudaError_t launch_pack_scene(const float* d_aos, uint64_t n, float4* pos, float4* rot,

@@ -136,9 +136,12 @@ __device__ __forceinline__ void store_outputs(uint64_t i, float px, float py, fl
 
 // --------------------------------------------------------------------- K1
 
-template <int DEG>
-__global__ void __launch_bounds__(256) k_project_count(SceneDev sc, CamParams cam, GridParams gp,
-                                                        FrameBufs fb) {
+// DEV_CAM: the camera comes from device memory (a captured frame graph replayed with new cameras)
+// instead of the kernel parameters.
+template <int DEG, bool DEV_CAM>
+__global__ void __launch_bounds__(256) k_project_count(SceneDev sc, CamParams cam_arg, const CamParams* cam_dev,
+                                                        GridParams gp, FrameBufs fb) {
+    const CamParams& cam = DEV_CAM ? *cam_dev : cam_arg;
     constexpr int kCoef = (DEG + 1) * (DEG + 1);
     constexpr int kPlanes = (3 * kCoef + 3) / 4;
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -311,15 +314,24 @@ __global__ void __launch_bounds__(256) k_pack_scene(const float* __restrict__ ao
 
 // ------------------------------------------------------------------ launchers
 
-cudaError_t launch_project_count(const SceneDev& sc, const CamParams& cam, const GridParams& gp,
-                                 const FrameBufs& fb, cudaStream_t stream) {
+cudaError_t launch_project_count(const SceneDev& sc, const CamParams& cam, const CamParams* cam_dev,
+                                 const GridParams& gp, const FrameBufs& fb, cudaStream_t stream) {
     if (sc.n == 0) return cudaSuccess;
     const dim3 grid((unsigned)((sc.n + 255) / 256));
-    switch (sc.deg) {
-        case 0: k_project_count<0><<<grid, 256, 0, stream>>>(sc, cam, gp, fb); break;
-        case 1: k_project_count<1><<<grid, 256, 0, stream>>>(sc, cam, gp, fb); break;
-        case 2: k_project_count<2><<<grid, 256, 0, stream>>>(sc, cam, gp, fb); break;
-        default: k_project_count<3><<<grid, 256, 0, stream>>>(sc, cam, gp, fb); break;
+    if (cam_dev) {
+        switch (sc.deg) {
+            case 0: k_project_count<0, true><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
+            case 1: k_project_count<1, true><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
+            case 2: k_project_count<2, true><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
+            default: k_project_count<3, true><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
+        }
+    } else {
+        switch (sc.deg) {
+            case 0: k_project_count<0, false><<<grid, 256, 0, stream>>>(sc, cam, nullptr, gp, fb); break;
+            case 1: k_project_count<1, false><<<grid, 256, 0, stream>>>(sc, cam, nullptr, gp, fb); break;
+            case 2: k_project_count<2, false><<<grid, 256, 0, stream>>>(sc, cam, nullptr, gp, fb); break;
+            default: k_project_count<3, false><<<grid, 256, 0, stream>>>(sc, cam, nullptr, gp, fb); break;
+        }
     }
     return cudaGetLastError();
 }

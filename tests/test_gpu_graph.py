@@ -1,0 +1,97 @@
+"""Frame graphs (KT_GS_FLAG_GRAPH): a path's frame captured once as a CUDA graph and replayed with
+new cameras must draw exactly what the stream-launched frame draws, and must be captured again
+when anything it bakes in changes (image pointer, scene, buffers after a capacity growth)."""
+
+import numpy as np
+import pytest
+
+from klartraum_b200 import Renderer, make_scene, native as N, orbit_views
+
+from helpers import background
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+W, H = 640, 360
+
+
+def _scene(n=60000, seed=21):
+    return make_scene("single_1m", n=n, seed=seed)
+
+
+@pytest.mark.parametrize("extra", [0, N.FLAG_SORTED_KEYS], ids=["placed", "sorted_keys"])
+def test_graph_replays_match_stream_frames(extra):
+    g3d = _scene()
+    cams = orbit_views(5, 2.5, W, H, fovy_deg=60.0)
+    bg = torch.from_numpy(background(H, W, "random")).cuda()
+    ref, got = [], []
+    for flags, out in ((extra, ref), (extra | N.FLAG_GRAPH, got)):
+        r = Renderer(W, H, bin_size=16, sh_degree=3, flags=flags)
+        r.set_gaussians(g3d)
+        img = bg.clone()
+        for c in cams:  # the same image buffer every frame: one capture, replays after it
+            img.copy_(bg)
+            r.render(c, img)
+            out.append(img.clone())
+        r.close()
+    for a, b in zip(ref, got):
+        assert torch.equal(a, b)
+
+
+def test_graph_recaptures_on_new_image_scene_and_capacity():
+    g3d, g3d_b = _scene(seed=21), _scene(n=40000, seed=22)
+    cams = orbit_views(3, 2.5, W, H, fovy_deg=60.0)
+    bg = torch.from_numpy(background(H, W)).cuda()
+
+    def plain(scene, cam):
+        r = Renderer(W, H, bin_size=16, sh_degree=3)
+        r.set_gaussians(scene)
+        img = bg.clone()
+        r.render(cam, img)
+        r.close()
+        return img
+
+    # a capacity far too small: the first replay overflows, the buffers grow, the graph is
+    # captured again and the frame is drawn
+    r = Renderer(W, H, bin_size=16, sh_degree=3, flags=N.FLAG_GRAPH, key_capacity=4096)
+    r.set_gaussians(g3d)
+    a = bg.clone()
+    r.render(cams[0], a)
+    assert r.stats()["key_capacity"] >= r.stats()["num_keys"] > 4096
+    assert torch.equal(a, plain(g3d, cams[0]))
+    # another output buffer
+    b = bg.clone()
+    r.render(cams[1], b)
+    assert torch.equal(b, plain(g3d, cams[1]))
+    # another scene
+    r.set_gaussians(g3d_b)
+    c = bg.clone()
+    r.render(cams[2], c)
+    assert torch.equal(c, plain(g3d_b, cams[2]))
+    # back to the first buffer, async replays, one sync at the end
+    r.set_flags(N.FLAG_GRAPH | N.FLAG_ASYNC)
+    for _ in range(20):
+        a.copy_(bg)
+        r.render(cams[1], a)
+    r.sync()
+    assert torch.equal(a, plain(g3d_b, cams[1]))
+    assert r.counters()["frames"] >= 20
+    r.close()
+
+
+def test_graph_render_host():
+    g3d = _scene(n=20000)
+    cam = orbit_views(1, 2.5, W, H, fovy_deg=60.0)[0]
+    bgh = background(H, W, "random")
+    outs = []
+    for flags in (0, N.FLAG_GRAPH):
+        r = Renderer(W, H, bin_size=16, sh_degree=3, flags=flags)
+        r.set_gaussians(g3d)
+        host = bgh.copy()
+        r.render_host(cam, host)
+        host2 = bgh.copy()
+        r.render_host(cam, host2)  # the second call replays
+        outs.append((host, host2))
+        r.close()
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
