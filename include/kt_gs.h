@@ -239,6 +239,17 @@ kt_status kt_gs_spz_decode(const char* path, kt_gaussian3d* out, uint64_t capaci
                            uint32_t* sh_degree);
 
 /*
+ * Load a 3D Gaussian Splatting .ply file (binary little endian or ASCII; x y z, f_dc_0..2,
+ * opacity, scale_0..2, rot_0..3 with rot_0 = w) as loadPLYModel does
+ * (src/vulkan_gaussian_splatting.cpp:367-417): only Gaussians inside [-1.5, 1.5]^3, alpha =
+ * sigmoid(opacity), scale = exp, colour pre-baked as 0.5 + 0.282095 f_dc, higher SH zero.
+ */
+kt_status kt_gs_load_ply(kt_gs_ctx* ctx, const char* path);
+
+/* The same decode into host records; with out == NULL only *count (Gaussians kept) is set. */
+kt_status kt_gs_ply_decode(const char* path, kt_gaussian3d* out, uint64_t capacity, uint64_t* count);
+
+/*
  * Render one frame. `cam` is host memory (the per-path camera UBO, uniformbufferobject.hpp:67-70).
  * `d_rgba8` is a device image of width*height RGBA8 pixels, row-major, row 0 at the top; it
  * is read-modify-written: out = clamp(in + vec4(C,1)*(1-T)) (gsplat_binned_splatting.comp:119-121).

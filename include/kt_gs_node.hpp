@@ -199,6 +199,10 @@ public:
         if (ctx) kt_gs_destroy(ctx);
     }
 
+    // The reference's scene loaders (src/vulkan_gaussian_splatting.cpp:322-417), replacing the scene.
+    void loadSPZModel(const std::string& path) { ktCheck(kt_gs_load_spz(ctx, path.c_str()), ctx); }
+    void loadPLYModel(const std::string& path) { ktCheck(kt_gs_load_ply(ctx, path.c_str()), ctx); }
+
     // src/vulkan_gaussian_splatting.cpp:220-232
     void checkInput(ComputeGraphElementPtr input, int index = 0) override {
         if (index == 0 && !std::dynamic_pointer_cast<ImageViewSrc>(input))

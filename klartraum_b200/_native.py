@@ -49,7 +49,7 @@ EXPORTED_SYMBOLS = [
     "kt_gs_set_gaussians_device", "kt_gs_load_spz", "kt_gs_render", "kt_gs_render_host",
     "kt_gs_render_batch", "kt_gs_render_projected", "kt_gs_sync", "kt_gs_frame_stats",
     "kt_gs_debug_dump", "kt_gs_stage_times", "kt_gs_stage_times_total", "kt_gs_radix_sort_pairs",
-    "kt_gs_set_flags", "kt_gs_counters_take", "kt_gs_spz_decode",
+    "kt_gs_set_flags", "kt_gs_counters_take", "kt_gs_spz_decode", "kt_gs_load_ply", "kt_gs_ply_decode",
 ]
 
 
@@ -129,6 +129,8 @@ def load() -> C.CDLL:
         "kt_gs_set_gaussians_device": (C.c_int, [vp, vp, u64, vp]),
         "kt_gs_load_spz": (C.c_int, [vp, C.c_char_p]),
         "kt_gs_spz_decode": (C.c_int, [C.c_char_p, vp, C.c_uint64, C.POINTER(C.c_uint64), C.POINTER(u32)]),
+        "kt_gs_load_ply": (C.c_int, [vp, C.c_char_p]),
+        "kt_gs_ply_decode": (C.c_int, [C.c_char_p, vp, C.c_uint64, C.POINTER(C.c_uint64)]),
         "kt_gs_render": (C.c_int, [vp, vp, vp, u32, vp]),
         "kt_gs_render_host": (C.c_int, [vp, vp, vp, u32, vp]),
         "kt_gs_render_batch": (C.c_int, [vp, vp, u32, vp, vp]),
@@ -206,3 +208,18 @@ def spz_decode(path: str):
     if n.value:
         check(lib.kt_gs_spz_decode(path.encode(), out.ctypes.data, n.value, C.byref(n), C.byref(deg)))
     return out, deg.value
+
+
+def ply_decode(path: str):
+    """Decode a 3D Gaussian Splatting .ply file on the host (kt_gs_ply_decode)."""
+    import numpy as np
+
+    from .types import GAUSSIAN3D_DTYPE
+
+    lib = load()
+    n = C.c_uint64(0)
+    check(lib.kt_gs_ply_decode(path.encode(), None, 0, C.byref(n)))
+    out = np.zeros(n.value, GAUSSIAN3D_DTYPE)
+    if n.value:
+        check(lib.kt_gs_ply_decode(path.encode(), out.ctypes.data, n.value, C.byref(n)))
+    return out

@@ -38,6 +38,7 @@ SOURCES = {
     "sort_static.cu": [],
     "api.cpp": [],
     "spz.cpp": [],
+    "ply.cpp": [],
 }
 
 

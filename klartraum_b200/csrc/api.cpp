@@ -1105,6 +1105,22 @@ kt_status kt_gs_load_spz(kt_gs_ctx* c, const char* path) {
     return kt_gs_set_gaussians(c, g.data(), n);
 }
 
+kt_status kt_gs_load_ply(kt_gs_ctx* c, const char* path) {
+    if (!c || !path) return KT_ERR_ARG;
+    uint64_t n = 0;
+    kt_status s = kt_gs_ply_decode(path, nullptr, 0, &n);
+    if (s != KT_OK) return fail(c, s, std::string("cannot read ply file ") + path);
+    std::vector<kt_gaussian3d> g;
+    try {
+        g.resize(n);
+    } catch (const std::bad_alloc&) {
+        return fail(c, KT_ERR_NOMEM, "no host memory for the ply records");
+    }
+    s = kt_gs_ply_decode(path, g.data(), n, &n);
+    if (s != KT_OK) return fail(c, s, std::string("cannot decode ply file ") + path);
+    return kt_gs_set_gaussians(c, g.data(), n);
+}
+
 kt_status kt_gs_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* vals_in,
                                  uint64_t* keys_out, uint32_t* vals_out, uint64_t n,
                                  uint32_t key_bits, void* d_temp, size_t* temp_bytes,

@@ -81,6 +81,9 @@ class Renderer:
     def load_spz(self, path: str) -> None:
         self._check(self._lib.kt_gs_load_spz(self._ctx, path.encode()))
 
+    def load_ply(self, path: str) -> None:
+        self._check(self._lib.kt_gs_load_ply(self._ctx, path.encode()))
+
     @property
     def sh_degree(self) -> int:
         cfg = N.Config()
