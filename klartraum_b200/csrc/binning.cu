@@ -62,10 +62,11 @@ __global__ void k_frame_init(FrameCtl* ctl, FrameCtl* ctl_depth, uint2* ranges, 
 // histograms of the depth sort. Gaussians that touch no bin take the largest depth; they
 // emit nothing, so where they land does not matter.
 __global__ void __launch_bounds__(256) k_depth_keys(FrameBufs fb, uint64_t n) {
-    __shared__ uint32_t s_hist[4][256];
+    __shared__ uint32_t s_hist[8][4][256];  // per warp, per pass
     const FrameCtl* ctl = fb.ctl;
     FrameCtl* cd = fb.ctl_depth;
-    for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) (&s_hist[0][0])[i] = 0u;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < 8 * 4 * 256; i += blockDim.x) (&s_hist[0][0][0])[i] = 0u;
     __syncthreads();
     const uint32_t dmin = ctl->depth_min, dmax = ctl->depth_max;
     const bool any = dmax >= dmin;
@@ -74,23 +75,31 @@ __global__ void __launch_bounds__(256) k_depth_keys(FrameBufs fb, uint64_t n) {
     const uint32_t ibits = bits_for(n - 1);
     const uint32_t npass = (dbits + 7) / 8;
     unsigned long long* out = fb.gsort[0];
+    uint32_t (*hw)[256] = s_hist[warp];
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    const int lane = threadIdx.x & 31;
     const uint64_t n_up = (n + 31) & ~31ull;  // whole warps iterate together
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_up; i += stride) {
         const bool live = i < n;
         const uint32_t dk = live ? (fb.counts[i] != 0u ? fb.depth[i] - dmin : dtop) : 0u;
         if (live) out[i] = ((unsigned long long)dk << ibits) | i;
+        const uint32_t act = __ballot_sync(0xFFFFFFFFu, live);
         for (uint32_t p = 0; p < npass; ++p) {
-            // lanes with the same digit add once (the top digits of nearby depths collide)
-            const uint32_t d = live ? (dk >> (8 * p)) & 255u : 256u;
-            const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
-            if (live && lane == __ffs(peers) - 1) atomicAdd(&s_hist[p][d], (uint32_t)__popc(peers));
+            if (dbits - 8 * p == 1) {  // a one-bit digit (the top of a 25-bit range): two counts
+                const uint32_t ones = __ballot_sync(0xFFFFFFFFu, live && ((dk >> (8 * p)) & 1u));
+                if (lane == 0) {
+                    hw[p][0] += (uint32_t)__popc(act & ~ones);
+                    hw[p][1] += (uint32_t)__popc(ones);
+                }
+            } else if (live) {  // warp-private counters: only lanes of this warp collide
+                atomicAdd(&hw[p][(dk >> (8 * p)) & 255u], 1u);
+            }
         }
     }
     __syncthreads();
     for (uint32_t i = threadIdx.x; i < npass * 256; i += blockDim.x) {
-        const uint32_t v = (&s_hist[0][0])[i];
+        uint32_t v = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) v += (&s_hist[w][0][0])[i];
         if (v) atomicAdd(&(&cd->hist[0][0])[i], v);
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -190,9 +199,11 @@ cudaError_t launch_frame_init(FrameCtl* ctl, FrameCtl* ctl_depth, uint2* ranges,
 
 cudaError_t launch_depth_keys(const FrameBufs& fb, uint64_t n, cudaStream_t stream) {
     if (n == 0) return cudaSuccess;
-    uint64_t blocks = (n + 255) / 256;
-    const uint64_t cap = (uint64_t)device_sm_count() * 8;
+    // few CTAs with many Gaussians each: every CTA adds its histograms to the frame's once
+    uint64_t blocks = (n + 2047) / 2048;
+    const uint64_t cap = (uint64_t)device_sm_count() * 2;
     if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
     k_depth_keys<<<(unsigned)blocks, 256, 0, stream>>>(fb, n);
     return cudaGetLastError();
 }

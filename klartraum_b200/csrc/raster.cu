@@ -1,4 +1,4 @@
-// K6: front-to-back splatting, one CTA per 16x16 pixel block, one thread per pixel.
+// K6: front-to-back splatting, one CTA per 16x16 pixel block, two pixels per thread.
 //
 // Restates shaders/gsplat/gsplat_binned_splatting.comp:41-125 per pixel:
 //   a = exp(-0.5 * dot(d, covInv * d)) * alpha, d = pixel - mean (integer pixel coordinates)
@@ -9,8 +9,8 @@
 // loop still blends the first element past the last full batch (comp:104-117). With
 // KT_GS_FLAG_EXIT_PER_ELEMENT the test runs after every Gaussian.
 //
-// The CTA stages 256 sorted Gaussians at a time in shared memory (each thread gathers one
-// 48-B record by index) and leaves the list as soon as every pixel of the block is done or
+// The CTA stages 256 sorted Gaussians at a time in shared memory (each thread gathers two
+// 48-B records by index) and leaves the list as soon as every pixel of the block is done or
 // only owes the reference's one tail element, which it then blends from global memory.
 #include "kt_common.cuh"
 #include "kt_kernels.h"
@@ -18,7 +18,7 @@
 namespace kt {
 namespace {
 
-constexpr int kRasterThreads = 256;
+constexpr int kRasterThreads = 128;  // two pixels per thread
 constexpr int kBatch = 256;
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -49,6 +49,46 @@ __device__ __forceinline__ float4 quad_form(float4 cov, float alpha) {
     return make_float4(cov.x * k, (cov.y + cov.z) * k, cov.w * k, alpha);
 }
 
+// One pixel's blend state.
+struct Pix {
+    float C0, C1, C2, T;
+    bool done;       // finished (T below the threshold, or outside the image)
+    bool wait_tail;  // stopped at a 64-batch end; owes the reference's one tail element
+};
+
+__device__ __forceinline__ void write_pixel(uchar4* img, const GridParams& gp, uint32_t px, uint32_t py,
+                                            const Pix& p) {
+    uchar4* pix = &img[(uint64_t)py * gp.width + px];
+    const uchar4 in = *pix;
+    const float w = 1.0f - p.T;
+    float o0 = (float)in.x / 255.0f + p.C0 * w;
+    float o1 = (float)in.y / 255.0f + p.C1 * w;
+    float o2 = (float)in.z / 255.0f + p.C2 * w;
+    float o3 = (float)in.w / 255.0f + 1.0f * w;
+    o0 = fminf(fmaxf(o0, 0.0f), 1.0f);
+    o1 = fminf(fmaxf(o1, 0.0f), 1.0f);
+    o2 = fminf(fmaxf(o2, 0.0f), 1.0f);
+    o3 = fminf(fmaxf(o3, 0.0f), 1.0f);
+    *pix = make_uchar4((unsigned char)__float2uint_rn(o0 * 255.0f), (unsigned char)__float2uint_rn(o1 * 255.0f),
+                       (unsigned char)__float2uint_rn(o2 * 255.0f), (unsigned char)__float2uint_rn(o3 * 255.0f));
+}
+
+// The reference's tail loop from `preend` for a pixel that stopped at a 64-batch end: one element
+// unless that element raised T again.
+template <typename IndexAt>
+__device__ __forceinline__ void blend_tail(const float4* __restrict__ rec, IndexAt index_at, uint32_t preend,
+                                           uint32_t end, float fx, float fy, float tmin, Pix& p) {
+    for (uint32_t i = preend; i < end; ++i) {
+        const uint32_t idx = index_at(i);
+        const float4 g = rec[3 * (uint64_t)idx + 0];
+        blend(fx, fy, make_float2(g.x, g.y), quad_form(rec[3 * (uint64_t)idx + 1], g.z), rec[3 * (uint64_t)idx + 2],
+              p.C0, p.C1, p.C2, p.T);
+        if (p.T <= tmin) break;
+    }
+}
+
+// Each thread shades two pixels of the 16x16 block, rows y and y + 8 of one column, so every
+// staged Gaussian read from shared memory serves both.
 template <bool PER_ELEM>
 __global__ void __launch_bounds__(kRasterThreads)
 k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__ ranges,
@@ -61,8 +101,7 @@ k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__
 
     const int tid = threadIdx.x;
     const uint32_t bx0 = blockIdx.x * 16, by0 = ypix0 + blockIdx.y * 16;
-    const uint32_t px = bx0 + (tid & 15), py = by0 + (tid >> 4);
-    const bool inside = px < gp.width && py < gp.height;
+    const uint32_t px = bx0 + (tid & 15), py0 = by0 + (tid >> 4), py1 = py0 + 8;
     const uint32_t bin = (by0 / gp.bin_h) * gp.tiles_x + bx0 / gp.bin_w;
     const uint2 r = ranges[bin];
     const uint32_t start = r.x, end = r.y;
@@ -76,82 +115,95 @@ k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__
         return packed ? (uint32_t)(elems[i] & imask) : vals[i];
     };
     const float tmin = (float)(1.0 - 0.9999);
-    const float fx = (float)px, fy = (float)py;
+    const float fx = (float)px, fy0 = (float)py0, fy1 = (float)py1;
 
-    float C0 = 0.0f, C1 = 0.0f, C2 = 0.0f, T = 1.0f;
-    bool done = !inside;
     // Reference exit rule: a pixel whose T <= 1-0.9999 at the end of a 64-batch leaves the batch
     // loop, but the tail loop (comp:104-117) still blends the element at `preend` before it
-    // stops. Such a pixel waits here and takes that one element after the staged loop.
-    bool wait_tail = false;
+    // stops. Such a pixel waits and takes that one element after the staged loop.
+    Pix p0{0.0f, 0.0f, 0.0f, 1.0f, !(px < gp.width && py0 < gp.height), false};
+    Pix p1{0.0f, 0.0f, 0.0f, 1.0f, !(px < gp.width && py1 < gp.height), false};
 
     for (uint32_t b = start; b < end; b += kBatch) {
-        if (__syncthreads_and(done || wait_tail)) break;
+        const bool idle = (p0.done || p0.wait_tail) && (p1.done || p1.wait_tail);
+        if (__syncthreads_and(idle)) break;
         const uint32_t nb = min((uint32_t)kBatch, end - b);
-        if ((uint32_t)tid < nb) {
-            const uint32_t idx = index_at(b + tid);
-            const float4 p = rec[3 * (uint64_t)idx + 0];
-            s_mean[tid] = make_float2(p.x, p.y);
-            s_q[tid] = quad_form(rec[3 * (uint64_t)idx + 1], p.z);
-            s_col[tid] = rec[3 * (uint64_t)idx + 2];
+        for (uint32_t k = (uint32_t)tid; k < nb; k += kRasterThreads) {
+            const uint32_t idx = index_at(b + k);
+            const float4 g = rec[3 * (uint64_t)idx + 0];
+            s_mean[k] = make_float2(g.x, g.y);
+            s_q[k] = quad_form(rec[3 * (uint64_t)idx + 1], g.z);
+            s_col[k] = rec[3 * (uint64_t)idx + 2];
         }
         __syncthreads();
-        if (done || wait_tail) continue;
+        bool a0 = !(p0.done || p0.wait_tail), a1 = !(p1.done || p1.wait_tail);
+        if (!a0 && !a1) continue;
         if (PER_ELEM) {
-            for (uint32_t jj = 0; jj < nb; ++jj) {
-                blend(fx, fy, s_mean[jj], s_q[jj], s_col[jj], C0, C1, C2, T);
-                if (T <= tmin) { done = true; break; }
+            for (uint32_t jj = 0; jj < nb && (a0 || a1); ++jj) {
+                const float2 m = s_mean[jj];
+                const float4 q = s_q[jj], c = s_col[jj];
+                if (a0) {
+                    blend(fx, fy0, m, q, c, p0.C0, p0.C1, p0.C2, p0.T);
+                    if (p0.T <= tmin) p0.done = true, a0 = false;
+                }
+                if (a1) {
+                    blend(fx, fy1, m, q, c, p1.C0, p1.C1, p1.C2, p1.T);
+                    if (p1.T <= tmin) p1.done = true, a1 = false;
+                }
             }
             continue;
         }
         // 64-element blocks counted from `start` (batches start 256 apart, so blocks align)
         for (uint32_t j0 = 0; j0 < nb; j0 += 64) {
             if (b + j0 < preend) {  // a whole 64-batch of the reference: test once at its end
+                if (a0 && a1) {
 #pragma unroll 8
-                for (uint32_t jj = j0; jj < j0 + 64; ++jj)
-                    blend(fx, fy, s_mean[jj], s_q[jj], s_col[jj], C0, C1, C2, T);
-                if (T <= tmin) {
-                    wait_tail = preend < end;
-                    done = !wait_tail;
-                    break;
+                    for (uint32_t jj = j0; jj < j0 + 64; ++jj) {
+                        const float2 m = s_mean[jj];
+                        const float4 q = s_q[jj], c = s_col[jj];
+                        blend(fx, fy0, m, q, c, p0.C0, p0.C1, p0.C2, p0.T);
+                        blend(fx, fy1, m, q, c, p1.C0, p1.C1, p1.C2, p1.T);
+                    }
+                } else if (a0) {
+#pragma unroll 8
+                    for (uint32_t jj = j0; jj < j0 + 64; ++jj)
+                        blend(fx, fy0, s_mean[jj], s_q[jj], s_col[jj], p0.C0, p0.C1, p0.C2, p0.T);
+                } else {
+#pragma unroll 8
+                    for (uint32_t jj = j0; jj < j0 + 64; ++jj)
+                        blend(fx, fy1, s_mean[jj], s_q[jj], s_col[jj], p1.C0, p1.C1, p1.C2, p1.T);
                 }
+                if (a0 && p0.T <= tmin) {
+                    p0.wait_tail = preend < end;
+                    p0.done = !p0.wait_tail;
+                    a0 = false;
+                }
+                if (a1 && p1.T <= tmin) {
+                    p1.wait_tail = preend < end;
+                    p1.done = !p1.wait_tail;
+                    a1 = false;
+                }
+                if (!a0 && !a1) break;
             } else {  // the tail: test after every element
-                for (uint32_t jj = j0; jj < nb; ++jj) {
-                    blend(fx, fy, s_mean[jj], s_q[jj], s_col[jj], C0, C1, C2, T);
-                    if (T <= tmin) { done = true; break; }
+                for (uint32_t jj = j0; jj < nb && (a0 || a1); ++jj) {
+                    const float2 m = s_mean[jj];
+                    const float4 q = s_q[jj], c = s_col[jj];
+                    if (a0) {
+                        blend(fx, fy0, m, q, c, p0.C0, p0.C1, p0.C2, p0.T);
+                        if (p0.T <= tmin) p0.done = true, a0 = false;
+                    }
+                    if (a1) {
+                        blend(fx, fy1, m, q, c, p1.C0, p1.C1, p1.C2, p1.T);
+                        if (p1.T <= tmin) p1.done = true, a1 = false;
+                    }
                 }
                 break;
             }
         }
     }
-    if (wait_tail) {
-        // the tail loop from `preend`: one element unless that element raised T again
-        for (uint32_t i = preend; i < end; ++i) {
-            const uint32_t idx = index_at(i);
-            const float4 p = rec[3 * (uint64_t)idx + 0];
-            blend(fx, fy, make_float2(p.x, p.y), quad_form(rec[3 * (uint64_t)idx + 1], p.z),
-                  rec[3 * (uint64_t)idx + 2], C0, C1, C2, T);
-            if (T <= tmin) break;
-        }
-    }
-
-    if (inside) {
-        uchar4* pix = &img[(uint64_t)py * gp.width + px];
-        const uchar4 in = *pix;
-        const float w = 1.0f - T;
-        float o0 = (float)in.x / 255.0f + C0 * w;
-        float o1 = (float)in.y / 255.0f + C1 * w;
-        float o2 = (float)in.z / 255.0f + C2 * w;
-        float o3 = (float)in.w / 255.0f + 1.0f * w;
-        o0 = fminf(fmaxf(o0, 0.0f), 1.0f);
-        o1 = fminf(fmaxf(o1, 0.0f), 1.0f);
-        o2 = fminf(fmaxf(o2, 0.0f), 1.0f);
-        o3 = fminf(fmaxf(o3, 0.0f), 1.0f);
-        *pix = make_uchar4((unsigned char)__float2uint_rn(o0 * 255.0f),
-                           (unsigned char)__float2uint_rn(o1 * 255.0f),
-                           (unsigned char)__float2uint_rn(o2 * 255.0f),
-                           (unsigned char)__float2uint_rn(o3 * 255.0f));
-    }
+    if (p0.wait_tail) blend_tail(rec, index_at, preend, end, fx, fy0, tmin, p0);
+    if (p1.wait_tail) blend_tail(rec, index_at, preend, end, fx, fy1, tmin, p1);
+    if (px < gp.width && py0 < gp.height) write_pixel(img, gp, px, py0, p0);
+    if (px < gp.width && py1 < gp.height) write_pixel(img, gp, px, py1, p1);
 }
 
 }  // namespace
