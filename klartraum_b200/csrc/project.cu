@@ -139,7 +139,7 @@ __device__ __forceinline__ void store_outputs(uint64_t i, float px, float py, fl
 // DEV_CAM: the camera comes from device memory (a captured frame graph replayed with new cameras)
 // instead of the kernel parameters.
 template <int DEG, bool DEV_CAM>
-__global__ void __launch_bounds__(256) k_project_count(SceneDev sc, CamParams cam_arg, const CamParams* cam_dev,
+__global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams cam_arg, const CamParams* cam_dev,
                                                         GridParams gp, FrameBufs fb) {
     const CamParams& cam = DEV_CAM ? *cam_dev : cam_arg;
     constexpr int kCoef = (DEG + 1) * (DEG + 1);
