@@ -55,9 +55,9 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
 // part through whist only; rank[j] is the position among equal digits within the warp.
 template <int DBITS, bool PACKED>
 __device__ __forceinline__ void rank_warp(SortSmem<PACKED>& sm, int cur, uint32_t wpos, uint32_t valid_items,
-                                          uint32_t shift, uint32_t lane, uint32_t lt, uint16_t* whist,
+                                          uint32_t shift, uint32_t mask, uint32_t lane, uint32_t lt, uint16_t* whist,
                                           uint16_t (&rank)[kSortItems]) {
-    constexpr uint32_t kMask = (1u << DBITS) - 1u;
+    const uint32_t kMask = mask & ((1u << DBITS) - 1u);  // the pass's digit bits
 #pragma unroll
     for (int j = 0; j < kSortItems; ++j) {
         const bool valid = (uint32_t)j < valid_items;
@@ -136,7 +136,6 @@ k_sort_pass(SortIO io, FrameCtl* ctl, unsigned long long* status, uint32_t pass,
     const uint32_t ntiles = (uint32_t)((K + kSortTile - 1) / kSortTile);
     const uint32_t shift = (PACKED ? ctl->idx_bits : 0u) + 8 * pass;
     const uint32_t mask = ctl->pass_mask[pass];
-    const uint32_t dbits_n = __popc(mask);  // digit bits of this pass
     const unsigned long long* __restrict__ src_k = io_keys(io, ctl->pass_src[pass]);
     const uint32_t* __restrict__ src_v = io_vals(io, ctl->pass_src[pass]);
     unsigned long long* __restrict__ dst_k = io_keys(io, ctl->pass_dst[pass]);
@@ -207,17 +206,9 @@ k_sort_pass(SortIO io, FrameCtl* ctl, unsigned long long* status, uint32_t pass,
 
         // ---- rank within the warp (positions warp*512 + j*32 + lane)
         uint16_t rank[kSortItems];
-        switch (dbits_n) {
-            case 8: rank_warp<8, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 7: rank_warp<7, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 6: rank_warp<6, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 5: rank_warp<5, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 4: rank_warp<4, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 3: rank_warp<3, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 2: rank_warp<2, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 1: rank_warp<1, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            default: rank_warp<0, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-        }
+        // one ranking routine for every digit width: fewer instantiations keep the kernel's code
+        // in the instruction cache (narrow digits only have zero high bits)
+        rank_warp<8, PACKED>(sm, cur, wpos, valid_items, shift, mask, lane, lt, sm.whist[warp], rank);
         __syncthreads();
 
         // ---- per digit (thread = digit): prefix over warps, then the look-back
@@ -378,7 +369,6 @@ k_rts_downsweep(SortIO io, FrameCtl* ctl, const uint32_t* __restrict__ tab, uint
     if (t0 >= t1) return;
     const uint32_t shift = (PACKED ? ctl->idx_bits : 0u) + 8 * pass;
     const uint32_t mask = ctl->pass_mask[pass];
-    const uint32_t dbits_n = __popc(mask);
     const unsigned long long* __restrict__ src_k = io_keys(io, ctl->pass_src[pass]);
     const uint32_t* __restrict__ src_v = io_vals(io, ctl->pass_src[pass]);
     unsigned long long* __restrict__ dst_k = io_keys(io, ctl->pass_dst[pass]);
@@ -430,17 +420,9 @@ k_rts_downsweep(SortIO io, FrameCtl* ctl, const uint32_t* __restrict__ tab, uint
         const uint32_t valid_items = rest < (uint64_t)kSortItems ? (uint32_t)rest : (uint32_t)kSortItems;
 
         uint16_t rank[kSortItems];
-        switch (dbits_n) {
-            case 8: rank_warp<8, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 7: rank_warp<7, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 6: rank_warp<6, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 5: rank_warp<5, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 4: rank_warp<4, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 3: rank_warp<3, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 2: rank_warp<2, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            case 1: rank_warp<1, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-            default: rank_warp<0, PACKED>(sm, cur, wpos, valid_items, shift, lane, lt, sm.whist[warp], rank); break;
-        }
+        // one ranking routine for every digit width: fewer instantiations keep the kernel's code
+        // in the instruction cache (narrow digits only have zero high bits)
+        rank_warp<8, PACKED>(sm, cur, wpos, valid_items, shift, mask, lane, lt, sm.whist[warp], rank);
         __syncthreads();
 
         // per digit (thread = digit): prefix over warps, the tile's count, its global start
