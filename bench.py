@@ -8,6 +8,9 @@ degree FOV): one view per GPU with the scene replicated, no data-path collective
 scaling). Inputs are larger than L2: 240 MB of scene planes and ~390 MB of key buffers per
 frame, so no L2 flush is needed between frames.
 
+Frames are kept in flight as klartraum's engine keeps its paths: frame s renders on path
+s mod 3 with its own stream, so consecutive frames overlap on the GPU.
+
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python bench.py --mode bands [--workload large_6m]   # one 4K frame split over the GPUs
 
@@ -40,6 +43,7 @@ sys.path.insert(0, ROOT)
 METRIC = "frames/s and Gaussians/s, 1M-splat SH3 1080p; multi-view fps at 1/2/4/8 B200"
 WORKLOAD = "single_1m"
 N_VIEWS = 64
+PATHS = 3  # frames in flight, each on its own path and stream, as klartraum's engine (3 paths)
 
 
 def parse():
@@ -278,7 +282,7 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
 
     base_flags = N.FLAG_SORTED_KEYS if args.sorted_keys else 0
     r = Renderer(w.width, w.height, bin_size=16, sh_degree=w.sh_degree, device=local_rank,
-                 flags=N.FLAG_TIMING | base_flags)
+                 flags=N.FLAG_TIMING | base_flags, num_paths=PATHS)
     if world > 1:
         # the scene is made once (rank 0) and broadcast over NCCL; records land in device memory
         from klartraum_b200.multigpu import broadcast_scene
@@ -297,33 +301,41 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
 
-    # warm-up: checked frames over every view this rank renders (sizes the key buffers)
-    views = sorted({view_of(s) for s in range(args.steps)} | {view_of(s) for s in range(args.warmup)})
+    e2e_steps = args.e2e_steps or max(10, args.steps // 4)
+    # warm-up: checked frames over every view each path renders (sizes its buffers; frames in
+    # flight are async and cannot grow them)
+    views = sorted({view_of(s) for s in range(max(args.steps, e2e_steps + 2 * PATHS, args.warmup))})
     for s in range(max(args.warmup, 3)):
         r.render(cams[view_of(s)], img, stream=sptr)
-    for v in views:
-        r.render(cams[v], img, stream=sptr)
+    for p in range(PATHS):
+        for v in views:
+            r.render(cams[v], img, path=p, stream=sptr)
     torch.cuda.synchronize()
     r.stage_times_total()
+    for p in range(PATHS):
+        r.counters(p)
+    # stage times: a stream-launched pass on one path, frames back to back (graph replays record
+    # no stage timers, and frames in flight would overlap the stages of different frames)
+    r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC | base_flags)
+    for s in range(min(args.steps, 200)):
+        r.render(cams[view_of(s)], img, stream=sptr)
+    r.sync()
+    stage_ms, timed_frames = r.stage_times_total()
     r.counters()
-    stage_pass = None
-    if (args.launch == 'graph'):
-        # stage timers are not recorded by graph replays: take them from a stream-launched pass
-        r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC | base_flags)
-        for s in range(min(args.steps, 200)):
-            r.render(cams[view_of(s)], img, stream=sptr)
-        r.sync()
-        stage_pass = r.stage_times_total()
-        r.counters()
-        run_flags = N.FLAG_GRAPH | N.FLAG_ASYNC | base_flags
-        for s in range(3):  # capture
-            r.set_flags(N.FLAG_GRAPH | base_flags)
-            r.render(cams[view_of(s)], img, stream=sptr)
-        r.counters()
-    else:
-        run_flags = N.FLAG_TIMING | N.FLAG_ASYNC | base_flags
+    graph = args.launch == "graph"
+    run_flags = (N.FLAG_GRAPH if graph else 0) | N.FLAG_ASYNC | base_flags
+    streams = [torch.cuda.Stream(dev) for _ in range(PATHS)]
+    imgs = [img] + [bg.clone() for _ in range(PATHS - 1)]
+    if graph:  # one capture per path, outside the timed region
+        r.set_flags(N.FLAG_GRAPH | base_flags)
+        for p in range(PATHS):
+            r.render(cams[view_of(p)], imgs[p], path=p, stream=streams[p].cuda_stream)
+        torch.cuda.synchronize()
+        for p in range(PATHS):
+            r.counters(p)
 
-    # ---- timed region (device-resident inputs): frames enqueued back to back, no host sync
+    # ---- timed region (device-resident inputs): PATHS frames in flight, frame s on path s % PATHS
+    # and its stream, no host sync
     r.set_flags(run_flags)
     clock = ClockSampler(local_rank)
     clock.start()
@@ -333,21 +345,29 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
         dist.barrier(device_ids=[local_rank])
     torch.cuda.synchronize()
     t_wall0 = time.time()
-    ev0.record(stream)
+    ev0.record(streams[0])
+    for strm in streams[1:]:
+        strm.wait_event(ev0)
     for s in range(args.steps):
-        r.render(cams[view_of(s)], img, stream=sptr)
-    ev1.record(stream)
+        p = s % PATHS
+        r.render(cams[view_of(s)], imgs[p], path=p, stream=streams[p].cuda_stream)
+    for strm in streams[1:]:
+        ev = torch.cuda.Event()
+        ev.record(strm)
+        streams[0].wait_event(ev)
+    ev1.record(streams[0])
     torch.cuda.synchronize()
     t_wall1 = time.time()
     if world > 1:
         dist.barrier(device_ids=[local_rank])
-    r.sync()  # raises if any timed frame overflowed or timed out
+    for p in range(PATHS):
+        r.sync(p)  # raises if any timed frame overflowed or timed out
     clocks = clock.summary(t_wall0, t_wall1)
     ms = ev0.elapsed_time(ev1)
-    stage_ms, timed_frames = r.stage_times_total()
-    if stage_pass is not None:
-        stage_ms, timed_frames = stage_pass
-    cnt = r.counters()
+    cnt = {}
+    for p in range(PATHS):
+        for k, v in r.counters(p).items():
+            cnt[k] = cnt.get(k, 0) + v
     assert cnt["frames"] == args.steps, cnt
     st = r.stats()
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
@@ -360,21 +380,40 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     stages, roofline, K_avg, passes_avg = stage_report(w, cnt, st, stage_ms, timed_frames, nplanes,
                                                        r.stage_names)
 
-    # ---- end to end through the public API with host buffers
-    r.set_flags(base_flags | (N.FLAG_GRAPH if (args.launch == 'graph') else 0))
-    e2e_steps = args.e2e_steps or max(10, args.steps // 4)
-    host = torch.empty((w.height, w.width, 4), dtype=torch.uint8, pin_memory=True)
-    host.copy_(bg.cpu())
-    for s in range(3):
-        r.render_host(cams[view_of(s)], host.data_ptr(), stream=sptr)
+    # ---- end to end through the public API with host buffers: PATHS frames in flight
+    # (klartraum's paths), each path on its own stream; a path's host image is reused only after
+    # kt_gs_sync(path) says its previous frame, copies included, is done
+    hosts = [torch.empty((w.height, w.width, 4), dtype=torch.uint8, pin_memory=True) for _ in range(PATHS)]
+    for h in hosts:
+        h.copy_(bg.cpu())
+    r.set_flags(run_flags)
+
+    def frame_host(s):
+        p = s % PATHS
+        if s >= PATHS:
+            r.sync(p)
+        r.render_host(cams[view_of(s)], hosts[p].data_ptr(), path=p, stream=streams[p].cuda_stream)
+
+    for s in range(2 * PATHS):
+        frame_host(s)
+    for p in range(PATHS):
+        r.sync(p)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
+    e0.record(streams[0])
+    for strm in streams[1:]:
+        strm.wait_event(e0)
     for s in range(e2e_steps):
-        r.render_host(cams[view_of(s)], host.data_ptr(), stream=sptr)
-    e1.record(stream)
+        frame_host(s)
+    for p in range(PATHS):
+        r.sync(p)
+    for strm in streams[1:]:
+        ev = torch.cuda.Event()
+        ev.record(strm)
+        streams[0].wait_event(ev)
+    e1.record(streams[0])
     torch.cuda.synchronize()
     te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -396,7 +435,8 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
         "stages": stages, "roofline": roofline,
         "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": img_bytes + 192,
                 "d2h_bytes_per_step": img_bytes + st["status_bytes"], "steps": e2e_steps,
-                "api": "kt_gs_render_host (pinned host image in, rendered image out, waits per frame)"},
+                "api": f"kt_gs_render_host (pinned host image in, rendered image out) with {PATHS} frames in "
+                       "flight on their own paths and streams; kt_gs_sync(path) before a host image is reused"},
         "gpu_launches": launches_per_frame * args.steps * world, "gpu_launches_per_step": launches_per_frame,
         "clocks": clocks,
     }
@@ -596,6 +636,7 @@ def main():
     cfg_block = workload_config(w)
     cfg_block["binning"] = "sorted_keys" if args.sorted_keys else "placed"
     cfg_block["launch"] = "cuda_graph" if (args.launch == 'graph') else "stream"
+    cfg_block["frames_in_flight"] = PATHS
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -263,6 +263,9 @@ kt_status kt_gs_render(kt_gs_ctx* ctx, const kt_camera_mvp* cam, void* d_rgba8, 
 /*
  * Render one frame into a host image: copies the host image to the device, renders, and
  * copies it back, all on `stream`, and waits. `h_rgba8` should be pinned for full speed.
+ * With KT_GS_FLAG_ASYNC nothing is waited for: the image is ready (and errors are reported)
+ * after kt_gs_sync(path), so frames on different paths and streams overlap their copies with
+ * each other's kernels.
  */
 kt_status kt_gs_render_host(kt_gs_ctx* ctx, const kt_camera_mvp* cam, void* h_rgba8,
                             uint32_t path, void* stream);

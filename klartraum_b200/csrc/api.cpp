@@ -799,6 +799,14 @@ kt_status kt_gs_render_host(kt_gs_ctx* c, const kt_camera_mvp* cam, void* h_rgba
     if (!w.img) KT_TRY_CUDA(c, cudaMalloc(&w.img, bytes));
     cudaStream_t s = (cudaStream_t)stream;
     KT_TRY_CUDA(c, cudaMemcpyAsync(w.img, h_rgba8, bytes, cudaMemcpyHostToDevice, s));
+    if (c->cfg.flags & KT_GS_FLAG_ASYNC) {
+        // frames in flight: everything is enqueued; kt_gs_sync(path) waits for the image copy too
+        kt_status st = render_impl(c, path, Source::Scene, cam, w.img, s);
+        if (st != KT_OK) return st;
+        KT_TRY_CUDA(c, cudaMemcpyAsync(h_rgba8, w.img, bytes, cudaMemcpyDeviceToHost, s));
+        KT_TRY_CUDA(c, cudaEventRecord(w.done_ev, s));
+        return KT_OK;
+    }
     const uint32_t saved = c->cfg.flags;
     c->cfg.flags &= ~KT_GS_FLAG_ASYNC;
     kt_status st = render_impl(c, path, Source::Scene, cam, w.img, s);

@@ -95,3 +95,41 @@ def test_graph_render_host():
         outs.append((host, host2))
         r.close()
     assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
+
+
+@pytest.mark.parametrize("flags", [0, N.FLAG_GRAPH], ids=["stream", "graph"])
+def test_async_render_host_frames_in_flight(flags):
+    """kt_gs_render_host with KT_GS_FLAG_ASYNC: three paths on three streams, each host image read
+    only after kt_gs_sync(path); every image equals the synchronous render of its view."""
+    g3d = _scene(n=30000)
+    cams = orbit_views(7, 2.5, W, H, fovy_deg=60.0)
+    bgh = background(H, W, "random")
+    ref = []
+    r = Renderer(W, H, bin_size=16, sh_degree=3)
+    r.set_gaussians(g3d)
+    for c in cams:
+        ref.append(r.render_host(c, bgh.copy()))
+    r.close()
+    r = Renderer(W, H, bin_size=16, sh_degree=3, num_paths=3)
+    r.set_gaussians(g3d)
+    img = torch.from_numpy(bgh).cuda()
+    for p in range(3):  # checked frames size every path's buffers (async frames cannot grow)
+        for c in cams:
+            r.render(c, img, path=p)
+    r.set_flags(flags | N.FLAG_ASYNC)
+    streams = [torch.cuda.Stream() for _ in range(3)]
+    hosts = [torch.empty((H, W, 4), dtype=torch.uint8, pin_memory=True) for _ in range(3)]
+    got = [None] * len(cams)
+    for i, c in enumerate(cams):
+        p = i % 3
+        if i >= 3:
+            r.sync(p)
+            got[i - 3] = hosts[p].numpy().copy()
+        hosts[p].copy_(torch.from_numpy(bgh))
+        r.render_host(c, hosts[p].data_ptr(), path=p, stream=streams[p].cuda_stream)
+    for i in range(len(cams) - 3, len(cams)):
+        r.sync(i % 3)
+        got[i] = hosts[i % 3].numpy().copy()
+    r.close()
+    for a, b in zip(ref, got):
+        assert np.array_equal(a, b)
