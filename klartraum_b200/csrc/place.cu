@@ -38,8 +38,8 @@ constexpr uint32_t kBandMaxBins = 1024;        // cursors of one warp (4 KB)
 constexpr uint32_t kPlaceSmem = kPlaceWarps * kBandMaxBins * 4;
 constexpr uint32_t kCountThreads = 512;
 constexpr uint32_t kCountMaxCells = 16384;     // difference table of a count CTA (64 KB)
-constexpr uint32_t kChunkTarget = 2048;        // Gaussians per chunk, about
-constexpr uint32_t kMaxChunks = 512;
+constexpr uint32_t kChunkTarget = 1024;        // Gaussians per chunk, about (the length of a warp's serial walk)
+constexpr uint32_t kMaxChunks = 1024;
 constexpr uint32_t kNone = 0xFFFFFFFFu;
 constexpr int kRangesThreads = 1024;
 constexpr int kRangesItems = 8;                // consecutive bins per thread and round
