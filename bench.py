@@ -190,7 +190,7 @@ def run_reference(args, w, cfg_block):
 # DRAM bytes (read + write) per launch of a stage's kernel, from the ncu captures summarised in
 # profiles/ (1M SH3 1080p workload): profiles/k_pair_place_single_1m.md,
 # profiles/k_project_count_single_1m.md.
-NCU_TRAFFIC = {"single_1m": {"pair_place": 77.7e6 + 59.9e6, "project_count": 240.0e6 + 46.2e6}}
+NCU_TRAFFIC = {"single_1m": {"pair_place": 84.08e6 + 48.94e6, "project_count": 240.02e6 + 45.03e6}}
 
 
 def stage_report(w, cnt, st, stage_ms, timed_frames, nplanes, stage_names=None):
