@@ -77,21 +77,34 @@ __global__ void __launch_bounds__(256) k_depth_keys(FrameBufs fb, uint64_t n) {
     unsigned long long* out = fb.gsort[0];
     uint32_t (*hw)[256] = s_hist[warp];
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    constexpr int kItems = 4;  // elements per thread and round, loaded before they are used
     const uint64_t n_up = (n + 31) & ~31ull;  // whole warps iterate together
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_up; i += stride) {
-        const bool live = i < n;
-        const uint32_t dk = live ? (fb.counts[i] != 0u ? fb.depth[i] - dmin : dtop) : 0u;
-        if (live) out[i] = ((unsigned long long)dk << ibits) | i;
-        const uint32_t act = __ballot_sync(0xFFFFFFFFu, live);
-        for (uint32_t p = 0; p < npass; ++p) {
-            if (dbits - 8 * p == 1) {  // a one-bit digit (the top of a 25-bit range): two counts
-                const uint32_t ones = __ballot_sync(0xFFFFFFFFu, live && ((dk >> (8 * p)) & 1u));
-                if (lane == 0) {
-                    hw[p][0] += (uint32_t)__popc(act & ~ones);
-                    hw[p][1] += (uint32_t)__popc(ones);
+    for (uint64_t i0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n_up; i0 += stride * kItems) {
+        uint32_t cnt[kItems], dep[kItems];
+#pragma unroll
+        for (int u = 0; u < kItems; ++u) {
+            const uint64_t i = i0 + (uint64_t)u * stride;
+            cnt[u] = i < n ? fb.counts[i] : 0u;
+            dep[u] = i < n ? fb.depth[i] : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < kItems; ++u) {
+            const uint64_t i = i0 + (uint64_t)u * stride;
+            if (i >= n_up) break;  // uniform over the warp
+            const bool live = i < n;
+            const uint32_t dk = live ? (cnt[u] != 0u ? dep[u] - dmin : dtop) : 0u;
+            if (live) out[i] = ((unsigned long long)dk << ibits) | i;
+            const uint32_t act = __ballot_sync(0xFFFFFFFFu, live);
+            for (uint32_t p = 0; p < npass; ++p) {
+                if (dbits - 8 * p == 1) {  // a one-bit digit (the top of a 25-bit range): two counts
+                    const uint32_t ones = __ballot_sync(0xFFFFFFFFu, live && ((dk >> (8 * p)) & 1u));
+                    if (lane == 0) {
+                        hw[p][0] += (uint32_t)__popc(act & ~ones);
+                        hw[p][1] += (uint32_t)__popc(ones);
+                    }
+                } else if (live) {  // warp-private counters: only lanes of this warp collide
+                    atomicAdd(&hw[p][(dk >> (8 * p)) & 255u], 1u);
                 }
-            } else if (live) {  // warp-private counters: only lanes of this warp collide
-                atomicAdd(&hw[p][(dk >> (8 * p)) & 255u], 1u);
             }
         }
     }
