@@ -188,9 +188,8 @@ def run_reference(args, w, cfg_block):
 # ------------------------------------------------------------------- our arm
 
 # DRAM bytes (read + write) per launch of a stage's kernel, from the ncu captures summarised in
-# profiles/ (1M SH3 1080p workload): profiles/k_pair_place_single_1m.md,
-# profiles/k_project_count_single_1m.md.
-NCU_TRAFFIC = {"single_1m": {"pair_place": 84.08e6 + 48.94e6, "project_count": 240.02e6 + 45.03e6}}
+# profiles/ (1M SH3 1080p workload): profiles/k_project_count_single_1m.md.
+NCU_TRAFFIC = {"single_1m": {"project_count": 240.02e6 + 45.03e6}}
 
 
 def stage_report(w, cnt, st, stage_ms, timed_frames, nplanes, stage_names=None):
@@ -206,21 +205,24 @@ def stage_report(w, cnt, st, stage_ms, timed_frames, nplanes, stage_names=None):
     passes_avg = cnt["key_passes"] / max(cnt["keys"], 1)
     nf = max(cnt["frames"], 1)
     tiles = st["tiles_x"] * st["tiles_y"]
-    table = st["place_chunks"] * tiles * 4  # pairs per (chunk, bin), u32
+    ncoarse = ((st["tiles_x"] + 3) // 4) * ((st["tiles_y"] + 3) // 4)
+    table = st["place_chunks"] * ncoarse * 4  # entries per (chunk, coarse bin), u32
+    # bytes the placement writes: 8 per (Gaussian, coarse bin) entry, 4 per pair
+    placed = cnt["sort_bytes"] / nf
+    entries = max(placed - 4 * K_avg, 0.0) / 8
     per_frame_bytes = {
         # scene planes read; record 48 + count 4 + rect 8 + depth 4 written
         "project_count": w.n * (16 * (3 + nplanes) + 64),
         # depth keys (counts + depths read, 8-B keys written) and the depth sort passes (16 B per
         # Gaussian per pass)
         "depth_sort": w.n * (4 + 4 + 8) + cnt["depth_sort_bytes"] / nf,
-        # rectangles gathered into depth order (order, count, rectangle read; 8 B written), read
-        # again by the count; the (chunk, bin) table written
-        "pair_count": w.n * (8 + 4 + 8 + 8 + 8) + table,
-        # the table read and rewritten as its prefix over chunks; bin ranges written
-        "bin_ranges": 2 * table + tiles * 8,
-        # depth order and rectangle per Gaussian, the table and bin starts read; 4 B per pair
-        # (its Gaussian's index) written once, at its place in bin order
-        "pair_place": w.n * (8 + 8) + table + tiles * 8 + cnt["sort_bytes"] / nf,
+        # rectangles gathered into depth order (order, count, rectangle read; 8 B written); the
+        # (chunk, coarse bin) table written, read and rewritten as its prefix over chunks
+        "coarse_count": w.n * (8 + 4 + 8 + 8) + 3 * table + ncoarse * 16,
+        # depth order and rectangle per Gaussian and the table read; 8 B per entry written
+        "coarse_place": w.n * (8 + 8) + table + ncoarse * 16 + entries * 8,
+        # entries read twice (count, place); 4 B per pair written; bin ranges
+        "fine_place": entries * 8 * 2 + K_avg * 4 + tiles * 16,
         # reference-structured path: counts, rectangles and depths read, offsets written; 12 B
         # (key + value) per pair written
         "scan_emit": w.n * (4 + 8 + 4 + 8) + K_avg * 12,

@@ -143,7 +143,7 @@ typedef struct kt_gs_stats {
     uint32_t packed;         /* 1: pairs are (bin << idx_bits | index) words */
     uint32_t idx_bits;       /* index bits of a packed element */
     uint32_t place_chunks;   /* chunks of depth order the pair placement split the Gaussians into */
-    uint32_t place_bands;    /* bands of bin rows of the pair placement */
+    uint32_t place_bands;    /* bands of coarse-bin rows (4x4 bins each) of the pair placement */
 } kt_gs_stats;
 
 /* Totals accumulated on the device over every frame rendered on a path since the last
@@ -153,7 +153,9 @@ typedef struct kt_gs_counters {
     uint64_t keys;        /* sum of K */
     uint64_t key_passes;  /* sum of K * (passes over the pairs; 0 with direct placement) */
     uint64_t visible;     /* sum of Gaussians with a non-zero tile count */
-    uint64_t sort_bytes;  /* sum of bytes of pairs written in bin order (4 per pair) */
+    uint64_t sort_bytes;  /* sum of bytes written by the binning: 4 per pair + 8 per (Gaussian,
+                             coarse bin) entry of the placement; 24 or 16 per pair and pass of
+                             the pair sort with KT_GS_FLAG_SORTED_KEYS */
     uint64_t depth_sort_bytes; /* same for the depth sort of the Gaussians */
 } kt_gs_counters;
 
@@ -177,9 +179,11 @@ typedef enum kt_gs_stage {
 
 /* Stage timers (KT_GS_FLAG_TIMING), in the order the stages run. */
 #define KT_GS_NSTAGES 7
-/* 0 projection+count, 1 pairs per bin -> bin ranges and pair-sort histograms, 2 depth keys +
- * depth sort of the Gaussians, 3 scan/emit of the (bin, Gaussian) pairs, 4 sort of the pairs by
- * bin (+ frame counters), 5 rasterise, 6 whole frame */
+/* Default binning: 0 projection + count, 1 depth keys + depth sort of the Gaussians, 2 coarse
+ * counts + their prefix over chunks + coarse list starts and K, 3 coarse placement, 4 bin counts +
+ * bin ranges + pair placement (+ frame counters), 5 rasterise, 6 whole frame.
+ * KT_GS_FLAG_SORTED_KEYS: 0 projection + count, 1 scan + key emission, 2 sort of the pairs by
+ * key, 3 bin ranges (boundary search), 4 frame counters, 5 rasterise, 6 whole frame. */
 
 typedef struct kt_gs_ctx kt_gs_ctx;
 

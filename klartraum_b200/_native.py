@@ -38,7 +38,7 @@ STAGE_KEYS_SORTED = 5
 STAGE_VALUES_SORTED = 6
 STAGE_TILE_RANGES = 7
 NSTAGES = 7
-STAGE_NAMES = ["project_count", "depth_sort", "pair_count", "bin_ranges", "pair_place", "rasterize", "frame"]
+STAGE_NAMES = ["project_count", "depth_sort", "coarse_count", "coarse_place", "fine_place", "rasterize", "frame"]
 # the same timer slots when KT_GS_FLAG_SORTED_KEYS selects the reference-structured binning
 STAGE_NAMES_KEYS = ["project_count", "scan_emit", "key_sort", "bin_ranges", "totals", "rasterize", "frame"]
 

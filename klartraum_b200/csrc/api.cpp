@@ -77,8 +77,16 @@ struct PathWs {
     unsigned long long* sort_status = nullptr;
     uint32_t* sort_table = nullptr;  // per-range digit table of reduce-then-scan passes
     uint64_t status_words = 0;
-    uint32_t* pair_table = nullptr;  // pairs per (chunk, bin), then their prefix over chunks
-    uint64_t pair_table_words = 0;
+    // pair placement (default path), allocated on first use
+    uint32_t* ctable = nullptr;  // entries per (chunk, coarse bin), then their prefix over chunks
+    uint64_t ctable_words = 0;
+    uint4* cinfo = nullptr;      // per coarse bin: list start, entries, first segment
+    uint64_t cinfo_n = 0;
+    uint2* clist = nullptr;      // (Gaussian, 4x4 bin mask) by coarse bin
+    uint64_t clist_n = 0;
+    uint32_t* seg_coarse = nullptr;  // coarse bin of every segment
+    uint32_t* seg_cnt = nullptr;     // pairs per (segment, bin of the 4x4)
+    uint64_t seg_n = 0;
     uint2* ranges = nullptr;
     // reference-structured path (KT_GS_FLAG_SORTED_KEYS), allocated on first use
     unsigned long long* keys[2] = {nullptr, nullptr};  // bin << depth_bits | depth, ping-pong
@@ -208,7 +216,8 @@ uint32_t ntiles(const kt_gs_ctx* c) { return c->gp.tiles_x * c->gp.tiles_y; }
 void free_path(PathWs& w) {
     dfree(w.rec); dfree(w.counts); dfree(w.rect); dfree(w.srect); dfree(w.depth); dfree(w.gsort[0]);
     dfree(w.gsort[1]);
-    dfree(w.pairs); dfree(w.pair_table);
+    dfree(w.pairs); dfree(w.ctable); dfree(w.cinfo); dfree(w.clist); dfree(w.seg_coarse); dfree(w.seg_cnt);
+    w.ctable_words = w.cinfo_n = w.clist_n = w.seg_n = 0;
     dfree(w.sort_status); dfree(w.sort_table); dfree(w.ranges); dfree(w.ctl); dfree(w.ctl_depth);
     dfree(w.keys[0]); dfree(w.keys[1]); dfree(w.vals[0]); dfree(w.vals[1]); dfree(w.key_status);
     dfree(w.key_table); dfree(w.offsets); dfree(w.scan_status);
@@ -229,7 +238,7 @@ void free_path(PathWs& w) {
             e = nullptr;
         }
     dfree(w.totals);
-    w.n_alloc = w.cap = w.pair_table_words = 0;
+    w.n_alloc = w.cap = 0;
 }
 
 kt_status ensure_path_base(kt_gs_ctx* c, PathWs& w) {
@@ -345,6 +354,11 @@ FrameBufs frame_bufs(const PathWs& w) {
     fb.gsort[0] = w.gsort[0];
     fb.gsort[1] = w.gsort[1];
     fb.pairs = w.pairs;
+    fb.ctable = w.ctable;
+    fb.cinfo = w.cinfo;
+    fb.clist = w.clist;
+    fb.seg_coarse = w.seg_coarse;
+    fb.seg_cnt = w.seg_cnt;
     fb.offsets = w.offsets;
     fb.keys[0] = w.keys[0];
     fb.keys[1] = w.keys[1];
@@ -417,12 +431,35 @@ kt_status prepare_frame(kt_gs_ctx* c, PathWs& w, uint64_t n, bool graph, FramePl
         w.key_epoch += passes;
         return KT_OK;
     }
-    KT_TRY_CUDA(c, place_geometry(c->gp, n, &fp.pg));
-    if (fp.pg.table_words > w.pair_table_words) {
-        dfree(w.pair_table);
-        w.pair_table_words = 0;
-        KT_TRY_CUDA(c, cudaMalloc(&w.pair_table, sizeof(uint32_t) * fp.pg.table_words));
-        w.pair_table_words = fp.pg.table_words;
+    KT_TRY_CUDA(c, place_geometry(c->gp, n, w.cap, &fp.pg));
+    if (fp.pg.table_words > w.ctable_words) {
+        dfree(w.ctable);
+        w.ctable_words = 0;
+        KT_TRY_CUDA(c, cudaMalloc(&w.ctable, sizeof(uint32_t) * fp.pg.table_words));
+        w.ctable_words = fp.pg.table_words;
+        ++w.buf_gen;
+    }
+    if (fp.pg.ncoarse > w.cinfo_n) {
+        dfree(w.cinfo);
+        w.cinfo_n = 0;
+        KT_TRY_CUDA(c, cudaMalloc(&w.cinfo, sizeof(uint4) * fp.pg.ncoarse));
+        w.cinfo_n = fp.pg.ncoarse;
+        ++w.buf_gen;
+    }
+    if (w.cap > w.clist_n) {  // entries <= pairs <= capacity
+        dfree(w.clist);
+        w.clist_n = 0;
+        KT_TRY_CUDA(c, cudaMalloc(&w.clist, sizeof(uint2) * w.cap));
+        w.clist_n = w.cap;
+        ++w.buf_gen;
+    }
+    if (fp.pg.max_segments > w.seg_n) {
+        dfree(w.seg_coarse);
+        dfree(w.seg_cnt);
+        w.seg_n = 0;
+        KT_TRY_CUDA(c, cudaMalloc(&w.seg_coarse, sizeof(uint32_t) * fp.pg.max_segments));
+        KT_TRY_CUDA(c, cudaMalloc(&w.seg_cnt, sizeof(uint32_t) * 16 * fp.pg.max_segments));
+        w.seg_n = fp.pg.max_segments;
         ++w.buf_gen;
     }
     if (graph) return KT_OK;
@@ -438,8 +475,9 @@ kt_status prepare_frame(kt_gs_ctx* c, PathWs& w, uint64_t n, bool graph, FramePl
 // The kernels and copies of one frame on `stream`: no allocation and no host wait, so the
 // sequence can be captured into a CUDA graph. `ev` (may be null) receives the stage events.
 // The camera comes from `cam_dev` (device memory) when it is not null, else from `cam`.
-//   default: init -> K1 -> depth keys -> plan -> depth passes -> rectangles in depth order + pair
-//            counts -> prefix over chunks + bin ranges -> placement + totals -> K6
+//   default: init -> K1 -> depth keys -> plan -> depth passes -> rectangles in depth order +
+//            coarse counts -> prefix over chunks + coarse ranges -> coarse placement -> bin
+//            counts + bin ranges + pair placement -> totals -> K6
 //   keys:    init -> K1 -> scan + key emission -> plan + key sort passes -> boundary search ->
 //            totals -> K6
 kt_status record_frame(kt_gs_ctx* c, PathWs& w, Source src, uint64_t n, const CamParams* cam,
@@ -496,13 +534,16 @@ kt_status record_frame(kt_gs_ctx* c, PathWs& w, Source src, uint64_t n, const Ca
             KT_TRY_CUDA(c, launch_sort_pass(io_depth, w.ctl_depth, w.sort_status, w.sort_table, p,
                                             fp.sort_epoch0 + p, n, true, stream));
         if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[2], stream));
-        // pairs per (chunk of depth order, bin); their prefix over chunks and the bin ranges
-        KT_TRY_CUDA(c, launch_pair_count(fb, c->gp, fp.pg, n, w.pair_table, stream));
+        // entries per (chunk of depth order, coarse bin), their prefix over chunks, K, the coarse
+        // list starts and segments
+        KT_TRY_CUDA(c, launch_coarse_count(fb, c->gp, fp.pg, n, stream));
+        KT_TRY_CUDA(c, launch_coarse_ranges(fb, c->gp, fp.pg, n, stream));
         if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[3], stream));
-        KT_TRY_CUDA(c, launch_pair_ranges(fb, c->gp, fp.pg, n, w.pair_table, stream));
+        // coarse lists in depth order
+        KT_TRY_CUDA(c, launch_coarse_place(fb, c->gp, fp.pg, n, stream));
         if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[4], stream));
-        // every pair at its place in bin order (depth order within a bin)
-        KT_TRY_CUDA(c, launch_pair_place(fb, c->gp, fp.pg, n, w.pair_table, stream));
+        // bin counts and ranges; every pair at its place in bin order (depth order within a bin)
+        KT_TRY_CUDA(c, launch_fine_place(fb, c->gp, fp.pg, n, stream));
     }
     KT_TRY_CUDA(c, launch_frame_totals(w.ctl, w.ctl_depth, w.totals, stream));
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[5], stream));
@@ -887,19 +928,18 @@ kt_status kt_gs_frame_stats(kt_gs_ctx* c, uint32_t path, kt_gs_stats* out) {
     out->depth_min_bits = h.depth_min;
     out->depth_max_bits = h.depth_max;
     out->status_bytes = (uint32_t)kCtlHeaderBytes;
-    // init, project, depth keys, plan, the depth passes, pair count, pair scan, bin ranges,
-    // placement, totals, rasterise; or init, project, scan/emit, plan, the key passes, ranges,
-    // totals, rasterise
+    // init, project, depth keys, plan, the depth passes, coarse count, coarse scan, coarse
+    // ranges, coarse placement, bin count, segment scan, bin ranges, pair placement, totals,
+    // rasterise; or init, project, scan/emit, plan, the key passes, ranges, totals, rasterise
     out->launches = w.keys_frame ? 7 + key_passes(c) * sort_pass_launches(w.cap, false)
-                                 : 10 + kDepthPasses * sort_pass_launches(w.frame_n, true);
+                                 : 14 + kDepthPasses * sort_pass_launches(w.frame_n, true);
     out->packed = h.packed;
     out->idx_bits = h.idx_bits;
     PlaceGeom pg{};
-    if (place_geometry(c->gp, w.frame_n, &pg) == cudaSuccess) {
+    if (place_geometry(c->gp, w.frame_n, w.cap, &pg) == cudaSuccess) {
         out->place_chunks = pg.nchunks;
         out->place_bands = pg.nbands;
     }
-    if (!w.keys_frame) out->launches += 1;  // the gather of the rectangles into depth order
     return KT_OK;
 }
 

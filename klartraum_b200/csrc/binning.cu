@@ -191,10 +191,11 @@ __global__ void k_frame_totals(const FrameCtl* ctl, const FrameCtl* ctl_depth, F
         totals->keys += ctl->num_keys;
         totals->key_passes += ctl->num_keys * (unsigned long long)ctl->passes_run;
         totals->visible += ctl->num_visible;
-        // pairs placed once (u32), or the executed passes of the pair sort (keys path)
+        // placement: (Gaussian, coarse bin) entries (8 B) and pairs (u32) written once; keys path:
+        // the executed passes of the pair sort
         totals->sort_bytes += ctl->passes_run ? ctl->num_keys * (unsigned long long)ctl->passes_run *
                                                     (ctl->packed ? 16ull : 24ull)
-                                              : ctl->num_keys * 4ull;
+                                              : ctl->num_keys * 4ull + ctl->num_entries * 8ull;
         totals->depth_sort_bytes += ctl_depth->num_keys * (unsigned long long)ctl_depth->passes_run * 16ull;
     }
 }

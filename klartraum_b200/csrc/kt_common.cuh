@@ -11,8 +11,10 @@
 //                  srect u32x2[N] (rect in depth order),
 //                  gsort u64[2][N] (Gaussians by depth), pairs u32[cap] (the Gaussian of
 //                  every (bin, Gaussian) pair, in bin order; the bin is implied by the ranges),
-//                  ranges u32x2[tiles], pair table u32[chunks][tiles], look-back status
-//                  words of the depth sort, two FrameCtl blocks.
+//                  ranges u32x2[tiles], coarse table u32[chunks][coarse bins], coarse info
+//                  u32x4[coarse bins], coarse lists u32x2[cap] (Gaussian, 4x4 bin mask),
+//                  segment map u32[segments], segment counts u32[segments][16], look-back
+//                  status words of the depth sort, two FrameCtl blocks.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -42,6 +44,7 @@ __host__ __device__ inline uint64_t status_value(uint64_t w) { return w & kValue
 // Per-frame control block in device memory, reset by k_frame_init.
 struct FrameCtl {
     unsigned long long num_keys;      // K: pairs (render path) or keys (sorts)
+    unsigned long long pair_total;    // sum of the Gaussians' bin counts (projection)
     unsigned int depth_min;           // min / max of floatBitsToUint(z) ^ 0x80000000
     unsigned int depth_max;           //   over Gaussians with a non-zero tile count
     unsigned int num_visible;         // Gaussians with a non-zero tile count
@@ -54,6 +57,8 @@ struct FrameCtl {
     unsigned int final_buf;           // which key/value buffer holds the sorted data
     unsigned int packed;              // 1: elements are (key << idx_bits) | index, no value array
     unsigned int idx_bits;            // bits of the index field of a packed element (0 unpacked)
+    unsigned int num_entries;         // (Gaussian, coarse bin) entries of the pair placement
+    unsigned int num_segments;        // segments of the coarse lists (second placement level)
     unsigned int pass_ticket[kMaxPasses];
     unsigned int pass_run[kMaxPasses];
     unsigned int pass_src[kMaxPasses];
@@ -108,15 +113,17 @@ struct SceneDev {
 
 // Work split of the pair placement (place.cu).
 struct PlaceGeom {
+    uint32_t ctx, cty;        // coarse grid (4x4 bins per coarse bin) over the binned rows
+    uint32_t ncoarse;         // ctx * cty
     uint32_t nchunks;         // chunks of consecutive Gaussians in depth order
     uint32_t chunk_len;       // Gaussians per chunk (the last may be shorter)
-    uint32_t nbands;          // placement bands of bin rows (one warp's cursors each)
-    uint32_t band_rows;       // bin rows per placement band (the last may be shorter)
-    uint32_t ncbands;         // count bands of bin rows (one CTA's difference table each)
-    uint32_t cband_rows;
+    uint32_t nbands;          // placement bands of coarse rows (one warp's cursors each)
+    uint32_t band_rows;       // coarse rows per placement band (the last may be shorter)
     uint32_t count_smem;      // dynamic shared memory of a count CTA
-    uint32_t place_ctas;      // persistent placement CTAs
-    uint64_t table_words;     // u32 words of table[chunk][bin]
+    uint32_t place_ctas;      // persistent coarse-placement CTAs
+    uint32_t seg_ctas;        // CTAs of the segment kernels
+    uint64_t table_words;     // u32 words of table[chunk][coarse bin]
+    uint64_t max_segments;    // segments the key capacity can produce, at most
 };
 
 struct FrameBufs {
@@ -127,6 +134,12 @@ struct FrameBufs {
     uint32_t* depth;
     unsigned long long* gsort[2];  // Gaussians by depth: (depth - min) << idx_bits | index
     uint32_t* pairs;               // Gaussian index of every (bin, Gaussian) pair, in bin order
+    // pair placement: (chunk, coarse bin) table, coarse lists and their segments
+    uint32_t* ctable;              // entries per (chunk, coarse bin), then their prefix over chunks
+    uint4* cinfo;                  // per coarse bin: list start, entries, first segment, 0
+    uint2* clist;                  // (Gaussian index, 4x4 bin mask) by coarse bin, depth order
+    uint32_t* seg_coarse;          // coarse bin of every segment
+    uint32_t* seg_cnt;             // pairs per (segment, bin of the 4x4), then their prefix
     // reference-structured path (KT_GS_FLAG_SORTED_KEYS): offsets, keys and values
     unsigned long long* offsets;   // exclusive scan of the counts, index order
     unsigned long long* keys[2];   // bin << depth_bits | (depth - depth_min), ping-pong

@@ -47,17 +47,20 @@ cudaError_t launch_plan(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes, i
 cudaError_t launch_frame_totals(const FrameCtl* ctl, const FrameCtl* ctl_depth, FrameTotals* totals,
                                 cudaStream_t stream);
 
-// place.cu: pairs by bin from the Gaussians in depth order (counting sort, no pair sort)
-cudaError_t place_geometry(const GridParams& gp, uint64_t n, PlaceGeom* out);
-// table[chunk][bin] <- the chunk's pairs per bin
-cudaError_t launch_pair_count(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
-                              uint32_t* table, cudaStream_t stream);
-// table -> prefix over chunks; bin ranges, K and the capacity check (FrameCtl::plan_ok)
-cudaError_t launch_pair_ranges(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
-                               uint32_t* table, cudaStream_t stream);
-// every pair written at its sorted position in fb.keys[0]
-cudaError_t launch_pair_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
-                              const uint32_t* table, cudaStream_t stream);
+// place.cu: pairs by bin from the Gaussians in depth order (two-level counting sort, no pair sort)
+cudaError_t place_geometry(const GridParams& gp, uint64_t n, uint64_t capacity, PlaceGeom* out);
+// rectangles in depth order; table[chunk][coarse bin] and its prefix over chunks
+cudaError_t launch_coarse_count(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
+                                cudaStream_t stream);
+// K and the capacity check (FrameCtl::plan_ok); coarse list starts and segments
+cudaError_t launch_coarse_ranges(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
+                                 cudaStream_t stream);
+// every (Gaussian, coarse bin) entry at its place in its coarse list
+cudaError_t launch_coarse_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
+                                cudaStream_t stream);
+// bin counts, bin ranges, and every pair at its place in bin order
+cudaError_t launch_fine_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
+                              cudaStream_t stream);
 
 // keys.cu: the reference-structured path (scan, key emission, boundary search)
 cudaError_t launch_key_scan_emit(const FrameBufs& fb, const GridParams& gp, uint64_t n, uint32_t epoch,

@@ -1,46 +1,55 @@
-// Pairs by bin without a sort: a stable counting sort of the (bin, Gaussian) pairs, fed with the
-// Gaussians in depth order.
+// Pairs by bin without a pair sort: a two-level stable counting sort of the (bin, Gaussian)
+// pairs, fed with the Gaussians in depth order.
 //
 // The reference duplicates each projected Gaussian once per overlapped bin and sorts the copies
 // by the 48-bit key bin << 32 | depth (shaders/gsplat/gsplat_binning.comp:112-159,
 // gsplat_radix_sort_include.glsl:51-63). With the Gaussians already sorted by depth (stable,
 // ties by index) that order is: by bin, then by the Gaussian's position in depth order. The
-// pairs of one Gaussian cover a rectangle of bins, so they never need to exist unsorted:
-//   k_depth_rects  the Gaussians' bin rectangles gathered into depth order (empty rectangle for
-//                  Gaussians without bins), so that everything after reads them coalesced.
-//   k_pair_count   one CTA per (chunk, count band). A chunk is a contiguous run of depth order;
-//                  its Gaussians add +1/-1 at the corners of their rectangles in a shared-memory
-//                  difference table of the band's bin rows; the table's 2D prefix sums are the
-//                  chunk's pairs per bin, stored as table[chunk][bin].
-//   k_pair_scan    per bin, the exclusive prefix of table[.][bin] over chunks (in place) and the
-//                  bin's total.
-//   k_bin_ranges   exclusive scan of the totals over bins: ranges {start, end} (empty bins keep
-//                  {0, 0}, as the reference's zeroed StartAndEnd buffer), K, the capacity check.
-//   k_pair_place   persistent warps take (band, chunk) items in band-major order. A band is a
-//                  few bin rows; the warp keeps one write cursor per bin of the band in shared
-//                  memory (bin start + the chunk's prefix), walks the chunk's Gaussians in depth
-//                  order and, for each one meeting the band, lets its lanes write the pairs at
-//                  their bins' cursors, which then advance.
-// A warp visits its Gaussians in order and chunks take consecutive slices of every bin, so
-// equal-bin pairs land in depth order: the stable sort of the pairs by bin, with no pass over
-// unsorted pairs. A pair is stored as its Gaussian's index (4 bytes); its bin is implied by the
-// bin ranges. Band-major order keeps the output sectors being filled at any moment (items in
-// flight x bins per band) within L2, so partial sectors merge there instead of in DRAM.
+// pairs of one Gaussian cover a rectangle of bins, so they never need to exist unsorted.
+//
+// Level 1, coarse bins of 4x4 bins (a Gaussian meets 3.4 of them on average where it meets 20
+// bins):
+//   k_coarse_count   one CTA per chunk (a run of depth order): the Gaussians' rectangles are
+//                    gathered into depth order (srect) and every coarse bin a rectangle meets is
+//                    counted in shared memory: table[chunk][coarse bin].
+//   k_coarse_scan    per coarse bin, the exclusive prefix of the table over chunks (in place)
+//                    and the bin's entry total.
+//   k_coarse_ranges  one CTA: K (the projection's pair total) and the capacity check; exclusive
+//                    scans of the coarse totals (list starts) and of their segment counts
+//                    (kSegLen entries per segment); the segment -> coarse bin map.
+//   k_coarse_place   persistent warps over (band, chunk) items: 32 Gaussians at a time, their
+//                    (Gaussian, coarse bin) entries flattened in depth order and taken 32 at a
+//                    time; lanes with equal coarse bins are ranked by lane (ballot match) and
+//                    written at the bin's cursor as (Gaussian index, mask of the 4x4 bins met).
+// Level 2, the bins of a coarse bin:
+//   k_fine_count     a warp per segment of a coarse list: pairs per bin of the 4x4 (ballots).
+//   k_fine_seg_scan  a CTA per coarse bin: per bin of its 4x4, the exclusive prefix of the
+//                    segments' counts (in place) and the bin's total.
+//   k_fine_ranges    one CTA: exclusive scan of the bin totals -> ranges {start, end} (empty
+//                    bins keep {0, 0}, as the reference's zeroed StartAndEnd buffer).
+//   k_fine_place     a warp per segment, 32 entries at a time: for each bin of the 4x4 a ballot
+//                    ranks the entries that meet it; each writes its Gaussian at the bin's
+//                    cursor + rank (consecutive addresses per bin).
+// Chunks take consecutive slices of every coarse list, segments consecutive slices of every bin
+// and every step ranks by lane, so equal-bin pairs land in depth order: the stable sort of the
+// pairs by bin. A pair is stored as its Gaussian's index (4 bytes); its bin is implied by the
+// ranges.
 #include "kt_common.cuh"
 #include "kt_kernels.h"
 
 namespace kt {
 namespace {
 
-constexpr uint32_t kPlaceWarps = 16;           // warps of a placement CTA (one CTA per SM)
-constexpr uint32_t kBandTargetBins = 768;      // bins of a placement band, about
-constexpr uint32_t kBandMaxBins = 1024;        // cursors of one warp (4 KB)
-constexpr uint32_t kPlaceSmem = kPlaceWarps * kBandMaxBins * 4;
+constexpr uint32_t kCoarse = 4;                // bins per side of a coarse bin
+constexpr uint32_t kChunkTarget = 512;         // Gaussians per chunk of depth order, about
+constexpr uint32_t kMaxChunks = 4096;
 constexpr uint32_t kCountThreads = 512;
-constexpr uint32_t kCountMaxCells = 16384;     // difference table of a count CTA (64 KB)
-constexpr uint32_t kChunkTarget = 1024;        // Gaussians per chunk, about (the length of a warp's serial walk)
-constexpr uint32_t kMaxChunks = 1024;
-constexpr uint32_t kNone = 0xFFFFFFFFu;
+constexpr uint32_t kCoarseMax = 16384;         // coarse bins of a frame (count CTA: 64 KB of counters)
+constexpr uint32_t kBandMax = 1024;            // coarse bins of a placement band (4 KB of cursors per warp)
+constexpr uint32_t kPlaceWarps = 16;           // warps of a coarse-placement CTA (one CTA per SM)
+constexpr uint32_t kPlaceSmem = kPlaceWarps * kBandMax * 4;
+constexpr uint32_t kSegLen = 512;              // entries of a segment of a coarse list
+constexpr uint32_t kSegWarps = 8;              // warps of a segment-kernel CTA
 constexpr int kRangesThreads = 1024;
 constexpr int kRangesItems = 8;                // consecutive bins per thread and round
 
@@ -52,100 +61,64 @@ __device__ __forceinline__ void divmod_small(uint32_t a, uint32_t w, float inv_w
     r = a - q * w;
 }
 
-__global__ void __launch_bounds__(256) k_depth_rects(FrameBufs fb, uint64_t n) {
+// Bits [lo, hi) of a 4-bit row or column set.
+__device__ __forceinline__ uint32_t span4(uint32_t lo, uint32_t hi) {
+    return ((1u << hi) - 1u) & ~((1u << lo) - 1u);
+}
+
+// Rectangle of a Gaussian in bins, clipped to the binned rows; rows relative to row_begin.
+// Returns false for an empty rectangle.
+__device__ __forceinline__ bool local_rect(uint2 r, const GridParams& gp, uint32_t& x0, uint32_t& x1, uint32_t& y0,
+                                           uint32_t& y1) {
+    x0 = r.x & 0xFFFFu;
+    x1 = min(r.x >> 16, gp.tiles_x);
+    y0 = max(r.y & 0xFFFFu, gp.row_begin);
+    y1 = min(r.y >> 16, gp.row_end);
+    if (x0 >= x1 || y0 >= y1) return false;
+    y0 -= gp.row_begin;
+    y1 -= gp.row_begin;
+    return true;
+}
+
+// ------------------------------------------------------------------- level 1
+
+__global__ void __launch_bounds__(kCountThreads) k_coarse_count(FrameBufs fb, GridParams gp, PlaceGeom pg,
+                                                                uint64_t n) {
+    extern __shared__ uint32_t s_cnt[];
+    const uint32_t chunk = blockIdx.x;
+    for (uint32_t i = threadIdx.x; i < pg.ncoarse; i += kCountThreads) s_cnt[i] = 0u;
+    __syncthreads();
     const FrameCtl* cd = fb.ctl_depth;
     const unsigned long long* __restrict__ order = io_select(fb.gsort, cd->final_buf);
     const unsigned long long imask = (1ull << cd->idx_bits) - 1ull;
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    for (uint64_t p = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; p < n; p += stride) {
-        const uint32_t g = (uint32_t)(order[p] & imask);
-        fb.srect[p] = fb.counts[g] != 0u ? fb.rect[g] : make_uint2(0u, 0u);
-    }
-}
-
-__global__ void __launch_bounds__(kCountThreads) k_pair_count(FrameBufs fb, GridParams gp, PlaceGeom pg, uint64_t n,
-                                                              uint32_t* __restrict__ table) {
-    extern __shared__ int s_tab[];
-    const uint32_t chunk = blockIdx.x / pg.ncbands, cband = blockIdx.x - chunk * pg.ncbands;
-    const uint32_t by0 = gp.row_begin + cband * pg.cband_rows;
-    const uint32_t by1 = min(by0 + pg.cband_rows, gp.row_end);
-    if (by0 >= by1) return;  // uniform over the CTA
-    const uint32_t rows = by1 - by0, tx = gp.tiles_x, W1 = tx + 1;
-    const uint32_t cells = W1 * (rows + 1);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (uint32_t i = tid; i < cells; i += kCountThreads) s_tab[i] = 0;
-    __syncthreads();
     const uint64_t q0 = (uint64_t)chunk * pg.chunk_len;
     const uint64_t q1 = min(q0 + (uint64_t)pg.chunk_len, n);
-    for (uint64_t q = q0 + tid; q < q1; q += kCountThreads) {
-        const uint2 r = fb.srect[q];
-        const uint32_t y0 = max(r.y & 0xFFFFu, by0), y1 = min(r.y >> 16, by1);
-        const uint32_t x0 = r.x & 0xFFFFu, x1 = r.x >> 16;
-        if (x0 >= x1 || y0 >= y1) continue;
-        const uint32_t a = (y0 - by0) * W1, b = (y1 - by0) * W1;
-        atomicAdd(&s_tab[a + x0], 1);
-        atomicAdd(&s_tab[a + x1], -1);
-        atomicAdd(&s_tab[b + x0], -1);
-        atomicAdd(&s_tab[b + x1], 1);
+    for (uint64_t q = q0 + threadIdx.x; q < q1; q += kCountThreads) {
+        const uint32_t g = (uint32_t)(order[q] & imask);
+        const uint2 r = fb.counts[g] != 0u ? fb.rect[g] : make_uint2(0u, 0u);
+        fb.srect[q] = r;
+        uint32_t x0, x1, y0, y1;
+        if (!local_rect(r, gp, x0, x1, y0, y1)) continue;
+        const uint32_t cx0 = x0 / kCoarse, cx1 = (x1 + kCoarse - 1) / kCoarse;
+        const uint32_t cy0 = y0 / kCoarse, cy1 = (y1 + kCoarse - 1) / kCoarse;
+        for (uint32_t cy = cy0; cy < cy1; ++cy)
+            for (uint32_t cx = cx0; cx < cx1; ++cx) atomicAdd(&s_cnt[cy * pg.ctx + cx], 1u);
     }
     __syncthreads();
-    // 2D prefix sums: along x (a warp per row, 32 columns per step), then along y (a thread
-    // per column, 8 loads in flight)
-    constexpr uint32_t kWarps = kCountThreads / 32;
-    for (uint32_t y = warp; y < rows; y += kWarps) {
-        int carry = 0;
-        for (uint32_t x0 = 0; x0 < tx; x0 += 32) {
-            const uint32_t x = x0 + lane;
-            int v = x < tx ? s_tab[y * W1 + x] : 0;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int t = __shfl_up_sync(0xFFFFFFFFu, v, o);
-                if (lane >= o) v += t;
-            }
-            if (x < tx) s_tab[y * W1 + x] = v + carry;
-            carry += __shfl_sync(0xFFFFFFFFu, v, 31);
-        }
-    }
-    __syncthreads();
-    for (uint32_t x = tid; x < tx; x += kCountThreads) {
-        int run = 0;
-        uint32_t y = 0;
-        for (; y + 8 <= rows; y += 8) {
-            int v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = s_tab[(y + u) * W1 + x];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                run += v[u];
-                s_tab[(y + u) * W1 + x] = run;
-            }
-        }
-        for (; y < rows; ++y) {
-            run += s_tab[y * W1 + x];
-            s_tab[y * W1 + x] = run;
-        }
-    }
-    __syncthreads();
-    uint32_t* __restrict__ trow = table + (uint64_t)chunk * tx * gp.tiles_y + (uint64_t)by0 * tx;
-    for (uint32_t i = tid; i < rows * tx; i += kCountThreads) {
-        const uint32_t y = i / tx, x = i - y * tx;
-        trow[i] = (uint32_t)s_tab[y * W1 + x];
-    }
+    uint32_t* __restrict__ trow = fb.ctable + (uint64_t)chunk * pg.ncoarse;
+    for (uint32_t i = threadIdx.x; i < pg.ncoarse; i += kCountThreads) trow[i] = s_cnt[i];
 }
 
-// 32 bins per CTA (lanes), the chunks split into 32 segments (warps). Bins outside the binned
-// rows are not touched (their ranges stay {0, 0} from k_frame_init).
-__global__ void __launch_bounds__(1024) k_pair_scan(GridParams gp, PlaceGeom pg, uint32_t* __restrict__ table,
-                                                    uint2* __restrict__ ranges) {
+// 32 coarse bins per CTA (lanes), the chunks split into 32 slices (warps).
+__global__ void __launch_bounds__(1024) k_coarse_scan(FrameBufs fb, PlaceGeom pg) {
     __shared__ uint32_t s_seg[32][33];
     const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
-    const uint64_t B = (uint64_t)gp.tiles_x * gp.tiles_y;
-    const uint32_t b_end = gp.row_end * gp.tiles_x;
-    const uint32_t b = gp.row_begin * gp.tiles_x + blockIdx.x * 32 + lane;
-    const bool live = b < b_end;
+    const uint64_t B = pg.ncoarse;
+    const uint32_t b = blockIdx.x * 32 + lane;
+    const bool live = b < pg.ncoarse;
     const uint32_t per = (pg.nchunks + 31) / 32;
     const uint32_t c0 = min(seg * per, pg.nchunks), c1 = min(c0 + per, pg.nchunks);
-    uint32_t* __restrict__ col = table + b;
+    uint32_t* __restrict__ col = fb.ctable + b;
     uint32_t sum = 0;
     if (live) {
         uint32_t c = c0;
@@ -159,7 +132,7 @@ __global__ void __launch_bounds__(1024) k_pair_scan(GridParams gp, PlaceGeom pg,
     uint32_t base = 0;
     for (int s = 0; s < seg; ++s) base += s_seg[s][lane];
     if (!live) return;
-    if (seg == 31) ranges[b] = make_uint2(0u, base + sum);  // the bin's total, for k_bin_ranges
+    if (seg == 31) fb.cinfo[b] = make_uint4(0u, base + sum, 0u, 0u);  // the bin's total
     for (uint32_t c = c0; c < c1; ++c) {
         const uint32_t v = col[(uint64_t)c * B];
         col[(uint64_t)c * B] = base;
@@ -167,10 +140,290 @@ __global__ void __launch_bounds__(1024) k_pair_scan(GridParams gp, PlaceGeom pg,
     }
 }
 
+// Exclusive block scan of two counters per thread; returns the prefixes, adds the block totals
+// to the carries.
+__device__ __forceinline__ uint2 block_scan2(uint32_t a, uint32_t b, uint32_t* s_a, uint32_t* s_b,
+                                             unsigned long long& carry_a, unsigned long long& carry_b) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint32_t xa = a, xb = b;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t ta = __shfl_up_sync(0xFFFFFFFFu, xa, o);
+        const uint32_t tb = __shfl_up_sync(0xFFFFFFFFu, xb, o);
+        if (lane >= o) {
+            xa += ta;
+            xb += tb;
+        }
+    }
+    if (lane == 31) {
+        s_a[warp] = xa;
+        s_b[warp] = xb;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t wa = s_a[lane], wb = s_b[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t ta = __shfl_up_sync(0xFFFFFFFFu, wa, o);
+            const uint32_t tb = __shfl_up_sync(0xFFFFFFFFu, wb, o);
+            if (lane >= o) {
+                wa += ta;
+                wb += tb;
+            }
+        }
+        s_a[lane] = wa;
+        s_b[lane] = wb;
+    }
+    __syncthreads();
+    const uint2 out = make_uint2((uint32_t)carry_a + (warp ? s_a[warp - 1] : 0u) + xa - a,
+                                 (uint32_t)carry_b + (warp ? s_b[warp - 1] : 0u) + xb - b);
+    const uint32_t ta = s_a[31], tb = s_b[31];
+    __syncthreads();
+    carry_a += ta;
+    carry_b += tb;
+    return out;
+}
+
+__global__ void __launch_bounds__(kRangesThreads) k_coarse_ranges(FrameBufs fb, GridParams gp, PlaceGeom pg) {
+    __shared__ uint32_t s_a[32], s_b[32];
+    __shared__ uint32_t s_ok;
+    FrameCtl* ctl = fb.ctl;
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        const FrameCtl* cd = fb.ctl_depth;
+        const unsigned long long K = ctl->pair_total;
+        const uint32_t dmin = ctl->depth_min, dmax = ctl->depth_max;
+        ctl->num_keys = K;
+        ctl->depth_bits = dmax >= dmin ? bits_for((uint64_t)(dmax - dmin)) : 0u;
+        ctl->key_bits = gp.tile_bits;
+        ctl->packed = 0u;  // pairs are u32 Gaussian indices
+        ctl->idx_bits = cd->idx_bits;
+        ctl->final_buf = 0u;
+        ctl->passes_run = 0u;
+        const bool fits = K <= fb.key_capacity;
+        if (!fits) atomicOr(&ctl->error_flags, kErrCapacity);
+        if (cd->error_flags & kErrTimeout) atomicOr(&ctl->error_flags, kErrTimeout);
+        // a timed-out depth sort leaves the depth order undefined: draw nothing
+        ctl->plan_ok = (fits && (ctl->error_flags & kErrTimeout) == 0u) ? 1u : 0u;
+        s_ok = ctl->plan_ok;
+    }
+    __syncthreads();
+    if (!s_ok) return;  // the lists and segments below are sized by the capacity
+    unsigned long long carry_e = 0, carry_s = 0;
+    constexpr uint32_t kRound = kRangesThreads * kRangesItems;
+    for (uint32_t r0 = 0; r0 < pg.ncoarse; r0 += kRound) {
+        const uint32_t first = r0 + (uint32_t)tid * kRangesItems;
+        uint32_t cnt[kRangesItems];
+        uint32_t ne = 0, ns = 0;
+#pragma unroll
+        for (int i = 0; i < kRangesItems; ++i) {
+            cnt[i] = first + i < pg.ncoarse ? fb.cinfo[first + i].y : 0u;
+            ne += cnt[i];
+            ns += (cnt[i] + kSegLen - 1) / kSegLen;
+        }
+        const uint2 st = block_scan2(ne, ns, s_a, s_b, carry_e, carry_s);
+        uint32_t e = st.x, s = st.y;
+#pragma unroll
+        for (int i = 0; i < kRangesItems; ++i) {
+            if (first + i >= pg.ncoarse) break;
+            const uint32_t k = (cnt[i] + kSegLen - 1) / kSegLen;
+            fb.cinfo[first + i] = make_uint4(e, cnt[i], s, 0u);
+            for (uint32_t j = 0; j < k; ++j) fb.seg_coarse[s + j] = first + i;
+            e += cnt[i];
+            s += k;
+        }
+    }
+    if (tid == 0) {
+        ctl->num_entries = (uint32_t)carry_e;
+        ctl->num_segments = (uint32_t)carry_s;
+    }
+}
+
+// Persistent: every warp takes (band, chunk) items from a ticket, band-major. For an item, the
+// chunk's Gaussians 32 at a time (one per lane, in depth order): their entries (the coarse bins
+// of the band their rectangles meet, row-major) are numbered in lane order, and the warp takes
+// them 32 at a time. Entries of the same coarse bin in one step are ranked by lane; the last of
+// them advances the bin's cursor.
+__global__ void __launch_bounds__(kPlaceWarps * 32, 1) k_coarse_place(FrameBufs fb, GridParams gp, PlaceGeom pg,
+                                                                      uint64_t n) {
+    extern __shared__ uint32_t s_cur[];  // kBandMax cursors per warp
+    FrameCtl* ctl = fb.ctl;
+    if (!ctl->plan_ok) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t lt = (1u << lane) - 1u;
+    uint32_t* cur = s_cur + (size_t)warp * kBandMax;
+    const FrameCtl* cd = fb.ctl_depth;
+    const unsigned long long* __restrict__ order = io_select(fb.gsort, cd->final_buf);
+    const unsigned long long imask = (1ull << cd->idx_bits) - 1ull;
+    uint2* __restrict__ out = fb.clist;
+    const uint32_t ctx = pg.ctx, items = pg.nbands * pg.nchunks;
+    for (;;) {
+        uint32_t item = 0;
+        if (lane == 0) item = atomicAdd(&ctl->scan_ticket, 1u);
+        item = __shfl_sync(0xFFFFFFFFu, item, 0);
+        if (item >= items) break;
+        const uint32_t band = item / pg.nchunks, chunk = item - band * pg.nchunks;
+        const uint32_t cb0 = band * pg.band_rows, cb1 = min(cb0 + pg.band_rows, pg.cty);
+        const uint32_t nb = (cb1 - cb0) * ctx, bin0 = cb0 * ctx;
+        const uint32_t nbits = nb > 1u ? 32u - __clz(nb - 1u) : 0u;
+        const uint64_t q0 = (uint64_t)chunk * pg.chunk_len;
+        const uint64_t q1 = min(q0 + (uint64_t)pg.chunk_len, n);
+        const uint32_t* __restrict__ trow = fb.ctable + (uint64_t)chunk * pg.ncoarse + bin0;
+        __syncwarp();  // the previous item is done with the cursors
+        for (uint32_t i = lane; i < nb; i += 32) cur[i] = trow[i] + fb.cinfo[bin0 + i].x;
+        __syncwarp();
+        // batch i is placed while batch i+1's rectangles and indices load
+        uint64_t q = q0 + lane;
+        uint2 r0 = q < q1 ? fb.srect[q] : make_uint2(0u, 0u);
+        uint32_t g0 = q < q1 ? (uint32_t)(order[q] & imask) : 0u;
+        for (uint64_t qb = q0; qb < q1; qb += 32) {
+            q = qb + 32 + lane;
+            const uint2 r1 = q < q1 ? fb.srect[q] : make_uint2(0u, 0u);
+            const uint32_t g1 = q < q1 ? (uint32_t)(order[q] & imask) : 0u;
+            // this lane's Gaussian: bins (x0..x1, y0..y1) and coarse bins of the band
+            uint32_t x0, x1, y0, y1, e = 0u, cpack = 0u, cy0 = 0u;
+            float inv = 1.0f;
+            if (local_rect(r0, gp, x0, x1, y0, y1)) {
+                const uint32_t cx0 = x0 / kCoarse, cx1 = (x1 + kCoarse - 1) / kCoarse;
+                cy0 = max(y0 / kCoarse, cb0);
+                const uint32_t cy1 = min((y1 + kCoarse - 1) / kCoarse, cb1);
+                if (cy0 < cy1) {
+                    const uint32_t cw = cx1 - cx0;
+                    e = cw * (cy1 - cy0);
+                    cpack = cx0 | (cw << 16);
+                    inv = __frcp_rn((float)cw);
+                }
+            } else {
+                x0 = x1 = y0 = y1 = 0u;
+            }
+            const uint32_t xs = x0 | (x1 << 16), ys = y0 | (y1 << 16);
+            uint32_t incl = e;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                if (lane >= o) incl += t;
+            }
+            const uint32_t total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+            const uint32_t first = incl - e;  // this lane's first entry
+            for (uint32_t t0 = 0; t0 < total; t0 += 32) {
+                const uint32_t t = t0 + lane;
+                const bool valid = t < total;
+                // the entry's Gaussian: the last lane whose first entry is <= t (lanes without
+                // entries share the next lane's first, so the last such lane has entries)
+                uint32_t j = 0;
+#pragma unroll
+                for (uint32_t s = 16; s; s >>= 1) {
+                    const uint32_t f = __shfl_sync(0xFFFFFFFFu, first, j + s);
+                    if (f <= t) j += s;
+                }
+                const uint32_t k = t - __shfl_sync(0xFFFFFFFFu, first, j);
+                const uint32_t cp = __shfl_sync(0xFFFFFFFFu, cpack, j);
+                const uint32_t cyj = __shfl_sync(0xFFFFFFFFu, cy0, j);
+                const float invj = __shfl_sync(0xFFFFFFFFu, inv, j);
+                const uint32_t xj = __shfl_sync(0xFFFFFFFFu, xs, j);
+                const uint32_t yj = __shfl_sync(0xFFFFFFFFu, ys, j);
+                const uint32_t gj = __shfl_sync(0xFFFFFFFFu, g0, j);
+                uint32_t dy = 0, dx = 0;
+                if (valid) divmod_small(k, cp >> 16, invj, dy, dx);
+                const uint32_t ccx = (cp & 0xFFFFu) + dx, ccy = cyj + dy;
+                const uint32_t cl = (ccy - cb0) * ctx + ccx;  // band-local coarse bin
+                // the bins of the coarse bin's 4x4 that the rectangle meets
+                const uint32_t bx = ccx * kCoarse, by = ccy * kCoarse;
+                const uint32_t cols = span4(max(xj & 0xFFFFu, bx) - bx, min(xj >> 16, bx + kCoarse) - bx);
+                const uint32_t rows = span4(max(yj & 0xFFFFu, by) - by, min(yj >> 16, by + kCoarse) - by);
+                const uint32_t spread = (rows & 1u) | ((rows & 2u) << 3) | ((rows & 4u) << 6) | ((rows & 8u) << 9);
+                const uint32_t mask = cols * spread;
+                // lanes of this step with the same coarse bin
+                uint32_t peers = __ballot_sync(0xFFFFFFFFu, valid);
+                for (uint32_t b = 0; b < nbits; ++b) {
+                    const bool bit = (cl >> b) & 1u;
+                    const uint32_t bb = __ballot_sync(0xFFFFFFFFu, bit);
+                    peers &= bit ? bb : ~bb;
+                }
+                uint32_t pos = 0;
+                if (valid) pos = cur[cl] + __popc(peers & lt);
+                __syncwarp();
+                if (valid && (peers >> lane) == 1u) cur[cl] = pos + 1u;  // the bin's last entry of this step
+                __syncwarp();
+                if (valid) out[pos] = make_uint2(gj, mask);
+            }
+            r0 = r1;
+            g0 = g1;
+        }
+    }
+}
+
+// ------------------------------------------------------------------- level 2
+
+struct Segment {
+    uint32_t coarse, e0, e1;
+};
+
+__device__ __forceinline__ Segment segment_of(const FrameBufs& fb, uint32_t s) {
+    const uint32_t c = fb.seg_coarse[s];
+    const uint4 info = fb.cinfo[c];
+    const uint32_t e0 = info.x + (s - info.z) * kSegLen;
+    return Segment{c, e0, min(e0 + kSegLen, info.x + info.y)};
+}
+
+__global__ void __launch_bounds__(kSegWarps * 32) k_fine_count(FrameBufs fb) {
+    const FrameCtl* ctl = fb.ctl;
+    if (!ctl->plan_ok) return;
+    const uint32_t ns = ctl->num_segments;
+    const int lane = threadIdx.x & 31;
+    const uint32_t nw = (gridDim.x * blockDim.x) >> 5;
+    for (uint32_t s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; s < ns; s += nw) {
+        const Segment sg = segment_of(fb, s);
+        uint32_t cnt[16];
+#pragma unroll
+        for (int f = 0; f < 16; ++f) cnt[f] = 0u;
+        for (uint32_t e = sg.e0; e < sg.e1; e += 32) {
+            const uint32_t m = e + lane < sg.e1 ? fb.clist[e + lane].y : 0u;
+#pragma unroll
+            for (int f = 0; f < 16; ++f) cnt[f] += __popc(__ballot_sync(0xFFFFFFFFu, (m >> f) & 1u));
+        }
+        uint32_t mine = 0;
+#pragma unroll
+        for (int f = 0; f < 16; ++f)
+            if (lane == f) mine = cnt[f];
+        if (lane < 16) fb.seg_cnt[(uint64_t)s * 16 + lane] = mine;
+    }
+}
+
+// A CTA per coarse bin, a warp per bin of its 4x4: exclusive prefix over the bin's segments.
+__global__ void __launch_bounds__(512) k_fine_seg_scan(FrameBufs fb, GridParams gp, PlaceGeom pg) {
+    if (!fb.ctl->plan_ok) return;
+    const uint32_t c = blockIdx.x;
+    const uint4 info = fb.cinfo[c];
+    if (info.y == 0u) return;
+    const int lane = threadIdx.x & 31, f = threadIdx.x >> 5;
+    const uint32_t ns = (info.y + kSegLen - 1) / kSegLen;
+    uint32_t carry = 0;
+    for (uint32_t s0 = 0; s0 < ns; s0 += 32) {
+        const uint32_t s = s0 + lane;
+        uint32_t* p = fb.seg_cnt + (uint64_t)(info.z + s) * 16 + f;
+        const uint32_t v = s < ns ? *p : 0u;
+        uint32_t x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, x, o);
+            if (lane >= o) x += t;
+        }
+        if (s < ns) *p = carry + x - v;
+        carry += __shfl_sync(0xFFFFFFFFu, x, 31);
+    }
+    if (lane == 0) {
+        const uint32_t cy = c / pg.ctx, cx = c - cy * pg.ctx;
+        const uint32_t bx = cx * kCoarse + (f & 3), by = gp.row_begin + cy * kCoarse + (f >> 2);
+        if (bx < gp.tiles_x && by < gp.row_end) fb.ranges[(uint64_t)by * gp.tiles_x + bx] = make_uint2(0u, carry);
+    }
+}
+
 // One CTA: exclusive scan of the per-bin totals over the binned rows in row-major order.
-__global__ void __launch_bounds__(kRangesThreads) k_bin_ranges(FrameBufs fb, GridParams gp) {
+__global__ void __launch_bounds__(kRangesThreads) k_fine_ranges(FrameBufs fb, GridParams gp) {
     __shared__ uint32_t s_warp[32];
     __shared__ unsigned long long s_carry;
+    if (!fb.ctl->plan_ok) return;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t b0 = gp.row_begin * gp.tiles_x, b1 = gp.row_end * gp.tiles_x;
     if (tid == 0) s_carry = 0ull;
@@ -215,168 +468,55 @@ __global__ void __launch_bounds__(kRangesThreads) k_bin_ranges(FrameBufs fb, Gri
         if (tid == 0) s_carry += s_warp[31];
         __syncthreads();
     }
-    if (tid == 0) {
-        FrameCtl* ctl = fb.ctl;
-        const FrameCtl* cd = fb.ctl_depth;
-        const unsigned long long K = s_carry;
-        const uint32_t dmin = ctl->depth_min, dmax = ctl->depth_max;
-        ctl->num_keys = K;
-        ctl->depth_bits = dmax >= dmin ? bits_for((uint64_t)(dmax - dmin)) : 0u;
-        ctl->key_bits = gp.tile_bits;
-        ctl->packed = 0u;  // pairs are u32 Gaussian indices
-        ctl->idx_bits = cd->idx_bits;
-        ctl->final_buf = 0u;
-        ctl->passes_run = 0u;
-        const bool fits = K <= fb.key_capacity;
-        if (!fits) atomicOr(&ctl->error_flags, kErrCapacity);
-        if (cd->error_flags & kErrTimeout) atomicOr(&ctl->error_flags, kErrTimeout);
-        // a timed-out depth sort leaves the depth order undefined: draw nothing
-        ctl->plan_ok = (fits && (ctl->error_flags & kErrTimeout) == 0u) ? 1u : 0u;
-    }
 }
 
-// One lane's Gaussian of a batch, clipped to the band, with what the placement loop needs.
-struct BatchGauss {
-    uint32_t idx;   // Gaussian index
-    uint32_t xw;    // x0 | w << 16 (0: nothing in this band)
-    uint32_t yc;    // band-local y0 | pair count in the band << 16 (count <= kBandMaxBins)
-    uint32_t step;  // (32 / w) | (32 % w) << 16
-    float inv_w;    // 1 / w
-};
-
-// (o / w) | (o % w) << 8 for w in 1..32, o in 0..31, in shared memory
-struct DivTable {
-    uint16_t qr[33][32];
-};
-
-__device__ __forceinline__ BatchGauss batch_gauss(uint32_t g, uint2 r, uint32_t by0, uint32_t by1,
-                                                  const DivTable& dt) {
-    BatchGauss b{g, 0u, 0u, 0u, 0.0f};
-    const uint32_t y0 = max(r.y & 0xFFFFu, by0), y1 = min(r.y >> 16, by1);
-    const uint32_t x0 = r.x & 0xFFFFu, x1 = r.x >> 16;
-    if (x0 >= x1 || y0 >= y1) return b;
-    const uint32_t w = x1 - x0;
-    b.xw = x0 | (w << 16);
-    b.yc = (y0 - by0) | ((w * (y1 - y0)) << 16);
-    uint32_t sy, sx;
-    if (w <= 32u) {  // 32 = 31 + 1
-        const uint32_t d = dt.qr[w][31];
-        sy = d & 0xFFu;
-        sx = (d >> 8) + 1u;
-        if (sx == w) {
-            ++sy;
-            sx = 0u;
-        }
-    } else {
-        b.inv_w = 1.0f / (float)w;
-        divmod_small(32u, w, b.inv_w, sy, sx);
-    }
-    b.step = sy | (sx << 16);
-    return b;
-}
-
-// Persistent: every warp takes (band, chunk) items from a ticket, band-major. For an item, the
-// chunk's Gaussians in depth order, one at a time: the lanes take the Gaussian's bins in the
-// band (row-major), write each pair at its bin's cursor and advance the cursor. The rectangle
-// arithmetic of a batch of 32 Gaussians is done by their own lanes beforehand.
-__global__ void __launch_bounds__(kPlaceWarps * 32, 1) k_pair_place(FrameBufs fb, GridParams gp, PlaceGeom pg,
-                                                                    uint64_t n, const uint32_t* __restrict__ table) {
-    extern __shared__ uint32_t s_cur[];  // kBandMaxBins cursors per warp
-    __shared__ DivTable s_div;
-    FrameCtl* ctl = fb.ctl;
+__global__ void __launch_bounds__(kSegWarps * 32) k_fine_place(FrameBufs fb, GridParams gp, PlaceGeom pg) {
+    const FrameCtl* ctl = fb.ctl;
     if (!ctl->plan_ok) return;
-    for (uint32_t i = threadIdx.x; i < 33 * 32; i += blockDim.x) {
-        const uint32_t w = i >> 5, o = i & 31u;
-        s_div.qr[w][o] = w ? (uint16_t)((o / w) | ((o % w) << 8)) : (uint16_t)0;
-    }
-    __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint32_t* cur = s_cur + (size_t)warp * kBandMaxBins;
-    const FrameCtl* cd = fb.ctl_depth;
-    const unsigned long long* __restrict__ order = io_select(fb.gsort, cd->final_buf);
-    const unsigned long long imask = (1ull << cd->idx_bits) - 1ull;
+    const uint32_t ns = ctl->num_segments;
+    const int lane = threadIdx.x & 31;
+    const uint32_t lt = (1u << lane) - 1u;
     uint32_t* __restrict__ out = fb.pairs;
-    const uint32_t tx = gp.tiles_x, items = pg.nbands * pg.nchunks;
-    for (;;) {
-        uint32_t item = 0;
-        if (lane == 0) item = atomicAdd(&ctl->scan_ticket, 1u);
-        item = __shfl_sync(0xFFFFFFFFu, item, 0);
-        if (item >= items) break;
-        const uint32_t band = item / pg.nchunks, chunk = item - band * pg.nchunks;
-        const uint32_t by0 = gp.row_begin + band * pg.band_rows;
-        const uint32_t by1 = min(by0 + pg.band_rows, gp.row_end);
-        const uint64_t q0 = (uint64_t)chunk * pg.chunk_len;
-        const uint64_t q1 = min(q0 + (uint64_t)pg.chunk_len, n);
-        const uint32_t nb = (by1 - by0) * tx, bin0 = by0 * tx;
-        const uint32_t* __restrict__ trow = table + (uint64_t)chunk * tx * gp.tiles_y + bin0;
-        __syncwarp();  // the previous item is done with the cursors
-        for (uint32_t i = lane; i < nb; i += 32) cur[i] = trow[i] + fb.ranges[bin0 + i].x;
-        __syncwarp();
-        // batch i is placed while batch i+1's rectangles and indices load
-        uint64_t q = q0 + lane;
-        uint2 r0 = q < q1 ? fb.srect[q] : make_uint2(0u, 0u);
-        uint32_t g0 = q < q1 ? (uint32_t)(order[q] & imask) : kNone;
-        for (uint64_t qb = q0; qb < q1; qb += 32) {
-            q = qb + 32 + lane;
-            const uint2 r1 = q < q1 ? fb.srect[q] : make_uint2(0u, 0u);
-            const uint32_t g1 = q < q1 ? (uint32_t)(order[q] & imask) : kNone;
-            const BatchGauss mine = batch_gauss(g0, r0, by0, by1, s_div);
-            uint32_t todo = __ballot_sync(0xFFFFFFFFu, mine.xw != 0u);
-            while (todo) {  // this batch's Gaussians in depth order
-                const int src = __ffs(todo) - 1;
-                todo &= todo - 1u;
-                const uint32_t gg = __shfl_sync(0xFFFFFFFFu, mine.idx, src);
-                const uint32_t xw = __shfl_sync(0xFFFFFFFFu, mine.xw, src);
-                const uint32_t yc = __shfl_sync(0xFFFFFFFFu, mine.yc, src);
-                const uint32_t st = __shfl_sync(0xFFFFFFFFu, mine.step, src);
-                const float inv_w = __shfl_sync(0xFFFFFFFFu, mine.inv_w, src);
-                const uint32_t x0 = xw & 0xFFFFu, w = xw >> 16, ly0 = yc & 0xFFFFu, cnt = yc >> 16;
-                const uint32_t sy = st & 0xFFFFu, sx = st >> 16;
-                uint32_t dy, dx;  // this lane's first bin
-                if (w <= 32u) {
-                    const uint32_t d = s_div.qr[w][lane];
-                    dy = d & 0xFFu;
-                    dx = d >> 8;
-                } else {
-                    divmod_small((uint32_t)lane, w, inv_w, dy, dx);
-                }
-                for (uint32_t j = lane; j < cnt; j += 32) {
-                    const uint32_t li = (ly0 + dy) * tx + x0 + dx;
-                    const uint32_t pos = cur[li];
-                    cur[li] = pos + 1u;
-                    out[pos] = gg;
-                    dx += sx;
-                    dy += sy;
-                    if (dx >= w) {
-                        dx -= w;
-                        ++dy;
-                    }
-                }
-                __syncwarp();  // cursor updates visible to every lane before the next Gaussian
+    const uint32_t nw = (gridDim.x * blockDim.x) >> 5;
+    for (uint32_t s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; s < ns; s += nw) {
+        const Segment sg = segment_of(fb, s);
+        const uint32_t cy = sg.coarse / pg.ctx, cx = sg.coarse - cy * pg.ctx;
+        uint32_t mine = 0;
+        if (lane < 16) {
+            const uint32_t bx = cx * kCoarse + (lane & 3), by = gp.row_begin + cy * kCoarse + (lane >> 2);
+            if (bx < gp.tiles_x && by < gp.row_end)
+                mine = fb.ranges[(uint64_t)by * gp.tiles_x + bx].x + fb.seg_cnt[(uint64_t)s * 16 + lane];
+        }
+        uint32_t off[16];  // write cursor of each bin of the 4x4
+#pragma unroll
+        for (int f = 0; f < 16; ++f) off[f] = __shfl_sync(0xFFFFFFFFu, mine, f);
+        for (uint32_t e = sg.e0; e < sg.e1; e += 32) {
+            const uint2 v = e + lane < sg.e1 ? fb.clist[e + lane] : make_uint2(0u, 0u);
+#pragma unroll
+            for (int f = 0; f < 16; ++f) {
+                const bool bit = (v.y >> f) & 1u;
+                const uint32_t b = __ballot_sync(0xFFFFFFFFu, bit);
+                if (bit) out[off[f] + __popc(b & lt)] = v.x;
+                off[f] += __popc(b);
             }
-            r0 = r1;
-            g0 = g1;
         }
     }
 }
 
 }  // namespace
 
-cudaError_t place_geometry(const GridParams& gp, uint64_t n, PlaceGeom* out) {
+cudaError_t place_geometry(const GridParams& gp, uint64_t n, uint64_t capacity, PlaceGeom* out) {
     PlaceGeom g{};
-    const uint32_t tx = gp.tiles_x, rows = gp.row_end - gp.row_begin;
-    if (tx > kBandMaxBins || tx + 1 > kCountMaxCells / 2) return cudaErrorInvalidValue;  // too many bins per row
-    // placement bands: about kBandTargetBins bins each
-    uint32_t br = kBandTargetBins / tx;
-    if (br < 1) br = 1;
-    if (br * tx > kBandMaxBins) br = kBandMaxBins / tx;
-    g.nbands = rows == 0 ? 1u : (rows + br - 1) / br;
-    g.band_rows = rows == 0 ? 0u : (rows + g.nbands - 1) / g.nbands;
-    // count bands: the largest row ranges whose difference table fits
-    const uint32_t cmax = kCountMaxCells / (tx + 1) - 1;
-    g.ncbands = rows == 0 ? 1u : (rows + cmax - 1) / cmax;
-    g.cband_rows = rows == 0 ? 0u : (rows + g.ncbands - 1) / g.ncbands;
-    g.count_smem = (tx + 1) * (g.cband_rows + 1) * 4u;
+    const uint32_t rows = gp.row_end - gp.row_begin;
+    g.ctx = (gp.tiles_x + kCoarse - 1) / kCoarse;
+    g.cty = (rows + kCoarse - 1) / kCoarse;
+    g.ncoarse = g.ctx * g.cty;
+    if (g.ctx > kBandMax || g.ncoarse > kCoarseMax) return cudaErrorInvalidValue;  // too many bins
+    // placement bands: whole coarse rows, at most kBandMax coarse bins
+    const uint32_t br = g.ctx ? kBandMax / g.ctx : 1u;
+    g.nbands = g.cty == 0 ? 1u : (g.cty + br - 1) / br;
+    g.band_rows = g.cty == 0 ? 0u : (g.cty + g.nbands - 1) / g.nbands;
+    g.count_smem = (g.ncoarse > 0u ? g.ncoarse : 1u) * 4u;
     // chunks of depth order
     uint64_t chunks = (n + kChunkTarget - 1) / kChunkTarget;
     if (chunks > kMaxChunks) chunks = kMaxChunks;
@@ -385,8 +525,12 @@ cudaError_t place_geometry(const GridParams& gp, uint64_t n, PlaceGeom* out) {
     chunks = n == 0 ? 1 : (n + len - 1) / len;
     g.nchunks = (uint32_t)chunks;
     g.chunk_len = (uint32_t)len;
-    g.place_ctas = (uint32_t)device_sm_count();
-    g.table_words = chunks * tx * gp.tiles_y;
+    const uint32_t sms = (uint32_t)device_sm_count();
+    g.place_ctas = sms;
+    g.seg_ctas = sms * (2048u / (kSegWarps * 32u));
+    g.table_words = chunks * (g.ncoarse > 0u ? g.ncoarse : 1u);
+    // entries <= pairs <= capacity; a coarse list of c entries has ceil(c / kSegLen) segments
+    g.max_segments = capacity / kSegLen + g.ncoarse + 1;
 
     static int attr_set[128] = {0};
     int dev = 0;
@@ -394,9 +538,9 @@ cudaError_t place_geometry(const GridParams& gp, uint64_t n, PlaceGeom* out) {
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
     if (!attr_set[dev]) {
-        e = cudaFuncSetAttribute(k_pair_count, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kCountMaxCells * 4));
+        e = cudaFuncSetAttribute(k_coarse_count, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kCoarseMax * 4));
         if (e != cudaSuccess) return e;
-        e = cudaFuncSetAttribute(k_pair_place, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPlaceSmem);
+        e = cudaFuncSetAttribute(k_coarse_place, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPlaceSmem);
         if (e != cudaSuccess) return e;
         attr_set[dev] = 1;
     }
@@ -404,33 +548,43 @@ cudaError_t place_geometry(const GridParams& gp, uint64_t n, PlaceGeom* out) {
     return cudaSuccess;
 }
 
-cudaError_t launch_pair_count(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
-                              uint32_t* table, cudaStream_t stream) {
+cudaError_t launch_coarse_count(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
+                                cudaStream_t stream) {
     if (n == 0 || gp.row_end <= gp.row_begin) return cudaSuccess;
-    unsigned blocks = (unsigned)((n + 255) / 256);
-    const unsigned cap = (unsigned)device_sm_count() * 8;
-    if (blocks > cap) blocks = cap;
-    k_depth_rects<<<blocks, 256, 0, stream>>>(fb, n);
-    k_pair_count<<<pg.nchunks * pg.ncbands, kCountThreads, pg.count_smem, stream>>>(fb, gp, pg, n, table);
+    k_coarse_count<<<pg.nchunks, kCountThreads, pg.count_smem, stream>>>(fb, gp, pg, n);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    k_coarse_scan<<<(pg.ncoarse + 31) / 32, 1024, 0, stream>>>(fb, pg);
     return cudaGetLastError();
 }
 
-cudaError_t launch_pair_ranges(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
-                               uint32_t* table, cudaStream_t stream) {
-    const uint32_t nbins = (gp.row_end - gp.row_begin) * gp.tiles_x;
-    if (n > 0 && nbins > 0) {
-        k_pair_scan<<<(nbins + 31) / 32, 1024, 0, stream>>>(gp, pg, table, fb.ranges);
-        cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) return e;
-    }
-    k_bin_ranges<<<1, kRangesThreads, 0, stream>>>(fb, gp);
+cudaError_t launch_coarse_ranges(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
+                                 cudaStream_t stream) {
+    // also when nothing is binned: K, the flags and plan_ok are set here
+    PlaceGeom p = pg;
+    if (n == 0 || gp.row_end <= gp.row_begin) p.ncoarse = 0;  // the coarse totals were not counted
+    k_coarse_ranges<<<1, kRangesThreads, 0, stream>>>(fb, gp, p);
     return cudaGetLastError();
 }
 
-cudaError_t launch_pair_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
-                              const uint32_t* table, cudaStream_t stream) {
+cudaError_t launch_coarse_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
+                                cudaStream_t stream) {
     if (n == 0 || gp.row_end <= gp.row_begin) return cudaSuccess;
-    k_pair_place<<<pg.place_ctas, kPlaceWarps * 32, kPlaceSmem, stream>>>(fb, gp, pg, n, table);
+    k_coarse_place<<<pg.place_ctas, kPlaceWarps * 32, kPlaceSmem, stream>>>(fb, gp, pg, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fine_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
+                              cudaStream_t stream) {
+    if (n == 0 || gp.row_end <= gp.row_begin) return cudaSuccess;
+    k_fine_count<<<pg.seg_ctas, kSegWarps * 32, 0, stream>>>(fb);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    k_fine_seg_scan<<<pg.ncoarse, 512, 0, stream>>>(fb, gp, pg);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    k_fine_ranges<<<1, kRangesThreads, 0, stream>>>(fb, gp);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    k_fine_place<<<pg.seg_ctas, kSegWarps * 32, 0, stream>>>(fb, gp, pg);
     return cudaGetLastError();
 }
 

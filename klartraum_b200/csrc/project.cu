@@ -95,17 +95,23 @@ __device__ __forceinline__ uint32_t bin_span(float px, float py, float z, const 
     return (uint32_t)(x1 - x0) * (uint32_t)(y1 - y0);
 }
 
-// Block-wide min/max of the depth bits of counted Gaussians, and their number.
-__device__ __forceinline__ void reduce_depth(bool counted, uint32_t flip, FrameCtl* ctl) {
+// Block-wide min/max of the depth bits of counted Gaussians, their number and their bin count.
+__device__ __forceinline__ void reduce_depth(uint32_t count, uint32_t flip, FrameCtl* ctl) {
     __shared__ uint32_t s_min[32], s_max[32];
+    __shared__ unsigned long long s_sum[32];
+    const bool counted = count > 0u;
     uint32_t dmin = counted ? flip : 0xFFFFFFFFu;
     uint32_t dmax = counted ? flip : 0u;
     dmin = __reduce_min_sync(0xFFFFFFFFu, dmin);
     dmax = __reduce_max_sync(0xFFFFFFFFu, dmax);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    unsigned long long sum = count;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
     if (lane == 0) {
         s_min[warp] = dmin;
         s_max[warp] = dmax;
+        s_sum[warp] = sum;
     }
     int vis = __syncthreads_count(counted);
     if (warp == 0) {
@@ -114,10 +120,14 @@ __device__ __forceinline__ void reduce_depth(bool counted, uint32_t flip, FrameC
         dmax = lane < nw ? s_max[lane] : 0u;
         dmin = __reduce_min_sync(0xFFFFFFFFu, dmin);
         dmax = __reduce_max_sync(0xFFFFFFFFu, dmax);
+        sum = lane < nw ? s_sum[lane] : 0ull;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
         if (lane == 0 && vis > 0) {
             atomicMin(&ctl->depth_min, dmin);
             atomicMax(&ctl->depth_max, dmax);
             atomicAdd(&ctl->num_visible, (unsigned)vis);
+            atomicAdd(&ctl->pair_total, sum);
         }
     }
 }
@@ -266,7 +276,7 @@ __global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams
         flip = __float_as_uint(z) ^ 0x80000000u;
         store_outputs(i, px, py, z, ci, rgb[0], rgb[1], rgb[2], P.w, count, rect, fb);
     }
-    reduce_depth(count > 0, flip, fb.ctl);
+    reduce_depth(count, flip, fb.ctl);
 }
 
 // Projected records supplied by the caller (kt_gaussian2d layout) -> internal buffers.
@@ -283,7 +293,7 @@ __global__ void __launch_bounds__(256) k_load_projected(const float* __restrict_
         flip = __float_as_uint(z) ^ 0x80000000u;
         store_outputs(i, px, py, z, ci, g[8], g[9], g[10], g[11], count, rect, fb);
     }
-    reduce_depth(count > 0, flip, fb.ctl);
+    reduce_depth(count, flip, fb.ctl);
 }
 
 // Array-of-structs Gaussian3D (59 floats) -> device planes.
