@@ -80,6 +80,8 @@ struct PathWs {
     // pair placement (default path), allocated on first use
     uint32_t* ctable = nullptr;  // entries per (chunk, coarse bin), then their prefix over chunks
     uint64_t ctable_words = 0;
+    uint32_t* gtable = nullptr;  // entries per (group of chunks, coarse bin), then their prefix over groups
+    uint64_t gtable_words = 0;
     uint4* cinfo = nullptr;      // per coarse bin: list start, entries, first segment
     uint64_t cinfo_n = 0;
     uint2* clist = nullptr;      // (Gaussian, 4x4 bin mask) by coarse bin
@@ -216,8 +218,8 @@ uint32_t ntiles(const kt_gs_ctx* c) { return c->gp.tiles_x * c->gp.tiles_y; }
 void free_path(PathWs& w) {
     dfree(w.rec); dfree(w.counts); dfree(w.rect); dfree(w.srect); dfree(w.depth); dfree(w.gsort[0]);
     dfree(w.gsort[1]);
-    dfree(w.pairs); dfree(w.ctable); dfree(w.cinfo); dfree(w.clist); dfree(w.seg_coarse); dfree(w.seg_cnt);
-    w.ctable_words = w.cinfo_n = w.clist_n = w.seg_n = 0;
+    dfree(w.pairs); dfree(w.ctable); dfree(w.gtable); dfree(w.cinfo); dfree(w.clist); dfree(w.seg_coarse); dfree(w.seg_cnt);
+    w.ctable_words = w.gtable_words = w.cinfo_n = w.clist_n = w.seg_n = 0;
     dfree(w.sort_status); dfree(w.sort_table); dfree(w.ranges); dfree(w.ctl); dfree(w.ctl_depth);
     dfree(w.keys[0]); dfree(w.keys[1]); dfree(w.vals[0]); dfree(w.vals[1]); dfree(w.key_status);
     dfree(w.key_table); dfree(w.offsets); dfree(w.scan_status);
@@ -355,6 +357,7 @@ FrameBufs frame_bufs(const PathWs& w) {
     fb.gsort[1] = w.gsort[1];
     fb.pairs = w.pairs;
     fb.ctable = w.ctable;
+    fb.gtable = w.gtable;
     fb.cinfo = w.cinfo;
     fb.clist = w.clist;
     fb.seg_coarse = w.seg_coarse;
@@ -437,6 +440,13 @@ kt_status prepare_frame(kt_gs_ctx* c, PathWs& w, uint64_t n, bool graph, FramePl
         w.ctable_words = 0;
         KT_TRY_CUDA(c, cudaMalloc(&w.ctable, sizeof(uint32_t) * fp.pg.table_words));
         w.ctable_words = fp.pg.table_words;
+        ++w.buf_gen;
+    }
+    if (fp.pg.gtable_words > w.gtable_words) {
+        dfree(w.gtable);
+        w.gtable_words = 0;
+        KT_TRY_CUDA(c, cudaMalloc(&w.gtable, sizeof(uint32_t) * fp.pg.gtable_words));
+        w.gtable_words = fp.pg.gtable_words;
         ++w.buf_gen;
     }
     if (fp.pg.ncoarse > w.cinfo_n) {
@@ -537,7 +547,6 @@ kt_status record_frame(kt_gs_ctx* c, PathWs& w, Source src, uint64_t n, const Ca
         // entries per (chunk of depth order, coarse bin), their prefix over chunks, K, the coarse
         // list starts and segments
         KT_TRY_CUDA(c, launch_coarse_count(fb, c->gp, fp.pg, n, stream));
-        KT_TRY_CUDA(c, launch_coarse_ranges(fb, c->gp, fp.pg, n, stream));
         if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[3], stream));
         // coarse lists in depth order
         KT_TRY_CUDA(c, launch_coarse_place(fb, c->gp, fp.pg, n, stream));
@@ -928,11 +937,11 @@ kt_status kt_gs_frame_stats(kt_gs_ctx* c, uint32_t path, kt_gs_stats* out) {
     out->depth_min_bits = h.depth_min;
     out->depth_max_bits = h.depth_max;
     out->status_bytes = (uint32_t)kCtlHeaderBytes;
-    // init, project, depth keys, plan, the depth passes, coarse count, coarse scan, coarse
-    // ranges, coarse placement, bin count, segment scan, bin ranges, pair placement, totals,
-    // rasterise; or init, project, scan/emit, plan, the key passes, ranges, totals, rasterise
+    // init, project, depth keys, plan, the depth passes, coarse count, coarse scan (+ list
+    // starts), coarse placement, bin count (+ bin ranges), pair placement, totals, rasterise; or
+    // init, project, scan/emit, plan, the key passes, ranges, totals, rasterise
     out->launches = w.keys_frame ? 7 + key_passes(c) * sort_pass_launches(w.cap, false)
-                                 : 14 + kDepthPasses * sort_pass_launches(w.frame_n, true);
+                                 : 11 + kDepthPasses * sort_pass_launches(w.frame_n, true);
     out->packed = h.packed;
     out->idx_bits = h.idx_bits;
     PlaceGeom pg{};

@@ -59,6 +59,8 @@ struct FrameCtl {
     unsigned int idx_bits;            // bits of the index field of a packed element (0 unpacked)
     unsigned int num_entries;         // (Gaussian, coarse bin) entries of the pair placement
     unsigned int num_segments;        // segments of the coarse lists (second placement level)
+    unsigned int done_scan;           // CTAs of the coarse scan that finished
+    unsigned int done_count;          // CTAs of the bin count that finished
     unsigned int pass_ticket[kMaxPasses];
     unsigned int pass_run[kMaxPasses];
     unsigned int pass_src[kMaxPasses];
@@ -117,12 +119,15 @@ struct PlaceGeom {
     uint32_t ncoarse;         // ctx * cty
     uint32_t nchunks;         // chunks of consecutive Gaussians in depth order
     uint32_t chunk_len;       // Gaussians per chunk (the last may be shorter)
+    uint32_t group;           // chunks per count CTA (a group)
+    uint32_t ngroups;
     uint32_t nbands;          // placement bands of coarse rows (one warp's cursors each)
     uint32_t band_rows;       // coarse rows per placement band (the last may be shorter)
     uint32_t count_smem;      // dynamic shared memory of a count CTA
     uint32_t place_ctas;      // persistent coarse-placement CTAs
     uint32_t seg_ctas;        // CTAs of the segment kernels
     uint64_t table_words;     // u32 words of table[chunk][coarse bin]
+    uint64_t gtable_words;    // u32 words of gtable[group][coarse bin]
     uint64_t max_segments;    // segments the key capacity can produce, at most
 };
 
@@ -135,7 +140,8 @@ struct FrameBufs {
     unsigned long long* gsort[2];  // Gaussians by depth: (depth - min) << idx_bits | index
     uint32_t* pairs;               // Gaussian index of every (bin, Gaussian) pair, in bin order
     // pair placement: (chunk, coarse bin) table, coarse lists and their segments
-    uint32_t* ctable;              // entries per (chunk, coarse bin), then their prefix over chunks
+    uint32_t* ctable;              // per (chunk, coarse bin): prefix of the entries over the group's chunks
+    uint32_t* gtable;              // per (group, coarse bin): entries, then their prefix over groups
     uint4* cinfo;                  // per coarse bin: list start, entries, first segment, 0
     uint2* clist;                  // (Gaussian index, 4x4 bin mask) by coarse bin, depth order
     uint32_t* seg_coarse;          // coarse bin of every segment

@@ -49,12 +49,10 @@ cudaError_t launch_frame_totals(const FrameCtl* ctl, const FrameCtl* ctl_depth, 
 
 // place.cu: pairs by bin from the Gaussians in depth order (two-level counting sort, no pair sort)
 cudaError_t place_geometry(const GridParams& gp, uint64_t n, uint64_t capacity, PlaceGeom* out);
-// rectangles in depth order; table[chunk][coarse bin] and its prefix over chunks
+// rectangles in depth order; coarse entries per (chunk, coarse bin) and their prefix; K and the
+// capacity check (FrameCtl::plan_ok); coarse list starts and segments
 cudaError_t launch_coarse_count(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
                                 cudaStream_t stream);
-// K and the capacity check (FrameCtl::plan_ok); coarse list starts and segments
-cudaError_t launch_coarse_ranges(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
-                                 cudaStream_t stream);
 // every (Gaussian, coarse bin) entry at its place in its coarse list
 cudaError_t launch_coarse_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
                                 cudaStream_t stream);

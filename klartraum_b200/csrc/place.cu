@@ -9,24 +9,26 @@
 //
 // Level 1, coarse bins of 4x4 bins (a Gaussian meets 3.4 of them on average where it meets 20
 // bins):
-//   k_coarse_count   one CTA per chunk (a run of depth order): the Gaussians' rectangles are
-//                    gathered into depth order (srect) and every coarse bin a rectangle meets is
-//                    counted in shared memory: table[chunk][coarse bin].
-//   k_coarse_scan    per coarse bin, the exclusive prefix of the table over chunks (in place)
-//                    and the bin's entry total.
-//   k_coarse_ranges  one CTA: K (the projection's pair total) and the capacity check; exclusive
-//                    scans of the coarse totals (list starts) and of their segment counts
-//                    (kSegLen entries per segment); the segment -> coarse bin map.
+//   k_coarse_count   one CTA per group of 8 chunks (a chunk is a run of depth order): the
+//                    Gaussians' rectangles are gathered into depth order (srect) and every
+//                    coarse bin a rectangle meets is counted in shared memory per chunk:
+//                    table[chunk][coarse bin] (prefix over the group's chunks) and
+//                    gtable[group][coarse bin] (the group's total).
+//   k_coarse_scan    per coarse bin, the exclusive prefix of gtable over groups (in place) and
+//                    the bin's entry total; the last CTA to finish then computes K (the
+//                    projection's pair total) and the capacity check, the exclusive scans of the
+//                    coarse totals (list starts) and of their segment counts (kSegLen entries per
+//                    segment), and the segment -> coarse bin map.
 //   k_coarse_place   persistent warps over (band, chunk) items: 32 Gaussians at a time, their
 //                    (Gaussian, coarse bin) entries flattened in depth order and taken 32 at a
 //                    time; lanes with equal coarse bins are ranked by lane (ballot match) and
 //                    written at the bin's cursor as (Gaussian index, mask of the 4x4 bins met).
 // Level 2, the bins of a coarse bin:
-//   k_fine_count     a warp per segment of a coarse list: pairs per bin of the 4x4 (ballots).
-//   k_fine_seg_scan  a CTA per coarse bin: per bin of its 4x4, the exclusive prefix of the
-//                    segments' counts (in place) and the bin's total.
-//   k_fine_ranges    one CTA: exclusive scan of the bin totals -> ranges {start, end} (empty
-//                    bins keep {0, 0}, as the reference's zeroed StartAndEnd buffer).
+//   k_fine_count     a warp per segment of a coarse list: pairs per bin of the 4x4 (ballot
+//                    counts). The last segment of a coarse bin to be counted turns its bins'
+//                    segment counts into exclusive prefixes (in place) and bin totals; the last
+//                    CTA to finish scans the totals into ranges {start, end} (empty bins keep
+//                    {0, 0}, as the reference's zeroed StartAndEnd buffer).
 //   k_fine_place     a warp per segment, 32 entries at a time: for each bin of the 4x4 a ballot
 //                    ranks the entries that meet it; each writes its Gaussian at the bin's
 //                    cursor + rank (consecutive addresses per bin).
@@ -44,9 +46,11 @@ constexpr uint32_t kCoarse = 4;                // bins per side of a coarse bin
 constexpr uint32_t kChunkTarget = 512;         // Gaussians per chunk of depth order, about
 constexpr uint32_t kMaxChunks = 4096;
 constexpr uint32_t kCountThreads = 512;
-constexpr uint32_t kCoarseMax = 16384;         // coarse bins of a frame (count CTA: 64 KB of counters)
+constexpr uint32_t kCoarseMax = 16384;         // coarse bins x chunks of a count CTA (64 KB of counters)
+constexpr uint32_t kGroupMax = 8;              // chunks of a count CTA
 constexpr uint32_t kBandMax = 1024;            // coarse bins of a placement band (4 KB of cursors per warp)
-constexpr uint32_t kPlaceWarps = 16;           // warps of a coarse-placement CTA (one CTA per SM)
+constexpr uint32_t kPlaceWarps = 16;           // warps of a coarse-placement CTA
+constexpr uint32_t kPlaceCtasPerSm = 1;
 constexpr uint32_t kPlaceSmem = kPlaceWarps * kBandMax * 4;
 constexpr uint32_t kSegLen = 512;              // entries of a segment of a coarse list
 constexpr uint32_t kSegWarps = 8;              // warps of a segment-kernel CTA
@@ -82,43 +86,75 @@ __device__ __forceinline__ bool local_rect(uint2 r, const GridParams& gp, uint32
 
 // ------------------------------------------------------------------- level 1
 
+// One CTA per group of chunks: the group's Gaussians counted per (chunk, coarse bin) in shared
+// memory; table[chunk][bin] <- prefix over the group's earlier chunks, gtable[group][bin] <- the
+// group's total.
 __global__ void __launch_bounds__(kCountThreads) k_coarse_count(FrameBufs fb, GridParams gp, PlaceGeom pg,
                                                                 uint64_t n) {
-    extern __shared__ uint32_t s_cnt[];
-    const uint32_t chunk = blockIdx.x;
-    for (uint32_t i = threadIdx.x; i < pg.ncoarse; i += kCountThreads) s_cnt[i] = 0u;
+    extern __shared__ uint32_t s_cnt[];  // [group][ncoarse]
+    const uint32_t c0 = blockIdx.x * pg.group, gk = min(pg.group, pg.nchunks - c0);
+    const uint32_t words = gk * pg.ncoarse;
+    for (uint32_t i = threadIdx.x; i < words; i += kCountThreads) s_cnt[i] = 0u;
     __syncthreads();
     const FrameCtl* cd = fb.ctl_depth;
     const unsigned long long* __restrict__ order = io_select(fb.gsort, cd->final_buf);
     const unsigned long long imask = (1ull << cd->idx_bits) - 1ull;
-    const uint64_t q0 = (uint64_t)chunk * pg.chunk_len;
-    const uint64_t q1 = min(q0 + (uint64_t)pg.chunk_len, n);
-    for (uint64_t q = q0 + threadIdx.x; q < q1; q += kCountThreads) {
-        const uint32_t g = (uint32_t)(order[q] & imask);
-        const uint2 r = fb.counts[g] != 0u ? fb.rect[g] : make_uint2(0u, 0u);
-        fb.srect[q] = r;
-        uint32_t x0, x1, y0, y1;
-        if (!local_rect(r, gp, x0, x1, y0, y1)) continue;
-        const uint32_t cx0 = x0 / kCoarse, cx1 = (x1 + kCoarse - 1) / kCoarse;
-        const uint32_t cy0 = y0 / kCoarse, cy1 = (y1 + kCoarse - 1) / kCoarse;
-        for (uint32_t cy = cy0; cy < cy1; ++cy)
-            for (uint32_t cx = cx0; cx < cx1; ++cx) atomicAdd(&s_cnt[cy * pg.ctx + cx], 1u);
+    const uint64_t q0 = (uint64_t)c0 * pg.chunk_len;
+    const uint64_t q1 = min(q0 + (uint64_t)gk * pg.chunk_len, n);
+    constexpr int kU = 4;  // Gaussians in flight per thread
+    for (uint64_t qb = q0 + threadIdx.x; qb < q1; qb += kU * kCountThreads) {
+        uint32_t g[kU];
+        uint2 r[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const uint64_t q = qb + (uint64_t)u * kCountThreads;
+            g[u] = q < q1 ? (uint32_t)(order[q] & imask) : 0xFFFFFFFFu;
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+            r[u] = (g[u] != 0xFFFFFFFFu && fb.counts[g[u]] != 0u) ? fb.rect[g[u]] : make_uint2(0u, 0u);
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const uint64_t q = qb + (uint64_t)u * kCountThreads;
+            if (q >= q1) break;
+            fb.srect[q] = r[u];
+            uint32_t x0, x1, y0, y1;
+            if (!local_rect(r[u], gp, x0, x1, y0, y1)) continue;
+            uint32_t* cnt = s_cnt + ((uint32_t)(q - q0) / pg.chunk_len) * pg.ncoarse;
+            const uint32_t cx0 = x0 / kCoarse, cx1 = (x1 + kCoarse - 1) / kCoarse;
+            const uint32_t cy0 = y0 / kCoarse, cy1 = (y1 + kCoarse - 1) / kCoarse;
+            for (uint32_t cy = cy0; cy < cy1; ++cy)
+                for (uint32_t cx = cx0; cx < cx1; ++cx) atomicAdd(&cnt[cy * pg.ctx + cx], 1u);
+        }
     }
     __syncthreads();
-    uint32_t* __restrict__ trow = fb.ctable + (uint64_t)chunk * pg.ncoarse;
-    for (uint32_t i = threadIdx.x; i < pg.ncoarse; i += kCountThreads) trow[i] = s_cnt[i];
+    uint32_t* __restrict__ trow = fb.ctable + (uint64_t)c0 * pg.ncoarse;
+    for (uint32_t b = threadIdx.x; b < pg.ncoarse; b += kCountThreads) {
+        uint32_t run = 0;
+        for (uint32_t k = 0; k < gk; ++k) {
+            const uint32_t v = s_cnt[k * pg.ncoarse + b];
+            trow[(uint64_t)k * pg.ncoarse + b] = run;
+            run += v;
+        }
+        fb.gtable[(uint64_t)blockIdx.x * pg.ncoarse + b] = run;
+    }
 }
 
-// 32 coarse bins per CTA (lanes), the chunks split into 32 slices (warps).
-__global__ void __launch_bounds__(1024) k_coarse_scan(FrameBufs fb, PlaceGeom pg) {
+// 32 coarse bins per CTA (lanes), the groups split into 32 slices (warps): gtable becomes the
+// exclusive prefix over groups, cinfo[bin].y the bin's entry total. The last CTA to finish then
+// computes the coarse list starts and segments (coarse_ranges, below).
+__device__ void coarse_ranges(const FrameBufs& fb, const GridParams& gp, uint32_t ncoarse);
+
+__global__ void __launch_bounds__(1024) k_coarse_scan(FrameBufs fb, GridParams gp, PlaceGeom pg) {
     __shared__ uint32_t s_seg[32][33];
+    __shared__ uint32_t s_last;
     const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
     const uint64_t B = pg.ncoarse;
     const uint32_t b = blockIdx.x * 32 + lane;
     const bool live = b < pg.ncoarse;
-    const uint32_t per = (pg.nchunks + 31) / 32;
-    const uint32_t c0 = min(seg * per, pg.nchunks), c1 = min(c0 + per, pg.nchunks);
-    uint32_t* __restrict__ col = fb.ctable + b;
+    const uint32_t per = (pg.ngroups + 31) / 32;
+    const uint32_t c0 = min(seg * per, pg.ngroups), c1 = min(c0 + per, pg.ngroups);
+    uint32_t* __restrict__ col = fb.gtable + b;
     uint32_t sum = 0;
     if (live) {
         uint32_t c = c0;
@@ -131,13 +167,21 @@ __global__ void __launch_bounds__(1024) k_coarse_scan(FrameBufs fb, PlaceGeom pg
     __syncthreads();
     uint32_t base = 0;
     for (int s = 0; s < seg; ++s) base += s_seg[s][lane];
-    if (!live) return;
-    if (seg == 31) fb.cinfo[b] = make_uint4(0u, base + sum, 0u, 0u);  // the bin's total
-    for (uint32_t c = c0; c < c1; ++c) {
-        const uint32_t v = col[(uint64_t)c * B];
-        col[(uint64_t)c * B] = base;
-        base += v;
+    if (live) {
+        if (seg == 31) fb.cinfo[b] = make_uint4(0u, base + sum, 0u, 0u);  // the bin's total
+        for (uint32_t c = c0; c < c1; ++c) {
+            const uint32_t v = col[(uint64_t)c * B];
+            col[(uint64_t)c * B] = base;
+            base += v;
+        }
     }
+    __threadfence();  // every thread's writes are visible before the CTA's ticket
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(&fb.ctl->done_scan, 1u) == gridDim.x - 1u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    coarse_ranges(fb, gp, pg.ncoarse);
 }
 
 // Exclusive block scan of two counters per thread; returns the prefixes, adds the block totals
@@ -184,7 +228,9 @@ __device__ __forceinline__ uint2 block_scan2(uint32_t a, uint32_t b, uint32_t* s
     return out;
 }
 
-__global__ void __launch_bounds__(kRangesThreads) k_coarse_ranges(FrameBufs fb, GridParams gp, PlaceGeom pg) {
+// K and the capacity check; list starts and segments of the coarse bins (entry totals in
+// cinfo[.].y, written by other CTAs of the same kernel or by an earlier one). One CTA.
+__device__ void coarse_ranges(const FrameBufs& fb, const GridParams& gp, uint32_t ncoarse) {
     __shared__ uint32_t s_a[32], s_b[32];
     __shared__ uint32_t s_ok;
     FrameCtl* ctl = fb.ctl;
@@ -210,14 +256,14 @@ __global__ void __launch_bounds__(kRangesThreads) k_coarse_ranges(FrameBufs fb, 
     __syncthreads();
     if (!s_ok) return;  // the lists and segments below are sized by the capacity
     unsigned long long carry_e = 0, carry_s = 0;
-    constexpr uint32_t kRound = kRangesThreads * kRangesItems;
-    for (uint32_t r0 = 0; r0 < pg.ncoarse; r0 += kRound) {
+    const uint32_t round = blockDim.x * kRangesItems;
+    for (uint32_t r0 = 0; r0 < ncoarse; r0 += round) {
         const uint32_t first = r0 + (uint32_t)tid * kRangesItems;
         uint32_t cnt[kRangesItems];
         uint32_t ne = 0, ns = 0;
 #pragma unroll
         for (int i = 0; i < kRangesItems; ++i) {
-            cnt[i] = first + i < pg.ncoarse ? fb.cinfo[first + i].y : 0u;
+            cnt[i] = first + i < ncoarse ? __ldcg(&fb.cinfo[first + i].y) : 0u;
             ne += cnt[i];
             ns += (cnt[i] + kSegLen - 1) / kSegLen;
         }
@@ -225,9 +271,9 @@ __global__ void __launch_bounds__(kRangesThreads) k_coarse_ranges(FrameBufs fb, 
         uint32_t e = st.x, s = st.y;
 #pragma unroll
         for (int i = 0; i < kRangesItems; ++i) {
-            if (first + i >= pg.ncoarse) break;
+            if (first + i >= ncoarse) break;
             const uint32_t k = (cnt[i] + kSegLen - 1) / kSegLen;
-            fb.cinfo[first + i] = make_uint4(e, cnt[i], s, 0u);
+            fb.cinfo[first + i] = make_uint4(e, cnt[i], s, 0u);  // .w: segments counted (bin count)
             for (uint32_t j = 0; j < k; ++j) fb.seg_coarse[s + j] = first + i;
             e += cnt[i];
             s += k;
@@ -239,12 +285,17 @@ __global__ void __launch_bounds__(kRangesThreads) k_coarse_ranges(FrameBufs fb, 
     }
 }
 
+// Frames with nothing to bin: K, the flags and plan_ok.
+__global__ void __launch_bounds__(kRangesThreads) k_coarse_ranges(FrameBufs fb, GridParams gp) {
+    coarse_ranges(fb, gp, 0u);
+}
+
 // Persistent: every warp takes (band, chunk) items from a ticket, band-major. For an item, the
 // chunk's Gaussians 32 at a time (one per lane, in depth order): their entries (the coarse bins
 // of the band their rectangles meet, row-major) are numbered in lane order, and the warp takes
 // them 32 at a time. Entries of the same coarse bin in one step are ranked by lane; the last of
 // them advances the bin's cursor.
-__global__ void __launch_bounds__(kPlaceWarps * 32, 1) k_coarse_place(FrameBufs fb, GridParams gp, PlaceGeom pg,
+__global__ void __launch_bounds__(kPlaceWarps * 32, kPlaceCtasPerSm) k_coarse_place(FrameBufs fb, GridParams gp, PlaceGeom pg,
                                                                       uint64_t n) {
     extern __shared__ uint32_t s_cur[];  // kBandMax cursors per warp
     FrameCtl* ctl = fb.ctl;
@@ -269,8 +320,9 @@ __global__ void __launch_bounds__(kPlaceWarps * 32, 1) k_coarse_place(FrameBufs 
         const uint64_t q0 = (uint64_t)chunk * pg.chunk_len;
         const uint64_t q1 = min(q0 + (uint64_t)pg.chunk_len, n);
         const uint32_t* __restrict__ trow = fb.ctable + (uint64_t)chunk * pg.ncoarse + bin0;
+        const uint32_t* __restrict__ grow = fb.gtable + (uint64_t)(chunk / pg.group) * pg.ncoarse + bin0;
         __syncwarp();  // the previous item is done with the cursors
-        for (uint32_t i = lane; i < nb; i += 32) cur[i] = trow[i] + fb.cinfo[bin0 + i].x;
+        for (uint32_t i = lane; i < nb; i += 32) cur[i] = trow[i] + grow[i] + fb.cinfo[bin0 + i].x;
         __syncwarp();
         // batch i is placed while batch i+1's rectangles and indices load
         uint64_t q = q0 + lane;
@@ -356,86 +408,83 @@ __global__ void __launch_bounds__(kPlaceWarps * 32, 1) k_coarse_place(FrameBufs 
 // ------------------------------------------------------------------- level 2
 
 struct Segment {
-    uint32_t coarse, e0, e1;
+    uint32_t coarse, e0, e1, nseg, seg0;
 };
 
 __device__ __forceinline__ Segment segment_of(const FrameBufs& fb, uint32_t s) {
     const uint32_t c = fb.seg_coarse[s];
     const uint4 info = fb.cinfo[c];
     const uint32_t e0 = info.x + (s - info.z) * kSegLen;
-    return Segment{c, e0, min(e0 + kSegLen, info.x + info.y)};
+    return Segment{c, e0, min(e0 + kSegLen, info.x + info.y), (info.y + kSegLen - 1) / kSegLen, info.z};
 }
 
-__global__ void __launch_bounds__(kSegWarps * 32) k_fine_count(FrameBufs fb) {
-    const FrameCtl* ctl = fb.ctl;
-    if (!ctl->plan_ok) return;
-    const uint32_t ns = ctl->num_segments;
+constexpr int kSegWaves = kSegLen / 32;
+
+// One warp: per bin of coarse bin `sg.coarse`'s 4x4, the exclusive prefix of the segments'
+// counts (in place) and the bin's total (ranges[bin].y). The counts come from other warps.
+__device__ __forceinline__ void seg_scan_warp(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg,
+                                              const Segment& sg) {
     const int lane = threadIdx.x & 31;
-    const uint32_t nw = (gridDim.x * blockDim.x) >> 5;
-    for (uint32_t s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; s < ns; s += nw) {
-        const Segment sg = segment_of(fb, s);
-        uint32_t cnt[16];
+    uint32_t carry[16];
 #pragma unroll
-        for (int f = 0; f < 16; ++f) cnt[f] = 0u;
-        for (uint32_t e = sg.e0; e < sg.e1; e += 32) {
-            const uint32_t m = e + lane < sg.e1 ? fb.clist[e + lane].y : 0u;
+    for (int f = 0; f < 16; ++f) carry[f] = 0u;
+    for (uint32_t s0 = 0; s0 < sg.nseg; s0 += 32) {
+        const bool live = s0 + lane < sg.nseg;
+        uint4* p = reinterpret_cast<uint4*>(fb.seg_cnt + (uint64_t)(sg.seg0 + s0 + lane) * 16);
+        uint32_t v[16];
 #pragma unroll
-            for (int f = 0; f < 16; ++f) cnt[f] += __popc(__ballot_sync(0xFFFFFFFFu, (m >> f) & 1u));
+        for (int i = 0; i < 4; ++i) {
+            const uint4 q = live ? __ldcg(p + i) : make_uint4(0u, 0u, 0u, 0u);
+            v[4 * i + 0] = q.x;
+            v[4 * i + 1] = q.y;
+            v[4 * i + 2] = q.z;
+            v[4 * i + 3] = q.w;
         }
-        uint32_t mine = 0;
 #pragma unroll
-        for (int f = 0; f < 16; ++f)
-            if (lane == f) mine = cnt[f];
-        if (lane < 16) fb.seg_cnt[(uint64_t)s * 16 + lane] = mine;
+        for (int f = 0; f < 16; ++f) {
+            uint32_t x = v[f];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, x, o);
+                if (lane >= o) x += t;
+            }
+            const uint32_t excl = carry[f] + x - v[f];
+            carry[f] += __shfl_sync(0xFFFFFFFFu, x, 31);
+            v[f] = excl;
+        }
+        if (live) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) p[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+    }
+    uint32_t tot = 0;
+#pragma unroll
+    for (int f = 0; f < 16; ++f)
+        if (lane == f) tot = carry[f];
+    if (lane < 16) {
+        const uint32_t cy = sg.coarse / pg.ctx, cx = sg.coarse - cy * pg.ctx;
+        const uint32_t bx = cx * kCoarse + (lane & 3), by = gp.row_begin + cy * kCoarse + (lane >> 2);
+        if (bx < gp.tiles_x && by < gp.row_end) fb.ranges[(uint64_t)by * gp.tiles_x + bx] = make_uint2(0u, tot);
     }
 }
 
-// A CTA per coarse bin, a warp per bin of its 4x4: exclusive prefix over the bin's segments.
-__global__ void __launch_bounds__(512) k_fine_seg_scan(FrameBufs fb, GridParams gp, PlaceGeom pg) {
-    if (!fb.ctl->plan_ok) return;
-    const uint32_t c = blockIdx.x;
-    const uint4 info = fb.cinfo[c];
-    if (info.y == 0u) return;
-    const int lane = threadIdx.x & 31, f = threadIdx.x >> 5;
-    const uint32_t ns = (info.y + kSegLen - 1) / kSegLen;
-    uint32_t carry = 0;
-    for (uint32_t s0 = 0; s0 < ns; s0 += 32) {
-        const uint32_t s = s0 + lane;
-        uint32_t* p = fb.seg_cnt + (uint64_t)(info.z + s) * 16 + f;
-        const uint32_t v = s < ns ? *p : 0u;
-        uint32_t x = v;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, x, o);
-            if (lane >= o) x += t;
-        }
-        if (s < ns) *p = carry + x - v;
-        carry += __shfl_sync(0xFFFFFFFFu, x, 31);
-    }
-    if (lane == 0) {
-        const uint32_t cy = c / pg.ctx, cx = c - cy * pg.ctx;
-        const uint32_t bx = cx * kCoarse + (f & 3), by = gp.row_begin + cy * kCoarse + (f >> 2);
-        if (bx < gp.tiles_x && by < gp.row_end) fb.ranges[(uint64_t)by * gp.tiles_x + bx] = make_uint2(0u, carry);
-    }
-}
-
-// One CTA: exclusive scan of the per-bin totals over the binned rows in row-major order.
-__global__ void __launch_bounds__(kRangesThreads) k_fine_ranges(FrameBufs fb, GridParams gp) {
+// One CTA: exclusive scan of the per-bin totals (ranges[.].y, written by other CTAs) over the
+// binned rows in row-major order -> ranges {start, end}; empty bins {0, 0}.
+__device__ void fine_ranges(const FrameBufs& fb, const GridParams& gp) {
     __shared__ uint32_t s_warp[32];
     __shared__ unsigned long long s_carry;
-    if (!fb.ctl->plan_ok) return;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     const uint32_t b0 = gp.row_begin * gp.tiles_x, b1 = gp.row_end * gp.tiles_x;
     if (tid == 0) s_carry = 0ull;
     __syncthreads();
-    constexpr uint32_t kRound = kRangesThreads * kRangesItems;
-    for (uint32_t r0 = b0; r0 < b1; r0 += kRound) {
+    const uint32_t round = blockDim.x * kRangesItems;
+    for (uint32_t r0 = b0; r0 < b1; r0 += round) {
         const uint32_t first = r0 + (uint32_t)tid * kRangesItems;
         uint32_t cnt[kRangesItems];
         uint32_t sum = 0;
 #pragma unroll
         for (int i = 0; i < kRangesItems; ++i) {
-            cnt[i] = first + i < b1 ? fb.ranges[first + i].y : 0u;
+            cnt[i] = first + i < b1 ? __ldcg(&fb.ranges[first + i].y) : 0u;
             sum += cnt[i];
         }
         uint32_t x = sum;
@@ -447,7 +496,7 @@ __global__ void __launch_bounds__(kRangesThreads) k_fine_ranges(FrameBufs fb, Gr
         if (lane == 31) s_warp[warp] = x;
         __syncthreads();
         if (warp == 0) {
-            uint32_t w = s_warp[lane];
+            uint32_t w = lane < nwarps ? s_warp[lane] : 0u;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, w, o);
@@ -465,9 +514,53 @@ __global__ void __launch_bounds__(kRangesThreads) k_fine_ranges(FrameBufs fb, Gr
             start += cnt[i];
         }
         __syncthreads();
-        if (tid == 0) s_carry += s_warp[31];
+        if (tid == 0) s_carry += s_warp[nwarps - 1];
         __syncthreads();
     }
+}
+
+// A warp per segment: pairs per bin of the 4x4 (ballot counts). The last segment of a coarse bin
+// to be counted scans the bin's segments; the last CTA to finish computes the bin ranges.
+__global__ void __launch_bounds__(kSegWarps * 32) k_fine_count(FrameBufs fb, GridParams gp, PlaceGeom pg) {
+    __shared__ uint32_t s_last;
+    FrameCtl* ctl = fb.ctl;
+    if (!ctl->plan_ok) return;  // the same for every CTA
+    const uint32_t ns = ctl->num_segments;
+    const int lane = threadIdx.x & 31;
+    const uint32_t nw = (gridDim.x * blockDim.x) >> 5;
+    for (uint32_t s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; s < ns; s += nw) {
+        const Segment sg = segment_of(fb, s);
+        uint32_t m[kSegWaves];  // the whole segment in flight
+#pragma unroll
+        for (int i = 0; i < kSegWaves; ++i) {
+            const uint32_t e = sg.e0 + i * 32 + lane;
+            m[i] = e < sg.e1 ? fb.clist[e].y : 0u;
+        }
+        uint32_t mine = 0;
+#pragma unroll
+        for (int f = 0; f < 16; ++f) {
+            uint32_t c = 0;
+#pragma unroll
+            for (int i = 0; i < kSegWaves; ++i) c += __popc(__ballot_sync(0xFFFFFFFFu, (m[i] >> f) & 1u));
+            if (lane == f) mine = c;
+        }
+        if (lane < 16) fb.seg_cnt[(uint64_t)s * 16 + lane] = mine;
+        __threadfence();  // every lane's count is visible before the warp's ticket
+        __syncwarp();
+        uint32_t last = 0;
+        if (lane == 0) last = atomicAdd(&fb.cinfo[sg.coarse].w, 1u) == sg.nseg - 1u;
+        if (__shfl_sync(0xFFFFFFFFu, last, 0)) {
+            __threadfence();
+            seg_scan_warp(fb, gp, pg, sg);
+        }
+    }
+    __threadfence();  // every thread's writes are visible before the CTA's ticket
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(&ctl->done_count, 1u) == gridDim.x - 1u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    fine_ranges(fb, gp);
 }
 
 __global__ void __launch_bounds__(kSegWarps * 32) k_fine_place(FrameBufs fb, GridParams gp, PlaceGeom pg) {
@@ -487,16 +580,22 @@ __global__ void __launch_bounds__(kSegWarps * 32) k_fine_place(FrameBufs fb, Gri
             if (bx < gp.tiles_x && by < gp.row_end)
                 mine = fb.ranges[(uint64_t)by * gp.tiles_x + bx].x + fb.seg_cnt[(uint64_t)s * 16 + lane];
         }
+        uint2 v[kSegWaves];  // the whole segment in flight
+#pragma unroll
+        for (int i = 0; i < kSegWaves; ++i) {
+            const uint32_t e = sg.e0 + i * 32 + lane;
+            v[i] = e < sg.e1 ? fb.clist[e] : make_uint2(0u, 0u);
+        }
         uint32_t off[16];  // write cursor of each bin of the 4x4
 #pragma unroll
         for (int f = 0; f < 16; ++f) off[f] = __shfl_sync(0xFFFFFFFFu, mine, f);
-        for (uint32_t e = sg.e0; e < sg.e1; e += 32) {
-            const uint2 v = e + lane < sg.e1 ? fb.clist[e + lane] : make_uint2(0u, 0u);
+#pragma unroll
+        for (int i = 0; i < kSegWaves; ++i) {
 #pragma unroll
             for (int f = 0; f < 16; ++f) {
-                const bool bit = (v.y >> f) & 1u;
+                const bool bit = (v[i].y >> f) & 1u;
                 const uint32_t b = __ballot_sync(0xFFFFFFFFu, bit);
-                if (bit) out[off[f] + __popc(b & lt)] = v.x;
+                if (bit) out[off[f] + __popc(b & lt)] = v[i].x;
                 off[f] += __popc(b);
             }
         }
@@ -516,7 +615,6 @@ cudaError_t place_geometry(const GridParams& gp, uint64_t n, uint64_t capacity, 
     const uint32_t br = g.ctx ? kBandMax / g.ctx : 1u;
     g.nbands = g.cty == 0 ? 1u : (g.cty + br - 1) / br;
     g.band_rows = g.cty == 0 ? 0u : (g.cty + g.nbands - 1) / g.nbands;
-    g.count_smem = (g.ncoarse > 0u ? g.ncoarse : 1u) * 4u;
     // chunks of depth order
     uint64_t chunks = (n + kChunkTarget - 1) / kChunkTarget;
     if (chunks > kMaxChunks) chunks = kMaxChunks;
@@ -525,10 +623,16 @@ cudaError_t place_geometry(const GridParams& gp, uint64_t n, uint64_t capacity, 
     chunks = n == 0 ? 1 : (n + len - 1) / len;
     g.nchunks = (uint32_t)chunks;
     g.chunk_len = (uint32_t)len;
+    // groups of chunks: one count CTA's counters, (chunks of the group) x (coarse bins), fit
+    const uint32_t nc = g.ncoarse > 0u ? g.ncoarse : 1u;
+    g.group = kCoarseMax / nc < kGroupMax ? kCoarseMax / nc : kGroupMax;
+    g.ngroups = (g.nchunks + g.group - 1) / g.group;
+    g.count_smem = g.group * nc * 4u;
     const uint32_t sms = (uint32_t)device_sm_count();
-    g.place_ctas = sms;
+    g.place_ctas = sms * kPlaceCtasPerSm;
     g.seg_ctas = sms * (2048u / (kSegWarps * 32u));
-    g.table_words = chunks * (g.ncoarse > 0u ? g.ncoarse : 1u);
+    g.table_words = chunks * nc;
+    g.gtable_words = (uint64_t)g.ngroups * nc;
     // entries <= pairs <= capacity; a coarse list of c entries has ceil(c / kSegLen) segments
     g.max_segments = capacity / kSegLen + g.ncoarse + 1;
 
@@ -550,20 +654,14 @@ cudaError_t place_geometry(const GridParams& gp, uint64_t n, uint64_t capacity, 
 
 cudaError_t launch_coarse_count(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
                                 cudaStream_t stream) {
-    if (n == 0 || gp.row_end <= gp.row_begin) return cudaSuccess;
-    k_coarse_count<<<pg.nchunks, kCountThreads, pg.count_smem, stream>>>(fb, gp, pg, n);
+    if (n == 0 || gp.row_end <= gp.row_begin) {  // nothing to bin: K, the flags and plan_ok
+        k_coarse_ranges<<<1, kRangesThreads, 0, stream>>>(fb, gp);
+        return cudaGetLastError();
+    }
+    k_coarse_count<<<pg.ngroups, kCountThreads, pg.count_smem, stream>>>(fb, gp, pg, n);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    k_coarse_scan<<<(pg.ncoarse + 31) / 32, 1024, 0, stream>>>(fb, pg);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_coarse_ranges(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
-                                 cudaStream_t stream) {
-    // also when nothing is binned: K, the flags and plan_ok are set here
-    PlaceGeom p = pg;
-    if (n == 0 || gp.row_end <= gp.row_begin) p.ncoarse = 0;  // the coarse totals were not counted
-    k_coarse_ranges<<<1, kRangesThreads, 0, stream>>>(fb, gp, p);
+    k_coarse_scan<<<(pg.ncoarse + 31) / 32, 1024, 0, stream>>>(fb, gp, pg);
     return cudaGetLastError();
 }
 
@@ -577,13 +675,9 @@ cudaError_t launch_coarse_place(const FrameBufs& fb, const GridParams& gp, const
 cudaError_t launch_fine_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
                               cudaStream_t stream) {
     if (n == 0 || gp.row_end <= gp.row_begin) return cudaSuccess;
-    k_fine_count<<<pg.seg_ctas, kSegWarps * 32, 0, stream>>>(fb);
+    k_fine_count<<<pg.seg_ctas, kSegWarps * 32, 0, stream>>>(fb, gp, pg);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    k_fine_seg_scan<<<pg.ncoarse, 512, 0, stream>>>(fb, gp, pg);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    k_fine_ranges<<<1, kRangesThreads, 0, stream>>>(fb, gp);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
     k_fine_place<<<pg.seg_ctas, kSegWarps * 32, 0, stream>>>(fb, gp, pg);
     return cudaGetLastError();
 }
