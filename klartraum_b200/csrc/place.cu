@@ -21,11 +21,11 @@
 //                    segment), and the segment -> coarse bin map.
 //   k_coarse_place   persistent warps over (band, chunk) items: 32 Gaussians at a time, their
 //                    (Gaussian, coarse bin) entries flattened in depth order and taken 32 at a
-//                    time; lanes with equal coarse bins are ranked by lane (ballot match) and
+//                    time; lanes with equal coarse bins are ranked by lane (warp match) and
 //                    written at the bin's cursor as (Gaussian index, mask of the 4x4 bins met).
 // Level 2, the bins of a coarse bin:
-//   k_fine_count     a warp per segment of a coarse list: pairs per bin of the 4x4 (ballot
-//                    counts). The last segment of a coarse bin to be counted turns its bins'
+//   k_fine_count     a warp per segment of a coarse list: pairs per bin of the 4x4 (byte
+//                    counters per lane, then warp sums). The last segment of a coarse bin to be counted turns its bins'
 //                    segment counts into exclusive prefixes (in place) and bin totals; the last
 //                    CTA to finish scans the totals into ranges {start, end} (empty bins keep
 //                    {0, 0}, as the reference's zeroed StartAndEnd buffer).
@@ -43,8 +43,8 @@ namespace kt {
 namespace {
 
 constexpr uint32_t kCoarse = 4;                // bins per side of a coarse bin
-constexpr uint32_t kChunkTarget = 512;         // Gaussians per chunk of depth order, about
-constexpr uint32_t kMaxChunks = 4096;
+constexpr uint32_t kChunkTarget = 256;         // Gaussians per chunk of depth order, about
+constexpr uint32_t kMaxChunks = 8192;
 constexpr uint32_t kCountThreads = 512;
 constexpr uint32_t kCoarseMax = 16384;         // coarse bins x chunks of a count CTA (64 KB of counters)
 constexpr uint32_t kGroupMax = 8;              // chunks of a count CTA
@@ -316,7 +316,6 @@ __global__ void __launch_bounds__(kPlaceWarps * 32, kPlaceCtasPerSm) k_coarse_pl
         const uint32_t band = item / pg.nchunks, chunk = item - band * pg.nchunks;
         const uint32_t cb0 = band * pg.band_rows, cb1 = min(cb0 + pg.band_rows, pg.cty);
         const uint32_t nb = (cb1 - cb0) * ctx, bin0 = cb0 * ctx;
-        const uint32_t nbits = nb > 1u ? 32u - __clz(nb - 1u) : 0u;
         const uint64_t q0 = (uint64_t)chunk * pg.chunk_len;
         const uint64_t q1 = min(q0 + (uint64_t)pg.chunk_len, n);
         const uint32_t* __restrict__ trow = fb.ctable + (uint64_t)chunk * pg.ncoarse + bin0;
@@ -385,13 +384,8 @@ __global__ void __launch_bounds__(kPlaceWarps * 32, kPlaceCtasPerSm) k_coarse_pl
                 const uint32_t rows = span4(max(yj & 0xFFFFu, by) - by, min(yj >> 16, by + kCoarse) - by);
                 const uint32_t spread = (rows & 1u) | ((rows & 2u) << 3) | ((rows & 4u) << 6) | ((rows & 8u) << 9);
                 const uint32_t mask = cols * spread;
-                // lanes of this step with the same coarse bin
-                uint32_t peers = __ballot_sync(0xFFFFFFFFu, valid);
-                for (uint32_t b = 0; b < nbits; ++b) {
-                    const bool bit = (cl >> b) & 1u;
-                    const uint32_t bb = __ballot_sync(0xFFFFFFFFu, bit);
-                    peers &= bit ? bb : ~bb;
-                }
+                // lanes of this step with the same coarse bin (lanes past the end match nobody)
+                const uint32_t peers = __match_any_sync(0xFFFFFFFFu, valid ? cl : 0x80000000u | (uint32_t)lane);
                 uint32_t pos = 0;
                 if (valid) pos = cur[cl] + __popc(peers & lt);
                 __syncwarp();
@@ -536,13 +530,22 @@ __global__ void __launch_bounds__(kSegWarps * 32) k_fine_count(FrameBufs fb, Gri
             const uint32_t e = sg.e0 + i * 32 + lane;
             m[i] = e < sg.e1 ? fb.clist[e].y : 0u;
         }
+        // per lane, bit 4r+k of the masks counted in byte k of acc[r] (at most kSegWaves = 16)
+        uint32_t acc[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int i = 0; i < kSegWaves; ++i)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[r] += (((m[i] >> (4 * r)) & 0xFu) * 0x00204081u) & 0x01010101u;
+        // warp sums, two 16-bit fields per reduction (at most 32 * 16 each)
         uint32_t mine = 0;
 #pragma unroll
-        for (int f = 0; f < 16; ++f) {
-            uint32_t c = 0;
-#pragma unroll
-            for (int i = 0; i < kSegWaves; ++i) c += __popc(__ballot_sync(0xFFFFFFFFu, (m[i] >> f) & 1u));
-            if (lane == f) mine = c;
+        for (int r = 0; r < 4; ++r) {
+            const uint32_t lo = __reduce_add_sync(0xFFFFFFFFu, acc[r] & 0x00FF00FFu);         // bits 4r, 4r+2
+            const uint32_t hi = __reduce_add_sync(0xFFFFFFFFu, (acc[r] >> 8) & 0x00FF00FFu);  // bits 4r+1, 4r+3
+            if (lane == 4 * r) mine = lo & 0xFFFFu;
+            if (lane == 4 * r + 1) mine = hi & 0xFFFFu;
+            if (lane == 4 * r + 2) mine = lo >> 16;
+            if (lane == 4 * r + 3) mine = hi >> 16;
         }
         if (lane < 16) fb.seg_cnt[(uint64_t)s * 16 + lane] = mine;
         __threadfence();  // every lane's count is visible before the warp's ticket
