@@ -30,18 +30,33 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // One blend step: a = exp(-0.5 * dot(d, covInv d)) * alpha; C += color * a * T; T *= 1 - a.
 // `q` = (A, B, C, alpha) with A = covInv[0][0] * k, B = (covInv[0][1] + covInv[1][0]) * k,
 // C = covInv[1][1] * k and k = -0.5 * log2(e), so the exponent is one quadratic form and the
-// exponential one exp2. T *= 1 - a is evaluated as T -= a * T.
-__device__ __forceinline__ void blend(float fx, float fy, float2 mean, const float4& q, const float4& col,
-                                      float& C0, float& C1, float& C2, float& T) {
-    const float dx = fx - mean.x, dy = fy - mean.y;
-    const float t = fmaf(q.y, dy, q.x * dx);
-    const float power = fmaf(q.z * dy, dy, dx * t);
+// exponential one exp2: power = (A dx) dx + (C dy + B dx) dy. The dx terms (`Xterms`) depend on
+// the pixel column only and are shared by the two pixels of a thread. T *= 1 - a is evaluated as
+// T -= a * T.
+struct Xterms {
+    float adx2, bdx;
+};
+
+__device__ __forceinline__ Xterms xterms(float fx, float2 mean, const float4& q) {
+    const float dx = fx - mean.x;
+    return Xterms{(q.x * dx) * dx, q.y * dx};
+}
+
+__device__ __forceinline__ void blend_y(const Xterms& xt, float fy, float2 mean, const float4& q, const float4& col,
+                                        float& C0, float& C1, float& C2, float& T) {
+    const float dy = fy - mean.y;
+    const float power = fmaf(fmaf(q.z, dy, xt.bdx), dy, xt.adx2);
     const float a = ex2_approx(power) * q.w;
     const float w = a * T;
     C0 = fmaf(col.x, w, C0);
     C1 = fmaf(col.y, w, C1);
     C2 = fmaf(col.z, w, C2);
     T -= w;
+}
+
+__device__ __forceinline__ void blend(float fx, float fy, float2 mean, const float4& q, const float4& col,
+                                      float& C0, float& C1, float& C2, float& T) {
+    blend_y(xterms(fx, mean, q), fy, mean, q, col, C0, C1, C2, T);
 }
 
 __device__ __forceinline__ float4 quad_form(float4 cov, float alpha) {
@@ -156,12 +171,13 @@ k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__
         for (uint32_t j0 = 0; j0 < nb; j0 += 64) {
             if (b + j0 < preend) {  // a whole 64-batch of the reference: test once at its end
                 if (a0 && a1) {
-#pragma unroll 8
+#pragma unroll 4
                     for (uint32_t jj = j0; jj < j0 + 64; ++jj) {
                         const float2 m = s_mean[jj];
                         const float4 q = s_q[jj], c = s_col[jj];
-                        blend(fx, fy0, m, q, c, p0.C0, p0.C1, p0.C2, p0.T);
-                        blend(fx, fy1, m, q, c, p1.C0, p1.C1, p1.C2, p1.T);
+                        const Xterms xt = xterms(fx, m, q);
+                        blend_y(xt, fy0, m, q, c, p0.C0, p0.C1, p0.C2, p0.T);
+                        blend_y(xt, fy1, m, q, c, p1.C0, p1.C1, p1.C2, p1.T);
                     }
                 } else if (a0) {
 #pragma unroll 8
