@@ -111,8 +111,8 @@ __global__ void __launch_bounds__(kCountThreads) k_coarse_count(FrameBufs fb, Gr
             g[u] = q < q1 ? (uint32_t)(order[q] & imask) : 0xFFFFFFFFu;
         }
 #pragma unroll
-        for (int u = 0; u < kU; ++u)
-            r[u] = (g[u] != 0xFFFFFFFFu && fb.counts[g[u]] != 0u) ? fb.rect[g[u]] : make_uint2(0u, 0u);
+        for (int u = 0; u < kU; ++u)  // the projection stores an empty rectangle for a Gaussian without bins
+            r[u] = g[u] != 0xFFFFFFFFu ? fb.rect[g[u]] : make_uint2(0u, 0u);
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
             const uint64_t q = qb + (uint64_t)u * kCountThreads;
@@ -155,13 +155,16 @@ __global__ void __launch_bounds__(1024) k_coarse_scan(FrameBufs fb, GridParams g
     const uint32_t per = (pg.ngroups + 31) / 32;
     const uint32_t c0 = min(seg * per, pg.ngroups), c1 = min(c0 + per, pg.ngroups);
     uint32_t* __restrict__ col = fb.gtable + b;
+    constexpr uint32_t kU = 8;  // rows in flight per thread
     uint32_t sum = 0;
     if (live) {
-        uint32_t c = c0;
-        for (; c + 4 <= c1; c += 4)
-            sum += col[(uint64_t)c * B] + col[(uint64_t)(c + 1) * B] + col[(uint64_t)(c + 2) * B] +
-                   col[(uint64_t)(c + 3) * B];
-        for (; c < c1; ++c) sum += col[(uint64_t)c * B];
+        for (uint32_t c = c0; c < c1; c += kU) {
+            uint32_t v[kU];
+#pragma unroll
+            for (uint32_t u = 0; u < kU; ++u) v[u] = c + u < c1 ? col[(uint64_t)(c + u) * B] : 0u;
+#pragma unroll
+            for (uint32_t u = 0; u < kU; ++u) sum += v[u];
+        }
     }
     s_seg[seg][lane] = sum;
     __syncthreads();
@@ -169,10 +172,15 @@ __global__ void __launch_bounds__(1024) k_coarse_scan(FrameBufs fb, GridParams g
     for (int s = 0; s < seg; ++s) base += s_seg[s][lane];
     if (live) {
         if (seg == 31) fb.cinfo[b] = make_uint4(0u, base + sum, 0u, 0u);  // the bin's total
-        for (uint32_t c = c0; c < c1; ++c) {
-            const uint32_t v = col[(uint64_t)c * B];
-            col[(uint64_t)c * B] = base;
-            base += v;
+        for (uint32_t c = c0; c < c1; c += kU) {
+            uint32_t v[kU];
+#pragma unroll
+            for (uint32_t u = 0; u < kU; ++u) v[u] = c + u < c1 ? col[(uint64_t)(c + u) * B] : 0u;
+#pragma unroll
+            for (uint32_t u = 0; u < kU; ++u) {
+                if (c + u < c1) col[(uint64_t)(c + u) * B] = base;
+                base += v[u];
+            }
         }
     }
     __threadfence();  // every thread's writes are visible before the CTA's ticket
