@@ -52,6 +52,8 @@ def parse():
     p.add_argument("--steps", type=int, default=400)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--paths", type=int, default=PATHS,
+                   help="frames in flight, each on its own path and stream (default 3, as klartraum's engine)")
     p.add_argument("--e2e-steps", type=int, default=None, help="steps of the host-buffer pass (default: steps/4)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--small", action="store_true", help="tiny frame for profiler captures")
@@ -271,6 +273,8 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
 
     from klartraum_b200 import Renderer, make_scene, native as N, orbit_views
 
+    paths = max(1, args.paths)
+
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
@@ -284,7 +288,7 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
 
     base_flags = N.FLAG_SORTED_KEYS if args.sorted_keys else 0
     r = Renderer(w.width, w.height, bin_size=16, sh_degree=w.sh_degree, device=local_rank,
-                 flags=N.FLAG_TIMING | base_flags, num_paths=PATHS)
+                 flags=N.FLAG_TIMING | base_flags, num_paths=paths)
     if world > 1:
         # the scene is made once (rank 0) and broadcast over NCCL; records land in device memory
         from klartraum_b200.multigpu import broadcast_scene
@@ -306,15 +310,15 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     e2e_steps = args.e2e_steps or max(10, args.steps // 4)
     # warm-up: checked frames over every view each path renders (sizes its buffers; frames in
     # flight are async and cannot grow them)
-    views = sorted({view_of(s) for s in range(max(args.steps, e2e_steps + 2 * PATHS, args.warmup))})
+    views = sorted({view_of(s) for s in range(max(args.steps, e2e_steps + 2 * paths, args.warmup))})
     for s in range(max(args.warmup, 3)):
         r.render(cams[view_of(s)], img, stream=sptr)
-    for p in range(PATHS):
+    for p in range(paths):
         for v in views:
             r.render(cams[v], img, path=p, stream=sptr)
     torch.cuda.synchronize()
     r.stage_times_total()
-    for p in range(PATHS):
+    for p in range(paths):
         r.counters(p)
     # stage times: a stream-launched pass on one path, frames back to back (graph replays record
     # no stage timers, and frames in flight would overlap the stages of different frames)
@@ -326,17 +330,17 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     r.counters()
     graph = args.launch == "graph"
     run_flags = (N.FLAG_GRAPH if graph else 0) | N.FLAG_ASYNC | base_flags
-    streams = [torch.cuda.Stream(dev) for _ in range(PATHS)]
-    imgs = [img] + [bg.clone() for _ in range(PATHS - 1)]
+    streams = [torch.cuda.Stream(dev) for _ in range(paths)]
+    imgs = [img] + [bg.clone() for _ in range(paths - 1)]
     if graph:  # one capture per path, outside the timed region
         r.set_flags(N.FLAG_GRAPH | base_flags)
-        for p in range(PATHS):
+        for p in range(paths):
             r.render(cams[view_of(p)], imgs[p], path=p, stream=streams[p].cuda_stream)
         torch.cuda.synchronize()
-        for p in range(PATHS):
+        for p in range(paths):
             r.counters(p)
 
-    # ---- timed region (device-resident inputs): PATHS frames in flight, frame s on path s % PATHS
+    # ---- timed region (device-resident inputs): paths frames in flight, frame s on path s % paths
     # and its stream, no host sync
     r.set_flags(run_flags)
     clock = ClockSampler(local_rank)
@@ -351,7 +355,7 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     for strm in streams[1:]:
         strm.wait_event(ev0)
     for s in range(args.steps):
-        p = s % PATHS
+        p = s % paths
         r.render(cams[view_of(s)], imgs[p], path=p, stream=streams[p].cuda_stream)
     for strm in streams[1:]:
         ev = torch.cuda.Event()
@@ -362,12 +366,12 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     t_wall1 = time.time()
     if world > 1:
         dist.barrier(device_ids=[local_rank])
-    for p in range(PATHS):
+    for p in range(paths):
         r.sync(p)  # raises if any timed frame overflowed or timed out
     clocks = clock.summary(t_wall0, t_wall1)
     ms = ev0.elapsed_time(ev1)
     cnt = {}
-    for p in range(PATHS):
+    for p in range(paths):
         for k, v in r.counters(p).items():
             cnt[k] = cnt.get(k, 0) + v
     assert cnt["frames"] == args.steps, cnt
@@ -382,23 +386,23 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     stages, roofline, K_avg, passes_avg = stage_report(w, cnt, st, stage_ms, timed_frames, nplanes,
                                                        r.stage_names)
 
-    # ---- end to end through the public API with host buffers: PATHS frames in flight
+    # ---- end to end through the public API with host buffers: paths frames in flight
     # (klartraum's paths), each path on its own stream; a path's host image is reused only after
     # kt_gs_sync(path) says its previous frame, copies included, is done
-    hosts = [torch.empty((w.height, w.width, 4), dtype=torch.uint8, pin_memory=True) for _ in range(PATHS)]
+    hosts = [torch.empty((w.height, w.width, 4), dtype=torch.uint8, pin_memory=True) for _ in range(paths)]
     for h in hosts:
         h.copy_(bg.cpu())
     r.set_flags(run_flags)
 
     def frame_host(s):
-        p = s % PATHS
-        if s >= PATHS:
+        p = s % paths
+        if s >= paths:
             r.sync(p)
         r.render_host(cams[view_of(s)], hosts[p].data_ptr(), path=p, stream=streams[p].cuda_stream)
 
-    for s in range(2 * PATHS):
+    for s in range(2 * paths):
         frame_host(s)
-    for p in range(PATHS):
+    for p in range(paths):
         r.sync(p)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
@@ -409,7 +413,7 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
         strm.wait_event(e0)
     for s in range(e2e_steps):
         frame_host(s)
-    for p in range(PATHS):
+    for p in range(paths):
         r.sync(p)
     for strm in streams[1:]:
         ev = torch.cuda.Event()
@@ -437,7 +441,7 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
         "stages": stages, "roofline": roofline,
         "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": img_bytes + 192,
                 "d2h_bytes_per_step": img_bytes + st["status_bytes"], "steps": e2e_steps,
-                "api": f"kt_gs_render_host (pinned host image in, rendered image out) with {PATHS} frames in "
+                "api": f"kt_gs_render_host (pinned host image in, rendered image out) with {paths} frames in "
                        "flight on their own paths and streams; kt_gs_sync(path) before a host image is reused"},
         "gpu_launches": launches_per_frame * args.steps * world, "gpu_launches_per_step": launches_per_frame,
         "clocks": clocks,
@@ -638,7 +642,7 @@ def main():
     cfg_block = workload_config(w)
     cfg_block["binning"] = "sorted_keys" if args.sorted_keys else "placed"
     cfg_block["launch"] = "cuda_graph" if (args.launch == 'graph') else "stream"
-    cfg_block["frames_in_flight"] = PATHS
+    cfg_block["frames_in_flight"] = args.paths
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

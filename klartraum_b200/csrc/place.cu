@@ -155,9 +155,18 @@ __global__ void __launch_bounds__(1024) k_coarse_scan(FrameBufs fb, GridParams g
     const uint32_t per = (pg.ngroups + 31) / 32;
     const uint32_t c0 = min(seg * per, pg.ngroups), c1 = min(c0 + per, pg.ngroups);
     uint32_t* __restrict__ col = fb.gtable + b;
-    constexpr uint32_t kU = 8;  // rows in flight per thread
+    constexpr uint32_t kU = 8;      // rows in flight per thread
+    constexpr uint32_t kHold = 16;  // rows a thread keeps in registers between the two passes
+    const bool hold = per <= kHold;  // the same for the whole CTA
+    uint32_t held[kHold];
     uint32_t sum = 0;
-    if (live) {
+    if (hold) {
+#pragma unroll
+        for (uint32_t u = 0; u < kHold; ++u) {
+            held[u] = live && c0 + u < c1 ? col[(uint64_t)(c0 + u) * B] : 0u;
+            sum += held[u];
+        }
+    } else if (live) {
         for (uint32_t c = c0; c < c1; c += kU) {
             uint32_t v[kU];
 #pragma unroll
@@ -172,14 +181,22 @@ __global__ void __launch_bounds__(1024) k_coarse_scan(FrameBufs fb, GridParams g
     for (int s = 0; s < seg; ++s) base += s_seg[s][lane];
     if (live) {
         if (seg == 31) fb.cinfo[b] = make_uint4(0u, base + sum, 0u, 0u);  // the bin's total
-        for (uint32_t c = c0; c < c1; c += kU) {
-            uint32_t v[kU];
+        if (hold) {
 #pragma unroll
-            for (uint32_t u = 0; u < kU; ++u) v[u] = c + u < c1 ? col[(uint64_t)(c + u) * B] : 0u;
+            for (uint32_t u = 0; u < kHold; ++u) {
+                if (c0 + u < c1) col[(uint64_t)(c0 + u) * B] = base;
+                base += held[u];
+            }
+        } else {
+            for (uint32_t c = c0; c < c1; c += kU) {
+                uint32_t v[kU];
 #pragma unroll
-            for (uint32_t u = 0; u < kU; ++u) {
-                if (c + u < c1) col[(uint64_t)(c + u) * B] = base;
-                base += v[u];
+                for (uint32_t u = 0; u < kU; ++u) v[u] = c + u < c1 ? col[(uint64_t)(c + u) * B] : 0u;
+#pragma unroll
+                for (uint32_t u = 0; u < kU; ++u) {
+                    if (c + u < c1) col[(uint64_t)(c + u) * B] = base;
+                    base += v[u];
+                }
             }
         }
     }
@@ -602,12 +619,18 @@ __global__ void __launch_bounds__(kSegWarps * 32) k_fine_place(FrameBufs fb, Gri
         for (int f = 0; f < 16; ++f) off[f] = __shfl_sync(0xFFFFFFFFu, mine, f);
 #pragma unroll
         for (int i = 0; i < kSegWaves; ++i) {
+            // the step's pairs per bin, bit 4r+k of the masks summed in byte k of tot[r] (at
+            // most 32): warp sums on the integer pipe instead of a population count per bin
+            uint32_t tot[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+                tot[r] = __reduce_add_sync(0xFFFFFFFFu, (((v[i].y >> (4 * r)) & 0xFu) * 0x00204081u) & 0x01010101u);
 #pragma unroll
             for (int f = 0; f < 16; ++f) {
                 const bool bit = (v[i].y >> f) & 1u;
                 const uint32_t b = __ballot_sync(0xFFFFFFFFu, bit);
                 if (bit) out[off[f] + __popc(b & lt)] = v[i].x;
-                off[f] += __popc(b);
+                off[f] += (tot[f >> 2] >> (8 * (f & 3))) & 0xFFu;
             }
         }
     }
