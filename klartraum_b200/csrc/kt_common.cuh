@@ -125,7 +125,8 @@ struct PlaceGeom {
     uint32_t band_rows;       // coarse rows per placement band (the last may be shorter)
     uint32_t count_smem;      // dynamic shared memory of a count CTA
     uint32_t place_ctas;      // persistent coarse-placement CTAs
-    uint32_t seg_ctas;        // CTAs of the segment kernels
+    uint32_t seg_ctas;        // CTAs of the pair placement
+    uint32_t count_ctas;      // CTAs of the bin count
     uint64_t table_words;     // u32 words of table[chunk][coarse bin]
     uint64_t gtable_words;    // u32 words of gtable[group][coarse bin]
     uint64_t max_segments;    // segments the key capacity can produce, at most

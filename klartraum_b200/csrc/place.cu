@@ -25,13 +25,13 @@
 //                    written at the bin's cursor as (Gaussian index, mask of the 4x4 bins met).
 // Level 2, the bins of a coarse bin:
 //   k_fine_count     a warp per segment of a coarse list: pairs per bin of the 4x4 (byte
-//                    counters per lane, then warp sums). The last segment of a coarse bin to be counted turns its bins'
-//                    segment counts into exclusive prefixes (in place) and bin totals; the last
-//                    CTA to finish scans the totals into ranges {start, end} (empty bins keep
-//                    {0, 0}, as the reference's zeroed StartAndEnd buffer).
-//   k_fine_place     a warp per segment, 32 entries at a time: for each bin of the 4x4 a ballot
-//                    ranks the entries that meet it; each writes its Gaussian at the bin's
-//                    cursor + rank (consecutive addresses per bin).
+//                    counters per lane, then warp sums), stored per segment and added to the
+//                    bins' totals; the last CTA to finish scans the totals into ranges {start,
+//                    end} (empty bins keep {0, 0}, as the reference's zeroed StartAndEnd buffer).
+//   k_fine_place     a warp per segment: its bins' cursors are the bin starts plus the counts of
+//                    the coarse list's earlier segments; then 32 entries at a time, for each bin
+//                    of the 4x4 a ballot ranks the entries that meet it; each writes its Gaussian
+//                    at the bin's cursor + rank (consecutive addresses per bin).
 // Chunks take consecutive slices of every coarse list, segments consecutive slices of every bin
 // and every step ranks by lane, so equal-bin pairs land in depth order: the stable sort of the
 // pairs by bin. A pair is stored as its Gaussian's index (4 bytes); its bin is implied by the
@@ -53,7 +53,8 @@ constexpr uint32_t kPlaceWarps = 16;           // warps of a coarse-placement CT
 constexpr uint32_t kPlaceCtasPerSm = 1;
 constexpr uint32_t kPlaceSmem = kPlaceWarps * kBandMax * 4;
 constexpr uint32_t kSegLen = 512;              // entries of a segment of a coarse list
-constexpr uint32_t kSegWarps = 8;              // warps of a segment-kernel CTA
+constexpr uint32_t kSegWarps = 8;              // warps of a pair-placement CTA
+constexpr uint32_t kCountWarps = 32;           // warps of a bin-count CTA (its last CTA scans 8192 bins a round)
 constexpr int kRangesThreads = 1024;
 constexpr int kRangesItems = 8;                // consecutive bins per thread and round
 
@@ -298,7 +299,7 @@ __device__ void coarse_ranges(const FrameBufs& fb, const GridParams& gp, uint32_
         for (int i = 0; i < kRangesItems; ++i) {
             if (first + i >= ncoarse) break;
             const uint32_t k = (cnt[i] + kSegLen - 1) / kSegLen;
-            fb.cinfo[first + i] = make_uint4(e, cnt[i], s, 0u);  // .w: segments counted (bin count)
+            fb.cinfo[first + i] = make_uint4(e, cnt[i], s, 0u);
             for (uint32_t j = 0; j < k; ++j) fb.seg_coarse[s + j] = first + i;
             e += cnt[i];
             s += k;
@@ -439,54 +440,6 @@ __device__ __forceinline__ Segment segment_of(const FrameBufs& fb, uint32_t s) {
 
 constexpr int kSegWaves = kSegLen / 32;
 
-// One warp: per bin of coarse bin `sg.coarse`'s 4x4, the exclusive prefix of the segments'
-// counts (in place) and the bin's total (ranges[bin].y). The counts come from other warps.
-__device__ __forceinline__ void seg_scan_warp(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg,
-                                              const Segment& sg) {
-    const int lane = threadIdx.x & 31;
-    uint32_t carry[16];
-#pragma unroll
-    for (int f = 0; f < 16; ++f) carry[f] = 0u;
-    for (uint32_t s0 = 0; s0 < sg.nseg; s0 += 32) {
-        const bool live = s0 + lane < sg.nseg;
-        uint4* p = reinterpret_cast<uint4*>(fb.seg_cnt + (uint64_t)(sg.seg0 + s0 + lane) * 16);
-        uint32_t v[16];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint4 q = live ? __ldcg(p + i) : make_uint4(0u, 0u, 0u, 0u);
-            v[4 * i + 0] = q.x;
-            v[4 * i + 1] = q.y;
-            v[4 * i + 2] = q.z;
-            v[4 * i + 3] = q.w;
-        }
-#pragma unroll
-        for (int f = 0; f < 16; ++f) {
-            uint32_t x = v[f];
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, x, o);
-                if (lane >= o) x += t;
-            }
-            const uint32_t excl = carry[f] + x - v[f];
-            carry[f] += __shfl_sync(0xFFFFFFFFu, x, 31);
-            v[f] = excl;
-        }
-        if (live) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) p[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        }
-    }
-    uint32_t tot = 0;
-#pragma unroll
-    for (int f = 0; f < 16; ++f)
-        if (lane == f) tot = carry[f];
-    if (lane < 16) {
-        const uint32_t cy = sg.coarse / pg.ctx, cx = sg.coarse - cy * pg.ctx;
-        const uint32_t bx = cx * kCoarse + (lane & 3), by = gp.row_begin + cy * kCoarse + (lane >> 2);
-        if (bx < gp.tiles_x && by < gp.row_end) fb.ranges[(uint64_t)by * gp.tiles_x + bx] = make_uint2(0u, tot);
-    }
-}
-
 // One CTA: exclusive scan of the per-bin totals (ranges[.].y, written by other CTAs) over the
 // binned rows in row-major order -> ranges {start, end}; empty bins {0, 0}.
 __device__ void fine_ranges(const FrameBufs& fb, const GridParams& gp) {
@@ -538,9 +491,9 @@ __device__ void fine_ranges(const FrameBufs& fb, const GridParams& gp) {
     }
 }
 
-// A warp per segment: pairs per bin of the 4x4 (ballot counts). The last segment of a coarse bin
-// to be counted scans the bin's segments; the last CTA to finish computes the bin ranges.
-__global__ void __launch_bounds__(kSegWarps * 32) k_fine_count(FrameBufs fb, GridParams gp, PlaceGeom pg) {
+// A warp per segment: pairs per bin of the 4x4, stored per segment and added to the bins' totals
+// (ranges[.].y); the last CTA to finish scans the totals into the bin ranges.
+__global__ void __launch_bounds__(kCountWarps * 32) k_fine_count(FrameBufs fb, GridParams gp, PlaceGeom pg) {
     __shared__ uint32_t s_last;
     FrameCtl* ctl = fb.ctl;
     if (!ctl->plan_ok) return;  // the same for every CTA
@@ -572,14 +525,12 @@ __global__ void __launch_bounds__(kSegWarps * 32) k_fine_count(FrameBufs fb, Gri
             if (lane == 4 * r + 2) mine = lo >> 16;
             if (lane == 4 * r + 3) mine = hi >> 16;
         }
-        if (lane < 16) fb.seg_cnt[(uint64_t)s * 16 + lane] = mine;
-        __threadfence();  // every lane's count is visible before the warp's ticket
-        __syncwarp();
-        uint32_t last = 0;
-        if (lane == 0) last = atomicAdd(&fb.cinfo[sg.coarse].w, 1u) == sg.nseg - 1u;
-        if (__shfl_sync(0xFFFFFFFFu, last, 0)) {
-            __threadfence();
-            seg_scan_warp(fb, gp, pg, sg);
+        if (lane < 16) {
+            fb.seg_cnt[(uint64_t)s * 16 + lane] = mine;
+            const uint32_t cy = sg.coarse / pg.ctx, cx = sg.coarse - cy * pg.ctx;
+            const uint32_t bx = cx * kCoarse + (lane & 3), by = gp.row_begin + cy * kCoarse + (lane >> 2);
+            if (mine && bx < gp.tiles_x && by < gp.row_end)  // the bin's total, over the segments
+                atomicAdd(&fb.ranges[(uint64_t)by * gp.tiles_x + bx].y, mine);
         }
     }
     __threadfence();  // every thread's writes are visible before the CTA's ticket
@@ -602,11 +553,30 @@ __global__ void __launch_bounds__(kSegWarps * 32) k_fine_place(FrameBufs fb, Gri
     for (uint32_t s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; s < ns; s += nw) {
         const Segment sg = segment_of(fb, s);
         const uint32_t cy = sg.coarse / pg.ctx, cx = sg.coarse - cy * pg.ctx;
+        // pairs per bin in the coarse bin's earlier segments: lanes take every 32nd segment
+        uint32_t part[16];
+#pragma unroll
+        for (int f = 0; f < 16; ++f) part[f] = 0u;
+        for (uint32_t k = lane; k < s - sg.seg0; k += 32) {
+            const uint4* q = reinterpret_cast<const uint4*>(fb.seg_cnt + (uint64_t)(sg.seg0 + k) * 16);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint4 c = q[i];
+                part[4 * i] += c.x;
+                part[4 * i + 1] += c.y;
+                part[4 * i + 2] += c.z;
+                part[4 * i + 3] += c.w;
+            }
+        }
         uint32_t mine = 0;
+#pragma unroll
+        for (int f = 0; f < 16; ++f) {
+            const uint32_t before = __reduce_add_sync(0xFFFFFFFFu, part[f]);
+            if (lane == f) mine = before;
+        }
         if (lane < 16) {
             const uint32_t bx = cx * kCoarse + (lane & 3), by = gp.row_begin + cy * kCoarse + (lane >> 2);
-            if (bx < gp.tiles_x && by < gp.row_end)
-                mine = fb.ranges[(uint64_t)by * gp.tiles_x + bx].x + fb.seg_cnt[(uint64_t)s * 16 + lane];
+            if (bx < gp.tiles_x && by < gp.row_end) mine += fb.ranges[(uint64_t)by * gp.tiles_x + bx].x;
         }
         uint2 v[kSegWaves];  // the whole segment in flight
 #pragma unroll
@@ -665,6 +635,7 @@ cudaError_t place_geometry(const GridParams& gp, uint64_t n, uint64_t capacity, 
     const uint32_t sms = (uint32_t)device_sm_count();
     g.place_ctas = sms * kPlaceCtasPerSm;
     g.seg_ctas = sms * (2048u / (kSegWarps * 32u));
+    g.count_ctas = sms * (2048u / (kCountWarps * 32u));
     g.table_words = chunks * nc;
     g.gtable_words = (uint64_t)g.ngroups * nc;
     // entries <= pairs <= capacity; a coarse list of c entries has ceil(c / kSegLen) segments
@@ -709,7 +680,7 @@ cudaError_t launch_coarse_place(const FrameBufs& fb, const GridParams& gp, const
 cudaError_t launch_fine_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
                               cudaStream_t stream) {
     if (n == 0 || gp.row_end <= gp.row_begin) return cudaSuccess;
-    k_fine_count<<<pg.seg_ctas, kSegWarps * 32, 0, stream>>>(fb, gp, pg);
+    k_fine_count<<<pg.count_ctas, kCountWarps * 32, 0, stream>>>(fb, gp, pg);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     k_fine_place<<<pg.seg_ctas, kSegWarps * 32, 0, stream>>>(fb, gp, pg);
