@@ -31,8 +31,8 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // `q` = (A, B, C, alpha) with A = covInv[0][0] * k, B = (covInv[0][1] + covInv[1][0]) * k,
 // C = covInv[1][1] * k and k = -0.5 * log2(e), so the exponent is one quadratic form and the
 // exponential one exp2: power = (A dx) dx + (C dy + B dx) dy. The dx terms (`Xterms`) depend on
-// the pixel column only and are shared by the two pixels of a thread. T *= 1 - a is evaluated as
-// T -= a * T.
+// the pixel column only and are shared by the two pixels of a thread. `cola` is color * alpha;
+// with u = exp2(power) * T the step is C += cola * u, T -= alpha * u.
 struct Xterms {
     float adx2, bdx;
 };
@@ -42,21 +42,25 @@ __device__ __forceinline__ Xterms xterms(float fx, float2 mean, const float4& q)
     return Xterms{(q.x * dx) * dx, q.y * dx};
 }
 
-__device__ __forceinline__ void blend_y(const Xterms& xt, float fy, float2 mean, const float4& q, const float4& col,
+__device__ __forceinline__ void blend_y(const Xterms& xt, float fy, float2 mean, const float4& q, const float4& cola,
                                         float& C0, float& C1, float& C2, float& T) {
     const float dy = fy - mean.y;
     const float power = fmaf(fmaf(q.z, dy, xt.bdx), dy, xt.adx2);
-    const float a = ex2_approx(power) * q.w;
-    const float w = a * T;
-    C0 = fmaf(col.x, w, C0);
-    C1 = fmaf(col.y, w, C1);
-    C2 = fmaf(col.z, w, C2);
-    T -= w;
+    const float u = ex2_approx(power) * T;
+    C0 = fmaf(cola.x, u, C0);
+    C1 = fmaf(cola.y, u, C1);
+    C2 = fmaf(cola.z, u, C2);
+    T = fmaf(-q.w, u, T);
 }
 
-__device__ __forceinline__ void blend(float fx, float fy, float2 mean, const float4& q, const float4& col,
+__device__ __forceinline__ void blend(float fx, float fy, float2 mean, const float4& q, const float4& cola,
                                       float& C0, float& C1, float& C2, float& T) {
-    blend_y(xterms(fx, mean, q), fy, mean, q, col, C0, C1, C2, T);
+    blend_y(xterms(fx, mean, q), fy, mean, q, cola, C0, C1, C2, T);
+}
+
+// A record's colour times its alpha.
+__device__ __forceinline__ float4 color_alpha(float4 col, float alpha) {
+    return make_float4(col.x * alpha, col.y * alpha, col.z * alpha, 0.0f);
 }
 
 __device__ __forceinline__ float4 quad_form(float4 cov, float alpha) {
@@ -96,7 +100,8 @@ __device__ __forceinline__ void blend_tail(const float4* __restrict__ rec, Index
     for (uint32_t i = preend; i < end; ++i) {
         const uint32_t idx = index_at(i);
         const float4 g = rec[3 * (uint64_t)idx + 0];
-        blend(fx, fy, make_float2(g.x, g.y), quad_form(rec[3 * (uint64_t)idx + 1], g.z), rec[3 * (uint64_t)idx + 2],
+        blend(fx, fy, make_float2(g.x, g.y), quad_form(rec[3 * (uint64_t)idx + 1], g.z),
+              color_alpha(rec[3 * (uint64_t)idx + 2], g.z),
               p.C0, p.C1, p.C2, p.T);
         if (p.T <= tmin) break;
     }
@@ -111,7 +116,7 @@ k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__
             uint32_t ypix0) {
     __shared__ float2 s_mean[kBatch];  // px, py
     __shared__ float4 s_q[kBatch];     // quadratic form, alpha
-    __shared__ float4 s_col[kBatch];   // r, g, b
+    __shared__ float4 s_col[kBatch];   // r, g, b times alpha
     if (!ctl->plan_ok) return;
 
     const int tid = threadIdx.x;
@@ -147,7 +152,7 @@ k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__
             const float4 g = rec[3 * (uint64_t)idx + 0];
             s_mean[k] = make_float2(g.x, g.y);
             s_q[k] = quad_form(rec[3 * (uint64_t)idx + 1], g.z);
-            s_col[k] = rec[3 * (uint64_t)idx + 2];
+            s_col[k] = color_alpha(rec[3 * (uint64_t)idx + 2], g.z);
         }
         __syncthreads();
         bool a0 = !(p0.done || p0.wait_tail), a1 = !(p1.done || p1.wait_tail);
