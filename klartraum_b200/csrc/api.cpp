@@ -4,9 +4,10 @@
 // (src/vulkan_gaussian_splatting.cpp:13-316): where the node builds a five-element compute
 // sub-graph with Vulkan buffers, this context owns the device buffers of each path (frame in
 // flight) and enqueues the kernels of one frame on a CUDA stream:
-//   init -> K1 project+count -> depth keys -> plan -> depth sort passes (Gaussians)
-//   -> pair counts per (chunk of depth order, bin) -> prefix over chunks, bin ranges (K5)
-//   -> pair placement by bin (K2-K4 without a pair sort) -> totals -> K6.
+//   init -> K1 project+count -> depth keys + plan -> depth sort passes (Gaussians)
+//   -> coarse-bin counts per (chunk of depth order, coarse bin) -> prefix, K, coarse list starts
+//   -> coarse placement -> bin counts + bin ranges (K5) -> pair placement by bin (K2-K4 without
+//   a pair sort) -> totals -> K6.
 // No host synchronisation happens inside a frame: the key count, the capacity check and the
 // depth-sort plan live in device memory. After the frame a 2.6 KB control block is copied back;
 // unless KT_GS_FLAG_ASYNC is set the call waits for it and, if the keys did not fit, grows
@@ -485,7 +486,7 @@ kt_status prepare_frame(kt_gs_ctx* c, PathWs& w, uint64_t n, bool graph, FramePl
 // The kernels and copies of one frame on `stream`: no allocation and no host wait, so the
 // sequence can be captured into a CUDA graph. `ev` (may be null) receives the stage events.
 // The camera comes from `cam_dev` (device memory) when it is not null, else from `cam`.
-//   default: init -> K1 -> depth keys -> plan -> depth passes -> rectangles in depth order +
+//   default: init -> K1 -> depth keys + plan -> depth passes -> rectangles in depth order +
 //            coarse counts -> prefix over chunks + coarse ranges -> coarse placement -> bin
 //            counts + bin ranges + pair placement -> totals -> K6
 //   keys:    init -> K1 -> scan + key emission -> plan + key sort passes -> boundary search ->
@@ -538,8 +539,7 @@ kt_status record_frame(kt_gs_ctx* c, PathWs& w, Source src, uint64_t n, const Ca
         io_depth.keys[0] = w.gsort[0];
         io_depth.keys[1] = w.gsort[1];
         // Gaussians by depth (stable: ties keep index order)
-        KT_TRY_CUDA(c, launch_depth_keys(fb, n, stream));
-        KT_TRY_CUDA(c, launch_plan(w.ctl_depth, n, kDepthPasses, 0, stream));
+        KT_TRY_CUDA(c, launch_depth_keys(fb, n, kDepthPasses, stream));  // and the plan of the passes
         for (uint32_t p = 0; p < kDepthPasses; ++p)
             KT_TRY_CUDA(c, launch_sort_pass(io_depth, w.ctl_depth, w.sort_status, w.sort_table, p,
                                             fp.sort_epoch0 + p, n, true, stream));
@@ -937,11 +937,11 @@ kt_status kt_gs_frame_stats(kt_gs_ctx* c, uint32_t path, kt_gs_stats* out) {
     out->depth_min_bits = h.depth_min;
     out->depth_max_bits = h.depth_max;
     out->status_bytes = (uint32_t)kCtlHeaderBytes;
-    // init, project, depth keys, plan, the depth passes, coarse count, coarse scan (+ list
+    // init, project, depth keys (+ plan), the depth passes, coarse count, coarse scan (+ list
     // starts), coarse placement, bin count (+ bin ranges), pair placement, totals, rasterise; or
     // init, project, scan/emit, plan, the key passes, ranges, totals, rasterise
     out->launches = w.keys_frame ? 7 + key_passes(c) * sort_pass_launches(w.cap, false)
-                                 : 11 + kDepthPasses * sort_pass_launches(w.frame_n, true);
+                                 : 10 + kDepthPasses * sort_pass_launches(w.frame_n, true);
     out->packed = h.packed;
     out->idx_bits = h.idx_bits;
     PlaceGeom pg{};

@@ -60,8 +60,11 @@ __global__ void k_frame_init(FrameCtl* ctl, FrameCtl* ctl_depth, uint2* ranges, 
 
 // Depth key of every Gaussian, (depth - depth_min) << idx_bits | index, with the digit
 // histograms of the depth sort. Gaussians that touch no bin take the largest depth; they
-// emit nothing, so where they land does not matter.
-__global__ void __launch_bounds__(256) k_depth_keys(FrameBufs fb, uint64_t n) {
+// emit nothing, so where they land does not matter. The last CTA to finish plans the passes.
+__device__ void plan_passes(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes, int mode);
+
+__global__ void __launch_bounds__(256) k_depth_keys(FrameBufs fb, uint64_t n, uint32_t max_passes) {
+    __shared__ uint32_t s_last;
     __shared__ uint32_t s_hist[8][4][256];  // per warp, per pass
     const FrameCtl* ctl = fb.ctl;
     FrameCtl* cd = fb.ctl_depth;
@@ -121,15 +124,22 @@ __global__ void __launch_bounds__(256) k_depth_keys(FrameBufs fb, uint64_t n) {
         cd->idx_bits = ibits;
         cd->packed = 1u;
     }
+    __threadfence();  // this CTA's counts (and sizes) are visible before its ticket
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(&cd->done_scan, 1u) == gridDim.x - 1u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    plan_passes(cd, n, max_passes, 0);
 }
 
-// One CTA of 256 threads: which passes move data, their bucket bases and buffer order.
-__global__ void __launch_bounds__(256) k_plan(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes,
-                                              int mode) {
+// One CTA of 256 threads: which passes move data, their bucket bases and buffer order. The
+// histograms may come from other CTAs of the calling kernel (read at L2).
+__device__ void plan_passes(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes, int mode) {
     __shared__ uint32_t s_warp[8];
     const int tid = threadIdx.x;
-    const uint64_t K = ctl->num_keys;
-    const bool ok = K <= capacity && (ctl->error_flags & kErrTimeout) == 0u;
+    const uint64_t K = __ldcg(&ctl->num_keys);
+    const bool ok = K <= capacity && (__ldcg(&ctl->error_flags) & kErrTimeout) == 0u;
     if (!ok) {
         if (tid == 0) {
             if (K > capacity) atomicOr(&ctl->error_flags, kErrCapacity);
@@ -137,12 +147,13 @@ __global__ void __launch_bounds__(256) k_plan(FrameCtl* ctl, uint64_t capacity, 
         }
         return;
     }
-    uint32_t npasses = (ctl->key_bits + 7) / 8;
+    const uint32_t key_bits = __ldcg(&ctl->key_bits);
+    uint32_t npasses = (key_bits + 7) / 8;
     if (npasses > max_passes) npasses = max_passes;
     uint32_t run[kMaxPasses];
     uint32_t executed = 0;
     for (uint32_t p = 0; p < max_passes; ++p) {
-        const uint32_t h = p < npasses ? ctl->hist[p][tid] : 0u;
+        const uint32_t h = p < npasses ? __ldcg(&ctl->hist[p][tid]) : 0u;
         const int nz = __syncthreads_count(h != 0u);
         run[p] = nz > 1 ? 1u : 0u;
         uint32_t total;
@@ -172,13 +183,18 @@ __global__ void __launch_bounds__(256) k_plan(FrameCtl* ctl, uint64_t capacity, 
             ++e;
         }
         for (uint32_t p = 0; p < max_passes; ++p) {
-            const uint32_t kb = ctl->key_bits, lo = 8 * p;
+            const uint32_t kb = key_bits, lo = 8 * p;
             ctl->pass_mask[p] = kb >= lo + 8 ? 255u : (kb > lo ? (1u << (kb - lo)) - 1u : 0u);
         }
         ctl->passes_run = executed;
         ctl->final_buf = (mode == 1 && executed == 0) ? 2u : cur;
         ctl->plan_ok = 1u;
     }
+}
+
+__global__ void __launch_bounds__(256) k_plan(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes,
+                                              int mode) {
+    plan_passes(ctl, capacity, max_passes, mode);
 }
 
 // After the pair placement: fold the frame's error bits and sizes into the running totals
@@ -211,14 +227,17 @@ cudaError_t launch_frame_init(FrameCtl* ctl, FrameCtl* ctl_depth, uint2* ranges,
     return cudaGetLastError();
 }
 
-cudaError_t launch_depth_keys(const FrameBufs& fb, uint64_t n, cudaStream_t stream) {
-    if (n == 0) return cudaSuccess;
+cudaError_t launch_depth_keys(const FrameBufs& fb, uint64_t n, uint32_t max_passes, cudaStream_t stream) {
+    if (n == 0) {  // nothing to sort: the plan alone
+        k_plan<<<1, 256, 0, stream>>>(fb.ctl_depth, n, max_passes, 0);
+        return cudaGetLastError();
+    }
     // few CTAs with many Gaussians each: every CTA adds its histograms to the frame's once
     uint64_t blocks = (n + 2047) / 2048;
     const uint64_t cap = (uint64_t)device_sm_count() * 2;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    k_depth_keys<<<(unsigned)blocks, 256, 0, stream>>>(fb, n);
+    k_depth_keys<<<(unsigned)blocks, 256, 0, stream>>>(fb, n, max_passes);
     return cudaGetLastError();
 }
 

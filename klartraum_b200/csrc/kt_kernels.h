@@ -40,7 +40,8 @@ cudaError_t launch_pack_scene(const float* d_aos, uint64_t n, float4* pos, float
 // binning.cu
 cudaError_t launch_frame_init(FrameCtl* ctl, FrameCtl* ctl_depth, uint2* ranges, uint32_t ntiles,
                               cudaStream_t stream);
-cudaError_t launch_depth_keys(const FrameBufs& fb, uint64_t n, cudaStream_t stream);
+// depth keys, their digit histograms and (last CTA) the pass plan of the depth sort
+cudaError_t launch_depth_keys(const FrameBufs& fb, uint64_t n, uint32_t max_passes, cudaStream_t stream);
 // mode 0: ping-pong between io.keys[0] and [1]; mode 1: [0] -> ... -> [2] via [1]
 cudaError_t launch_plan(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes, int mode,
                         cudaStream_t stream);
