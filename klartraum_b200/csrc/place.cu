@@ -324,11 +324,13 @@ __global__ void __launch_bounds__(kRangesThreads) k_coarse_ranges(FrameBufs fb, 
 __global__ void __launch_bounds__(kPlaceWarps * 32, kPlaceCtasPerSm) k_coarse_place(FrameBufs fb, GridParams gp, PlaceGeom pg,
                                                                       uint64_t n) {
     extern __shared__ uint32_t s_cur[];  // kBandMax cursors per warp
+    __shared__ uint4 s_slots[kPlaceWarps][32];  // per warp: (first entry, x0|x1<<16, y0|y1<<16, index)
     FrameCtl* ctl = fb.ctl;
     if (!ctl->plan_ok) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t lt = (1u << lane) - 1u;
     uint32_t* cur = s_cur + (size_t)warp * kBandMax;
+    uint4* slots = s_slots[warp];
     const FrameCtl* cd = fb.ctl_depth;
     const unsigned long long* __restrict__ order = io_select(fb.gsort, cd->final_buf);
     const unsigned long long imask = (1ull << cd->idx_bits) - 1ull;
@@ -357,23 +359,12 @@ __global__ void __launch_bounds__(kPlaceWarps * 32, kPlaceCtasPerSm) k_coarse_pl
             q = qb + 32 + lane;
             const uint2 r1 = q < q1 ? fb.srect[q] : make_uint2(0u, 0u);
             const uint32_t g1 = q < q1 ? (uint32_t)(order[q] & imask) : 0u;
-            // this lane's Gaussian: bins (x0..x1, y0..y1) and coarse bins of the band
-            uint32_t x0, x1, y0, y1, e = 0u, cpack = 0u, cy0 = 0u;
-            float inv = 1.0f;
+            // this lane's Gaussian: bins (x0..x1, y0..y1) and its number of coarse bins in the band
+            uint32_t x0, x1, y0, y1, e = 0u;
             if (local_rect(r0, gp, x0, x1, y0, y1)) {
-                const uint32_t cx0 = x0 / kCoarse, cx1 = (x1 + kCoarse - 1) / kCoarse;
-                cy0 = max(y0 / kCoarse, cb0);
-                const uint32_t cy1 = min((y1 + kCoarse - 1) / kCoarse, cb1);
-                if (cy0 < cy1) {
-                    const uint32_t cw = cx1 - cx0;
-                    e = cw * (cy1 - cy0);
-                    cpack = cx0 | (cw << 16);
-                    inv = __frcp_rn((float)cw);
-                }
-            } else {
-                x0 = x1 = y0 = y1 = 0u;
+                const uint32_t cy0 = max(y0 / kCoarse, cb0), cy1 = min((y1 + kCoarse - 1) / kCoarse, cb1);
+                if (cy0 < cy1) e = ((x1 + kCoarse - 1) / kCoarse - x0 / kCoarse) * (cy1 - cy0);
             }
-            const uint32_t xs = x0 | (x1 << 16), ys = y0 | (y1 << 16);
             uint32_t incl = e;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -382,32 +373,30 @@ __global__ void __launch_bounds__(kPlaceWarps * 32, kPlaceCtasPerSm) k_coarse_pl
             }
             const uint32_t total = __shfl_sync(0xFFFFFFFFu, incl, 31);
             const uint32_t first = incl - e;  // this lane's first entry
+            // the batch's Gaussians with entries, in lane order (first entries increasing)
+            const uint32_t ne = __ballot_sync(0xFFFFFFFFu, e != 0u);
+            __syncwarp();  // the previous batch's steps are done with the slots
+            if (e != 0u) slots[__popc(ne & lt)] = make_uint4(first, x0 | (x1 << 16), y0 | (y1 << 16), g0);
+            __syncwarp();
             for (uint32_t t0 = 0; t0 < total; t0 += 32) {
                 const uint32_t t = t0 + lane;
                 const bool valid = t < total;
-                // the entry's Gaussian: the last lane whose first entry is <= t (lanes without
-                // entries share the next lane's first, so the last such lane has entries)
-                uint32_t j = 0;
-#pragma unroll
-                for (uint32_t s = 16; s; s >>= 1) {
-                    const uint32_t f = __shfl_sync(0xFFFFFFFFu, first, j + s);
-                    if (f <= t) j += s;
-                }
-                const uint32_t k = t - __shfl_sync(0xFFFFFFFFu, first, j);
-                const uint32_t cp = __shfl_sync(0xFFFFFFFFu, cpack, j);
-                const uint32_t cyj = __shfl_sync(0xFFFFFFFFu, cy0, j);
-                const float invj = __shfl_sync(0xFFFFFFFFu, inv, j);
-                const uint32_t xj = __shfl_sync(0xFFFFFFFFu, xs, j);
-                const uint32_t yj = __shfl_sync(0xFFFFFFFFu, ys, j);
-                const uint32_t gj = __shfl_sync(0xFFFFFFFFu, g0, j);
+                // the entry's slot: the last Gaussian whose first entry is <= t, i.e. the slots
+                // starting at or before t0 (minus one) plus the slots starting in (t0, t]
+                const uint32_t before = __popc(__ballot_sync(0xFFFFFFFFu, e != 0u && first <= t0)) - 1u;
+                const uint32_t starts = __reduce_or_sync(
+                    0xFFFFFFFFu, (e != 0u && first > t0 && first - t0 < 32u) ? 1u << (first - t0) : 0u);
+                const uint4 sl = slots[before + __popc(starts & ((2u << lane) - 1u))];
+                const uint32_t gx0 = sl.y & 0xFFFFu, gx1 = sl.y >> 16, gy0 = sl.z & 0xFFFFu, gy1 = sl.z >> 16;
+                const uint32_t cx0 = gx0 / kCoarse, cw = (gx1 + kCoarse - 1) / kCoarse - cx0;
                 uint32_t dy = 0, dx = 0;
-                if (valid) divmod_small(k, cp >> 16, invj, dy, dx);
-                const uint32_t ccx = (cp & 0xFFFFu) + dx, ccy = cyj + dy;
+                if (valid) divmod_small(t - sl.x, cw, __frcp_rn((float)cw), dy, dx);
+                const uint32_t ccx = cx0 + dx, ccy = max(gy0 / kCoarse, cb0) + dy;
                 const uint32_t cl = (ccy - cb0) * ctx + ccx;  // band-local coarse bin
                 // the bins of the coarse bin's 4x4 that the rectangle meets
                 const uint32_t bx = ccx * kCoarse, by = ccy * kCoarse;
-                const uint32_t cols = span4(max(xj & 0xFFFFu, bx) - bx, min(xj >> 16, bx + kCoarse) - bx);
-                const uint32_t rows = span4(max(yj & 0xFFFFu, by) - by, min(yj >> 16, by + kCoarse) - by);
+                const uint32_t cols = span4(max(gx0, bx) - bx, min(gx1, bx + kCoarse) - bx);
+                const uint32_t rows = span4(max(gy0, by) - by, min(gy1, by + kCoarse) - by);
                 const uint32_t spread = (rows & 1u) | ((rows & 2u) << 3) | ((rows & 4u) << 6) | ((rows & 8u) << 9);
                 const uint32_t mask = cols * spread;
                 // lanes of this step with the same coarse bin (lanes past the end match nobody)
@@ -417,7 +406,7 @@ __global__ void __launch_bounds__(kPlaceWarps * 32, kPlaceCtasPerSm) k_coarse_pl
                 __syncwarp();
                 if (valid && (peers >> lane) == 1u) cur[cl] = pos + 1u;  // the bin's last entry of this step
                 __syncwarp();
-                if (valid) out[pos] = make_uint2(gj, mask);
+                if (valid) out[pos] = make_uint2(sl.w, mask);
             }
             r0 = r1;
             g0 = g1;
