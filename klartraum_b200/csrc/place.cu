@@ -21,8 +21,9 @@
 //                    segment), and the segment -> coarse bin map.
 //   k_coarse_place   persistent warps over (band, chunk) items: 32 Gaussians at a time, their
 //                    (Gaussian, coarse bin) entries flattened in depth order and taken 32 at a
-//                    time; lanes with equal coarse bins are ranked by lane (warp match) and
-//                    written at the bin's cursor as (Gaussian index, mask of the 4x4 bins met).
+//                    time; lanes with equal coarse bins are ranked by lane (each sets its bit in the
+//                    bin's word of a per-warp shared-memory array) and written at the bin's cursor
+//                    as (Gaussian index, mask of the 4x4 bins met).
 // Level 2, the bins of a coarse bin:
 //   k_fine_count     a warp per segment of a coarse list: pairs per bin of the 4x4 (byte
 //                    counters per lane, then warp sums), stored per segment and added to the
@@ -51,7 +52,7 @@ constexpr uint32_t kGroupMax = 8;              // chunks of a count CTA
 constexpr uint32_t kBandMax = 1024;            // coarse bins of a placement band (4 KB of cursors per warp)
 constexpr uint32_t kPlaceWarps = 16;           // warps of a coarse-placement CTA
 constexpr uint32_t kPlaceCtasPerSm = 1;
-constexpr uint32_t kPlaceSmem = kPlaceWarps * kBandMax * 4;
+constexpr uint32_t kPlaceSmem = 2 * kPlaceWarps * kBandMax * 4;  // cursors and lane bits
 constexpr uint32_t kSegLen = 512;              // entries of a segment of a coarse list
 constexpr uint32_t kSegWarps = 8;              // warps of a pair-placement CTA
 constexpr uint32_t kCountWarps = 32;           // warps of a bin-count CTA (its last CTA scans 8192 bins a round)
@@ -330,6 +331,8 @@ __global__ void __launch_bounds__(kPlaceWarps * 32, kPlaceCtasPerSm) k_coarse_pl
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t lt = (1u << lane) - 1u;
     uint32_t* cur = s_cur + (size_t)warp * kBandMax;
+    uint32_t* mb = s_cur + (size_t)(kPlaceWarps + warp) * kBandMax;  // lane bits per coarse bin, kept zero
+    for (uint32_t i = lane; i < kBandMax; i += 32) mb[i] = 0u;
     uint4* slots = s_slots[warp];
     const FrameCtl* cd = fb.ctl_depth;
     const unsigned long long* __restrict__ order = io_select(fb.gsort, cd->final_buf);
@@ -399,12 +402,20 @@ __global__ void __launch_bounds__(kPlaceWarps * 32, kPlaceCtasPerSm) k_coarse_pl
                 const uint32_t rows = span4(max(gy0, by) - by, min(gy1, by + kCoarse) - by);
                 const uint32_t spread = (rows & 1u) | ((rows & 2u) << 3) | ((rows & 4u) << 6) | ((rows & 8u) << 9);
                 const uint32_t mask = cols * spread;
-                // lanes of this step with the same coarse bin (lanes past the end match nobody)
-                const uint32_t peers = __match_any_sync(0xFFFFFFFFu, valid ? cl : 0x80000000u | (uint32_t)lane);
-                uint32_t pos = 0;
-                if (valid) pos = cur[cl] + __popc(peers & lt);
+                // lanes of this step with the same coarse bin: every entry sets its lane's bit in
+                // the bin's word; the bin's last entry of the step advances the cursor and clears it
+                if (valid) atomicOr(&mb[cl], 1u << lane);
                 __syncwarp();
-                if (valid && (peers >> lane) == 1u) cur[cl] = pos + 1u;  // the bin's last entry of this step
+                uint32_t peers = 0, pos = 0;
+                if (valid) {
+                    peers = mb[cl];
+                    pos = cur[cl] + __popc(peers & lt);
+                }
+                __syncwarp();
+                if (valid && (peers >> lane) == 1u) {
+                    cur[cl] = pos + 1u;
+                    mb[cl] = 0u;
+                }
                 __syncwarp();
                 if (valid) out[pos] = make_uint2(sl.w, mask);
             }
