@@ -125,6 +125,8 @@ struct PlaceGeom {
     uint32_t band_rows;       // coarse rows per placement band (the last may be shorter)
     uint32_t count_smem;      // dynamic shared memory of a count CTA
     uint32_t place_ctas;      // persistent coarse-placement CTAs
+    uint32_t band_bins;       // coarse bins of the largest placement band (cursor stride)
+    uint32_t place_smem;      // dynamic shared memory of a coarse-placement CTA
     uint32_t seg_ctas;        // CTAs of the pair placement
     uint32_t count_ctas;      // CTAs of the bin count
     uint64_t table_words;     // u32 words of table[chunk][coarse bin]

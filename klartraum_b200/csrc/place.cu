@@ -51,7 +51,7 @@ constexpr uint32_t kCoarseMax = 16384;         // coarse bins x chunks of a coun
 constexpr uint32_t kGroupMax = 8;              // chunks of a count CTA
 constexpr uint32_t kBandMax = 1024;            // coarse bins of a placement band (4 KB of cursors per warp)
 constexpr uint32_t kPlaceWarps = 16;           // warps of a coarse-placement CTA
-constexpr uint32_t kPlaceCtasPerSm = 1;
+constexpr uint32_t kPlaceCtasPerSm = 2;
 constexpr uint32_t kPlaceSmem = 2 * kPlaceWarps * kBandMax * 4;  // cursors and lane bits
 constexpr uint32_t kSegLen = 512;              // entries of a segment of a coarse list
 constexpr uint32_t kSegWarps = 8;              // warps of a pair-placement CTA
@@ -324,15 +324,15 @@ __global__ void __launch_bounds__(kRangesThreads) k_coarse_ranges(FrameBufs fb, 
 // them advances the bin's cursor.
 __global__ void __launch_bounds__(kPlaceWarps * 32, kPlaceCtasPerSm) k_coarse_place(FrameBufs fb, GridParams gp, PlaceGeom pg,
                                                                       uint64_t n) {
-    extern __shared__ uint32_t s_cur[];  // kBandMax cursors per warp
+    extern __shared__ uint32_t s_cur[];  // band_bins cursors, then band_bins lane-bit words, per warp
     __shared__ uint4 s_slots[kPlaceWarps][32];  // per warp: (first entry, x0|x1<<16, y0|y1<<16, index)
     FrameCtl* ctl = fb.ctl;
     if (!ctl->plan_ok) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t lt = (1u << lane) - 1u;
-    uint32_t* cur = s_cur + (size_t)warp * kBandMax;
-    uint32_t* mb = s_cur + (size_t)(kPlaceWarps + warp) * kBandMax;  // lane bits per coarse bin, kept zero
-    for (uint32_t i = lane; i < kBandMax; i += 32) mb[i] = 0u;
+    uint32_t* cur = s_cur + (size_t)warp * pg.band_bins;
+    uint32_t* mb = s_cur + (size_t)(kPlaceWarps + warp) * pg.band_bins;  // lane bits per coarse bin, kept zero
+    for (uint32_t i = lane; i < pg.band_bins; i += 32) mb[i] = 0u;
     uint4* slots = s_slots[warp];
     const FrameCtl* cd = fb.ctl_depth;
     const unsigned long long* __restrict__ order = io_select(fb.gsort, cd->final_buf);
@@ -634,6 +634,8 @@ cudaError_t place_geometry(const GridParams& gp, uint64_t n, uint64_t capacity, 
     g.count_smem = g.group * nc * 4u;
     const uint32_t sms = (uint32_t)device_sm_count();
     g.place_ctas = sms * kPlaceCtasPerSm;
+    g.band_bins = g.band_rows * g.ctx > 0u ? g.band_rows * g.ctx : 1u;
+    g.place_smem = 2u * kPlaceWarps * g.band_bins * 4u;
     g.seg_ctas = sms * (2048u / (kSegWarps * 32u));
     g.count_ctas = sms * (2048u / (kCountWarps * 32u));
     g.table_words = chunks * nc;
@@ -673,7 +675,7 @@ cudaError_t launch_coarse_count(const FrameBufs& fb, const GridParams& gp, const
 cudaError_t launch_coarse_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
                                 cudaStream_t stream) {
     if (n == 0 || gp.row_end <= gp.row_begin) return cudaSuccess;
-    k_coarse_place<<<pg.place_ctas, kPlaceWarps * 32, kPlaceSmem, stream>>>(fb, gp, pg, n);
+    k_coarse_place<<<pg.place_ctas, kPlaceWarps * 32, pg.place_smem, stream>>>(fb, gp, pg, n);
     return cudaGetLastError();
 }
 
