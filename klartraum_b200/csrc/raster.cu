@@ -9,8 +9,8 @@
 // loop still blends the first element past the last full batch (comp:104-117). With
 // KT_GS_FLAG_EXIT_PER_ELEMENT the test runs after every Gaussian.
 //
-// The CTA stages 256 sorted Gaussians at a time in shared memory (each thread gathers two
-// 48-B records by index) and leaves the list as soon as every pixel of the block is done or
+// The CTA stages 128 sorted Gaussians at a time in shared memory (each thread gathers one
+// 48-B record by index) and leaves the list as soon as every pixel of the block is done or
 // only owes the reference's one tail element, which it then blends from global memory.
 #include "kt_common.cuh"
 #include "kt_kernels.h"
@@ -19,7 +19,7 @@ namespace kt {
 namespace {
 
 constexpr int kRasterThreads = 128;  // two pixels per thread
-constexpr int kBatch = 256;
+constexpr int kBatch = 128;
 
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
@@ -172,7 +172,7 @@ k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__
             }
             continue;
         }
-        // 64-element blocks counted from `start` (batches start 256 apart, so blocks align)
+        // 64-element blocks counted from `start` (batches start kBatch apart, a multiple of 64, so blocks align)
         for (uint32_t j0 = 0; j0 < nb; j0 += 64) {
             if (b + j0 < preend) {  // a whole 64-batch of the reference: test once at its end
                 if (a0 && a1) {
