@@ -53,7 +53,7 @@ constexpr uint32_t kBandMax = 1024;            // coarse bins of a placement ban
 constexpr uint32_t kPlaceWarps = 16;           // warps of a coarse-placement CTA
 constexpr uint32_t kPlaceCtasPerSm = 2;
 constexpr uint32_t kPlaceSmem = 2 * kPlaceWarps * kBandMax * 4;  // cursors and lane bits
-constexpr uint32_t kSegLen = 512;              // entries of a segment of a coarse list
+constexpr uint32_t kSegLen = 256;              // entries of a segment of a coarse list
 constexpr uint32_t kSegWarps = 8;              // warps of a pair-placement CTA
 constexpr uint32_t kCountWarps = 32;           // warps of a bin-count CTA (its last CTA scans 8192 bins a round)
 constexpr int kRangesThreads = 1024;
