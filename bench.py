@@ -54,7 +54,11 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--paths", type=int, default=PATHS,
                    help="frames in flight, each on its own path and stream (default 3, as klartraum's engine)")
-    p.add_argument("--e2e-steps", type=int, default=None, help="steps of the host-buffer pass (default: steps/4)")
+    p.add_argument("--e2e-steps", type=int, default=None, help="steps of a host-buffer window (default: steps)")
+    p.add_argument("--min-window-ms", type=float, default=1000.0,
+                   help="repeat the timed window of `steps` frames until this much device time has passed")
+    p.add_argument("--no-multiview", dest="multiview", action="store_false",
+                   help="skip the 3M-Gaussian multi-view batch measured after the main workload")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--small", action="store_true", help="tiny frame for profiler captures")
     p.add_argument("--mode", choices=["views", "bands"], default="views",
@@ -270,23 +274,60 @@ def load_peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-def run_ours(args, w, cfg_block, rank, world, local_rank):
-    import datetime
-
+def timed_windows(window, world, dev, dist, local_rank, min_ms=1000.0, min_windows=5, max_windows=2000):
+    """Repeat a timed window of exactly `steps` frames until about `min_ms` of device time has
+    passed. `window()` enqueues one window and returns its (start, end) CUDA events. Every
+    window is bracketed by a barrier and a device synchronize; the window count is fixed from a
+    first window timed as the max over ranks, so every rank runs the same collectives. Returns the
+    per-window milliseconds (each the max over ranks) and the wall-clock span of all windows."""
     import torch
-    import torch.distributed as dist
 
-    from klartraum_b200 import Renderer, make_scene, native as N, orbit_views
+    def one():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+        e0, e1 = window()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    def max_over_ranks(vals):
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    first = max_over_ranks([one()])[0]
+    count = int(min(max(math.ceil(min_ms / max(first, 1e-3)), min_windows), max_windows))
+    t0 = time.time()
+    ms = [one() for _ in range(count)]
+    t1 = time.time()
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    return max_over_ranks(ms), (t0, t1)
+
+
+def window_stats(ms: list, steps: int) -> dict:
+    """Median and spread of per-window times."""
+    q = sorted(ms)
+    med = statistics.median(q)
+    return {"windows": len(q), "ms_per_window_median": med, "ms_per_step_median": med / steps,
+            "ms_per_window_min": q[0], "ms_per_window_max": q[-1],
+            "spread_pct": 100.0 * (q[-1] - q[0]) / med if med > 0 else 0.0,
+            "iqr_pct": 100.0 * (q[(3 * len(q)) // 4] - q[len(q) // 4]) / med if med > 0 else 0.0,
+            "device_ms_total": sum(q)}
+
+
+def measure_views(args, w, rank, world, local_rank, dev, dist, cams, scene, stage_pass=True) -> dict:
+    """Frames/s of the multi-view protocol on one workload: rank r renders view (s * N + r) mod 64
+    at step s, `paths` frames in flight on their own paths and streams. Device-resident windows of
+    exactly `steps` frames are repeated for about a second (median reported); then the same
+    through kt_gs_render_host with pinned host images (e2e). `scene` is host records or a
+    (device pointer, count) pair from the broadcast."""
+    import torch
+
+    from klartraum_b200 import Renderer, native as N
 
     paths = max(1, args.paths)
-
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    if args.small:
-        w = type(w)(**{**w.__dict__, "n": 20000, "width": 640, "height": 360})
-    cams = orbit_views(N_VIEWS, w.distance, w.width, w.height, fovy_deg=w.fovy_deg)
 
     def view_of(s):
         return (s * world + rank) % N_VIEWS
@@ -294,25 +335,18 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     base_flags = N.FLAG_SORTED_KEYS if args.sorted_keys else 0
     r = Renderer(w.width, w.height, bin_size=16, sh_degree=w.sh_degree, device=local_rank,
                  flags=N.FLAG_TIMING | base_flags, num_paths=paths)
-    if world > 1:
-        # the scene is made once (rank 0) and broadcast over NCCL; records land in device memory
-        from klartraum_b200.multigpu import broadcast_scene
-
-        scene_dev, n_rec = broadcast_scene(make_scene(w) if rank == 0 else None, dist, rank, dev)
+    if isinstance(scene, tuple):
+        r.set_gaussians_device(*scene)
         torch.cuda.synchronize()
-        r.set_gaussians_device(scene_dev.data_ptr(), n_rec)
-        torch.cuda.synchronize()
-        del scene_dev
     else:
-        r.set_gaussians(make_scene(w))
+        r.set_gaussians(scene)
     nplanes = (3 * (w.sh_degree + 1) ** 2 + 3) // 4
     bg = torch.zeros((w.height, w.width, 4), dtype=torch.uint8, device=dev)
     bg[..., 3] = 255
     img = bg.clone()
-    stream = torch.cuda.current_stream(dev)
-    sptr = stream.cuda_stream
+    sptr = torch.cuda.current_stream(dev).cuda_stream
 
-    e2e_steps = args.e2e_steps or max(10, args.steps // 4)
+    e2e_steps = args.e2e_steps or args.steps
     # warm-up: checked frames over every view each path renders (sizes its buffers; frames in
     # flight are async and cannot grow them)
     views = sorted({view_of(s) for s in range(max(args.steps, e2e_steps + 2 * paths, args.warmup))})
@@ -325,14 +359,16 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     r.stage_times_total()
     for p in range(paths):
         r.counters(p)
-    # stage times: a stream-launched pass on one path, frames back to back (graph replays record
-    # no stage timers, and frames in flight would overlap the stages of different frames)
-    r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC | base_flags)
-    for s in range(min(args.steps, 200)):
-        r.render(cams[view_of(s)], img, stream=sptr)
-    r.sync()
-    stage_ms, timed_frames = r.stage_times_total()
-    r.counters()
+    stage_ms, timed_frames = {}, 0
+    if stage_pass:
+        # stage times: a stream-launched pass on one path, frames back to back (graph replays
+        # record no stage timers, and frames in flight would overlap the stages of different frames)
+        r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC | base_flags)
+        for s in range(min(max(args.steps, 50), 200)):
+            r.render(cams[view_of(s)], img, stream=sptr)
+        r.sync()
+        stage_ms, timed_frames = r.stage_times_total()
+        r.counters()
     graph = args.launch == "graph"
     run_flags = (N.FLAG_GRAPH if graph else 0) | N.FLAG_ASYNC | base_flags
     streams = [torch.cuda.Stream(dev) for _ in range(paths)]
@@ -345,51 +381,50 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
         for p in range(paths):
             r.counters(p)
 
-    # ---- timed region (device-resident inputs): paths frames in flight, frame s on path s % paths
-    # and its stream, no host sync
+    def join_streams():
+        for strm in streams[1:]:
+            ev = torch.cuda.Event()
+            ev.record(strm)
+            streams[0].wait_event(ev)
+
+    # ---- device-resident windows: `paths` frames in flight, frame s on path s % paths and its
+    # stream, no host sync inside a window
     r.set_flags(run_flags)
+
+    def window():
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(streams[0])
+        for strm in streams[1:]:
+            strm.wait_event(ev0)
+        for s in range(args.steps):
+            p = s % paths
+            r.render(cams[view_of(s)], imgs[p], path=p, stream=streams[p].cuda_stream)
+        join_streams()
+        ev1.record(streams[0])
+        return ev0, ev1
+
     clock = ClockSampler(local_rank)
     clock.start()
-    time.sleep(0.5)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
-    torch.cuda.synchronize()
-    t_wall0 = time.time()
-    ev0.record(streams[0])
-    for strm in streams[1:]:
-        strm.wait_event(ev0)
-    for s in range(args.steps):
-        p = s % paths
-        r.render(cams[view_of(s)], imgs[p], path=p, stream=streams[p].cuda_stream)
-    for strm in streams[1:]:
-        ev = torch.cuda.Event()
-        ev.record(strm)
-        streams[0].wait_event(ev)
-    ev1.record(streams[0])
-    torch.cuda.synchronize()
-    t_wall1 = time.time()
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
+    time.sleep(0.3)
+    ms_list, (tw0, tw1) = timed_windows(window, world, dev, dist, local_rank, args.min_window_ms)
+    clocks = clock.summary(tw0, tw1)
     for p in range(paths):
         r.sync(p)  # raises if any timed frame overflowed or timed out
-    clocks = clock.summary(t_wall0, t_wall1)
-    ms = ev0.elapsed_time(ev1)
     cnt = {}
     for p in range(paths):
         for k, v in r.counters(p).items():
             cnt[k] = cnt.get(k, 0) + v
-    assert cnt["frames"] == args.steps, cnt
+    wins = window_stats(ms_list, args.steps)
+    assert cnt["frames"] == args.steps * (wins["windows"] + 1), cnt
     st = r.stats()
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    fps = world * args.steps / (ms_max / 1000.0)
+    ms_step = wins["ms_per_step_median"]
+    fps = world / (ms_step / 1000.0)
 
-    # ---- per-stage bandwidth over the timed region
-    stages, roofline, K_avg, passes_avg = stage_report(w, cnt, st, stage_ms, timed_frames, nplanes,
-                                                       r.stage_names)
+    stages = roofline = None
+    K_avg = cnt["keys"] / max(cnt["frames"], 1)
+    passes_avg = cnt["key_passes"] / max(cnt["keys"], 1)
+    if stage_pass:
+        stages, roofline, _, _ = stage_report(w, cnt, st, stage_ms, timed_frames, nplanes, r.stage_names)
 
     # ---- end to end through the public API with host buffers: paths frames in flight
     # (klartraum's paths), each path on its own stream; a path's host image is reused only after
@@ -399,64 +434,129 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
         h.copy_(bg.cpu())
     r.set_flags(run_flags)
 
-    def frame_host(s):
+    def frame_host(s, first_of_window):
         p = s % paths
-        if s >= paths:
+        if not first_of_window or s >= paths:
             r.sync(p)
         r.render_host(cams[view_of(s)], hosts[p].data_ptr(), path=p, stream=streams[p].cuda_stream)
 
     for s in range(2 * paths):
-        frame_host(s)
+        frame_host(s, False)
     for p in range(paths):
         r.sync(p)
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(streams[0])
-    for strm in streams[1:]:
-        strm.wait_event(e0)
-    for s in range(e2e_steps):
-        frame_host(s)
-    for p in range(paths):
-        r.sync(p)
-    for strm in streams[1:]:
-        ev = torch.cuda.Event()
-        ev.record(strm)
-        streams[0].wait_event(ev)
-    e1.record(streams[0])
-    torch.cuda.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_fps = world * e2e_steps / (float(te.item()) / 1000.0)
-    img_bytes = w.width * w.height * 4
-    clock.stop()
 
+    def window_host():
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(streams[0])
+        for strm in streams[1:]:
+            strm.wait_event(e0)
+        for s in range(e2e_steps):
+            frame_host(s, True)
+        for p in range(paths):
+            r.sync(p)
+        join_streams()
+        e1.record(streams[0])
+        return e0, e1
+
+    ems, _ = timed_windows(window_host, world, dev, dist, local_rank, args.min_window_ms)
+    clock.stop()
+    ewins = window_stats(ems, e2e_steps)
+    e2e_fps = world / (ewins["ms_per_step_median"] / 1000.0)
+    img_bytes = w.width * w.height * 4
+    view0 = None
+    if rank == 0:
+        # the image of view 0, for the divergence check of the CPU baseline
+        r.set_flags(base_flags)
+        img0 = bg.clone()
+        r.render(cams[0], img0, stream=sptr)
+        torch.cuda.synchronize()
+        view0 = img0.cpu().numpy()
+    out = {
+        "value": fps, "ms_per_step": ms_step, "windows": wins, "st": st, "K_avg": K_avg, "passes_avg": passes_avg,
+        "stages": stages, "roofline": roofline, "clocks": clocks, "view0": view0,
+        "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": img_bytes + 192,
+                "d2h_bytes_per_step": img_bytes + st["status_bytes"], "steps": e2e_steps, "windows": ewins,
+                "api": f"kt_gs_render_host (pinned host image in, rendered image out) with {paths} frames in "
+                       "flight on their own paths and streams; kt_gs_sync(path) before a host image is reused"},
+        "gpu_launches": st["launches"] * args.steps * world * wins["windows"],
+    }
+    r.close()
+    return out
+
+
+def run_ours(args, w, cfg_block, rank, world, local_rank):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from klartraum_b200 import make_scene, orbit_views
+    from klartraum_b200.scenes import WORKLOADS
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if args.small:
+        w = type(w)(**{**w.__dict__, "n": 20000, "width": 640, "height": 360})
+
+    def scene_of(wl):
+        if world > 1:
+            # the scene is made once (rank 0) and broadcast over NCCL; records land in device memory
+            from klartraum_b200.multigpu import broadcast_scene
+
+            scene_dev, n_rec = broadcast_scene(make_scene(wl) if rank == 0 else None, dist, rank, dev)
+            torch.cuda.synchronize()
+            return scene_dev, (scene_dev.data_ptr(), n_rec)
+        return None, make_scene(wl)
+
+    cams = orbit_views(N_VIEWS, w.distance, w.width, w.height, fovy_deg=w.fovy_deg)
+    keep, scene = scene_of(w)
+    m = measure_views(args, w, rank, world, local_rank, dev, dist, cams, scene)
+    del keep, scene
+    torch.cuda.synchronize()
+
+    # the multi-view batch workload (3M SH3, 64 views), measured the same way at every N
+    mv = None
+    if args.multiview and not args.small and w.name != "multiview_3m":
+        wm = WORKLOADS["multiview_3m"]
+        cams_m = orbit_views(N_VIEWS, wm.distance, wm.width, wm.height, fovy_deg=wm.fovy_deg)
+        keep, scene = scene_of(wm)
+        mm = measure_views(args, wm, rank, world, local_rank, dev, dist, cams_m, scene, stage_pass=False)
+        del keep, scene
+        mv = {"workload": workload_config(wm)["workload"], "value": mm["value"], "unit": "frames/s",
+              "gaussians_per_s": mm["value"] * wm.n, "ms_per_step": mm["ms_per_step"], "steps": args.steps,
+              "windows": mm["windows"], "keys_per_frame": mm["K_avg"], "e2e": mm["e2e"], "clocks": mm["clocks"],
+              "scaling": "weak", "n_gpus": world}
+
+    st = m["st"]
     launches_per_frame = st["launches"]
     line = {
-        "metric": METRIC, "value": fps, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+        "metric": METRIC, "value": m["value"], "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": m["ms_per_step"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg_block,
-        "gaussians_per_s": fps * w.n, "keys_per_frame": K_avg, "sort_passes_per_frame": passes_avg,
+        "gaussians_per_s": m["value"] * w.n, "keys_per_frame": m["K_avg"], "sort_passes_per_frame": m["passes_avg"],
+        "timing": {"protocol": f"windows of exactly {args.steps} frames repeated for >= {args.min_window_ms:.0f} ms "
+                               "of device time, each bracketed by barrier + synchronize and timed with CUDA events "
+                               "(max over ranks); value and ms_per_step from the median window",
+                   **m["windows"]},
         "sort_layout": ("reference-structured: index-order scan, (bin << depth_bits | depth, index) pairs, "
                         "LSD radix sort of the pairs, boundary search" if args.sorted_keys else
                         "Gaussians radix-sorted by depth; pairs placed in bin order by a two-level counting sort "
                         "(coarse lists of 4x4 bins filled by chunk of depth order, then bins of each coarse list by "
                         "segment); a pair is stored as its u32 Gaussian index"),
-        "stages": stages, "roofline": roofline,
-        "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": img_bytes + 192,
-                "d2h_bytes_per_step": img_bytes + st["status_bytes"], "steps": e2e_steps,
-                "api": f"kt_gs_render_host (pinned host image in, rendered image out) with {paths} frames in "
-                       "flight on their own paths and streams; kt_gs_sync(path) before a host image is reused"},
+        "stages": m["stages"], "roofline": m["roofline"],
+        "e2e": m["e2e"],
         "gpu_launches": launches_per_frame * args.steps * world, "gpu_launches_per_step": launches_per_frame,
-        "clocks": clocks,
+        "gpu_launches_all_windows": m["gpu_launches"],
+        "clocks": m["clocks"],
     }
+    if mv is not None:
+        line["multiview_3m"] = mv
     if world == 1 and rank == 0 and not args.no_cpu_baseline and not args.small:
-        line["cpu_baseline"] = cpu_baseline(w, cams)
+        line["cpu_baseline"] = cpu_baseline(w, cams, m["view0"])
     if rank == 0:
         print(json.dumps(line), flush=True)
-    r.close()
     if world > 1:
         dist.destroy_process_group()
 
@@ -538,27 +638,22 @@ def run_bands(args, w, rank, world, local_rank):
     r.set_flags(N.FLAG_TIMING | N.FLAG_ASYNC | base_flags)
     clock = ClockSampler(local_rank)
     clock.start()
-    time.sleep(0.5)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
-    torch.cuda.synchronize()
-    t_wall0 = time.time()
-    ev0.record(stream)
-    for s in range(args.steps):
-        frame(s)
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    t_wall1 = time.time()
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
+    time.sleep(0.3)
+
+    def window():
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for s in range(args.steps):
+            frame(s)
+        ev1.record(stream)
+        return ev0, ev1
+
+    ms_list, (tw0, tw1) = timed_windows(window, world, dev, dist, local_rank, args.min_window_ms)
     r.sync()
-    clocks = clock.summary(t_wall0, t_wall1)
-    t = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    fps = args.steps / (ms_max / 1000.0)
+    clocks = clock.summary(tw0, tw1)
+    wins = window_stats(ms_list, args.steps)
+    ms_step = wins["ms_per_step_median"]
+    fps = 1000.0 / ms_step
     stage_ms, timed_frames = r.stage_times_total()
     cnt = r.counters()
     st = r.stats()
@@ -568,43 +663,45 @@ def run_bands(args, w, rank, world, local_rank):
 
     # end to end: camera from host through the API, band render, strip gather, frame to host
     r.set_flags(base_flags)
-    e2e_steps = args.e2e_steps or max(10, args.steps // 4)
+    e2e_steps = args.e2e_steps or args.steps
     host = torch.empty((w.height, w.width, 4), dtype=torch.uint8, pin_memory=True)
     for s in range(3):
         host.copy_(frame(s), non_blocking=True)
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for s in range(e2e_steps):
-        out = frame(s)
-        if rank == 0:
-            host.copy_(out, non_blocking=True)
-        stream.synchronize()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_fps = e2e_steps / (float(te.item()) / 1000.0)
+
+    def window_host():
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for s in range(e2e_steps):
+            out = frame(s)
+            if rank == 0:
+                host.copy_(out, non_blocking=True)
+            stream.synchronize()
+        e1.record(stream)
+        return e0, e1
+
+    ems, _ = timed_windows(window_host, world, dev, dist, local_rank, args.min_window_ms)
+    ewins = window_stats(ems, e2e_steps)
+    e2e_fps = 1000.0 / ewins["ms_per_step_median"]
     clock.stop()
     img_bytes = w.width * w.height * 4
     line = {
         "metric": f"frames/s, {w.n:,}-splat SH{w.sh_degree} {w.width}x{w.height} split into bin-row bands",
         "value": fps, "unit": "frames/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{w.name}: {w.n:,} Gaussians SH{w.sh_degree} {w.width}x{w.height}, 16x16-px bins, "
                                f"{N_VIEWS}-view orbit, one frame per step split into {world} bin-row bands",
                    "bands": bands, "parallelism": f"bands{world}: projection replicated, binning/sort/splat per band, "
                                                   "strips all-gathered (NCCL) every step",
                    "l2": "inputs larger than L2; no flush", "seed": w.seed},
+        "timing": {"protocol": f"windows of exactly {args.steps} frames repeated for >= {args.min_window_ms:.0f} ms "
+                               "of device time (max over ranks), median window", **wins},
         "keys_per_frame_this_rank": K_avg, "sort_passes_per_frame": passes_avg, "stages_rank0": stages,
         "roofline": roofline,
         "gather_bytes_per_step": gather.bytes_per_frame if world > 1 else 0,
         "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": 192 * world,
-                "d2h_bytes_per_step": img_bytes, "steps": e2e_steps,
+                "d2h_bytes_per_step": img_bytes, "steps": e2e_steps, "windows": ewins,
                 "api": "kt_gs_render (camera from host) + strip all_gather + frame copied to pinned host on rank 0"},
         "gpu_launches": st["launches"] * args.steps * world, "gpu_launches_per_step": st["launches"] * world,
         "clocks": clocks,
@@ -616,8 +713,10 @@ def run_bands(args, w, rank, world, local_rank):
         dist.destroy_process_group()
 
 
-def cpu_baseline(w, cams) -> dict:
-    """The oracle (C restatement of the reference shaders, OpenMP) on one full frame."""
+def cpu_baseline(w, cams, gpu_view0=None) -> dict:
+    """The oracle (C restatement of the reference shaders, OpenMP) on full frames of the workload,
+    and, for view 0, how far the GPU's and the float32 oracle's images are from the
+    double-precision oracle."""
     import oracle
     from klartraum_b200 import make_scene
 
@@ -626,7 +725,7 @@ def cpu_baseline(w, cams) -> dict:
     bg = np.zeros((w.height, w.width, 4), np.uint8)
     bg[..., 3] = 255
     oracle.set_threads(len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1))
-    oracle.render_frame_fast(cfg, cams[0], g3d, bg)  # warm caches / page in
+    img0, _ = oracle.render_frame_fast(cfg, cams[0], g3d, bg)  # also warms caches / pages in
     frames = 0
     t0 = time.perf_counter()
     while True:
@@ -635,9 +734,18 @@ def cpu_baseline(w, cams) -> dict:
         if time.perf_counter() - t0 > 10.0 or frames >= 8:
             break
     dt = time.perf_counter() - t0
-    return {"value": frames / dt, "unit": "frames/s", "cores": oracle.lib().ko_get_threads(), "kind": "port",
-            "sample": f"{frames} full frames of the same workload (views 0..{frames - 1}) through the C "
-                      f"restatement of the reference shaders (oracle/kt_oracle.c), OpenMP"}
+    out = {"value": frames / dt, "unit": "frames/s", "cores": oracle.lib().ko_get_threads(), "kind": "port",
+           "sample": f"{frames} full frames of the same workload (views 0..{frames - 1}) through the C "
+                     f"restatement of the reference shaders (oracle/kt_oracle.c), OpenMP"}
+    if gpu_view0 is not None:
+        f64, _ = oracle.render_frame_f64(cfg, cams[0], g3d, bg)
+        d = np.abs(gpu_view0.astype(np.int16) - img0.astype(np.int16))
+        out["divergence_view0"] = {
+            "units": "1/255 per channel, against the double-precision oracle (oracle/kt_oracle.c "
+                     "ko_render_frame_f64)",
+            "gpu": oracle.divergence(gpu_view0, f64), "float32_oracle": oracle.divergence(img0, f64),
+            "gpu_vs_float32_oracle_max_abs": int(d.max())}
+    return out
 
 
 def main():

@@ -159,22 +159,41 @@ typedef struct kt_gs_counters {
     uint64_t depth_sort_bytes; /* same for the depth sort of the Gaussians */
 } kt_gs_counters;
 
-/* Buffers that kt_gs_debug_dump() can copy out after a render. */
+/* Buffers that kt_gs_debug_dump() can copy out after a render.
+ *
+ * Device buffers on both binning paths: PROJECTED, TILE_COUNTS, VALUES_SORTED, TILE_RANGES.
+ * KT_GS_FLAG_SORTED_KEYS also keeps OFFSETS and KEYS_SORTED in device buffers. The default path
+ * (pairs placed in bin order) has no such buffers: there OFFSETS, KEYS_UNSORTED and
+ * VALUES_UNSORTED are REBUILT ON THE HOST from the device's counts, bin rectangles and depths,
+ * and KEYS_SORTED is assembled on the host from the device's pairs, bin ranges and depths; they
+ * exist to compare against the reference's stage layout and are no evidence of a kernel. The
+ * placement's own device products are DEPTH_ORDER, COARSE_INFO, COARSE_LISTS and
+ * SEGMENT_COUNTS (default path only). */
 typedef enum kt_gs_stage {
     KT_GS_STAGE_PROJECTED = 0,       /* kt_gaussian2d[N], binMask = 0xFFFFFFFF as projected
                                         (gsplat_projection.comp:228) */
     KT_GS_STAGE_TILE_COUNTS = 1,     /* uint32[N] bins overlapped by each Gaussian (0 if culled) */
     KT_GS_STAGE_OFFSETS = 2,         /* uint64[N] exclusive scan of the tile counts in Gaussian index
-                                        order (derived from the counts; the device scans in depth order) */
+                                        order (default path: host-rebuilt from the counts) */
     KT_GS_STAGE_KEYS_UNSORTED = 3,   /* uint64[K] bin<<32 | (floatBitsToUint(z) ^ 0x80000000), Gaussians
-                                        in index order, bins ascending (rebuilt from the device's
-                                        per-Gaussian bin rectangles and depths) */
-    KT_GS_STAGE_VALUES_UNSORTED = 4, /* uint32[K] Gaussian index, same order */
-    KT_GS_STAGE_KEYS_SORTED = 5,     /* uint64[K], same key layout, stably sorted */
-    KT_GS_STAGE_VALUES_SORTED = 6,   /* uint32[K] */
+                                        in index order, bins ascending (both paths: host-rebuilt from
+                                        the device's per-Gaussian bin rectangles and depths) */
+    KT_GS_STAGE_VALUES_UNSORTED = 4, /* uint32[K] Gaussian index, same order (host-rebuilt) */
+    KT_GS_STAGE_KEYS_SORTED = 5,     /* uint64[K], same key layout, stably sorted (default path:
+                                        host-assembled from the device's pairs, ranges and depths) */
+    KT_GS_STAGE_VALUES_SORTED = 6,   /* uint32[K] Gaussian index of every pair in sorted order */
     KT_GS_STAGE_TILE_RANGES = 7,     /* uint32[2 * tiles] {start, end} per bin (StartAndEnd,
                                         gsplat_types.glsl:21-24); empty bins {0, 0} */
-    KT_GS_STAGE_COUNT = 8
+    KT_GS_STAGE_DEPTH_ORDER = 8,     /* uint32[N] Gaussian index at each position of the depth sort's
+                                        output (stable by depth; Gaussians without bins sort as the
+                                        deepest) */
+    KT_GS_STAGE_COARSE_INFO = 9,     /* uint32[4 * coarse bins] per coarse bin (4x4 bins, over the binned
+                                        rows): list start, entries, first segment, 0 */
+    KT_GS_STAGE_COARSE_LISTS = 10,   /* uint32[2 * entries] (Gaussian index, mask of the 4x4 bins met:
+                                        bit 4*row + col) by coarse bin, depth order within a list */
+    KT_GS_STAGE_SEGMENT_COUNTS = 11, /* uint32[16 * segments] pairs per bin of the 4x4 in each segment
+                                        (256 consecutive entries of one coarse list) */
+    KT_GS_STAGE_COUNT = 12
 } kt_gs_stage;
 
 /* Stage timers (KT_GS_FLAG_TIMING), in the order the stages run. */
@@ -298,6 +317,13 @@ kt_status kt_gs_frame_stats(kt_gs_ctx* ctx, uint32_t path, kt_gs_stats* out);
 kt_status kt_gs_debug_dump(kt_gs_ctx* ctx, uint32_t path, kt_gs_stage stage, void* host_dst,
                            uint64_t bytes, uint64_t* written);
 
+/* Elements [first, first + count) of a stage buffer (count is clipped to the stage's length;
+ * the element is one record, word or range as listed in kt_gs_stage). For slices of stages too
+ * large to copy whole, e.g. the sorted pairs of one band of bin rows (their positions are given
+ * by TILE_RANGES). With host_dst == NULL only *written (the bytes needed) is set. */
+kt_status kt_gs_debug_dump_range(kt_gs_ctx* ctx, uint32_t path, kt_gs_stage stage, uint64_t first,
+                                 uint64_t count, void* host_dst, uint64_t bytes, uint64_t* written);
+
 /* Per-stage milliseconds of the last frame on `path` (needs KT_GS_FLAG_TIMING). */
 kt_status kt_gs_stage_times(kt_gs_ctx* ctx, uint32_t path, float ms[KT_GS_NSTAGES]);
 
@@ -330,18 +356,38 @@ kt_status kt_gs_radix_sort_pairs(const uint64_t* d_keys_in, const uint32_t* d_va
  * memory pool already holds the device's free memory. No counterpart in the reference.
  *
  * The caller passes inputs and outputs only; the scratch is one fixed array of
- * KT_GS_STATIC_SORT_SCRATCH_BYTES in the library, kept on every device that loads it until the
- * process exits. n above KT_GS_STATIC_SORT_MAX_PAIRS returns KT_ERR_CAPACITY without doing
- * anything. The first call on a device looks up the array's device address (set-up done once
- * per device, with that device current); make that first call before any stream capture.
- * All calls share the array: calls that overlap on the GPU race and must be ordered by the
- * caller (e.g. issued on one stream). Asynchronous on `stream`; no allocation of any kind.
+ * KT_GS_STATIC_SORT_SCRATCH_BYTES (13,123,840 bytes, 12.5 MiB) in the library, kept on every
+ * device that loads it until the process exits. n above KT_GS_STATIC_SORT_MAX_PAIRS returns
+ * KT_ERR_CAPACITY without doing anything. keys_out/vals_out must not alias keys_in/vals_in
+ * (KT_ERR_ARG). Every call looks up the array's device address on the current device; the first
+ * call on a device also loads the module there, so make that first call before any stream
+ * capture. All calls share the array: calls that overlap on the GPU race and must be ordered by
+ * the caller (e.g. issued on one stream). Asynchronous on `stream`; no allocation of any kind.
+ * A look-back wait that runs out is reported by kt_gs_radix_sort_status(NULL, stream).
  */
 #define KT_GS_STATIC_SORT_MAX_PAIRS 1048576u
 #define KT_GS_STATIC_SORT_SCRATCH_BYTES 13123840u
 kt_status kt_gs_radix_sort_pairs_static(const uint64_t* d_keys_in, const uint32_t* d_vals_in,
                                         uint64_t* d_keys_out, uint32_t* d_vals_out, uint64_t n,
                                         uint32_t key_bits, void* stream);
+
+/*
+ * Wait for `stream` and report the device error bits of the last sort that used a scratch:
+ * d_temp of kt_gs_radix_sort_pairs, or NULL for kt_gs_radix_sort_pairs_static's fixed array.
+ * KT_ERR_TIMEOUT when a bounded look-back wait ran out (that sort's output is not sorted).
+ * No counterpart in the reference (its sort reports nothing).
+ */
+kt_status kt_gs_radix_sort_status(const void* d_temp, void* stream);
+
+/*
+ * Check of the timeout path: runs the sort's look-back wait against status words of the fixed
+ * scratch that nothing publishes, giving up after spin_limit polls (1 .. 2^22); the timeout is
+ * recorded in the scratch's control block as a sort would record it, so the next
+ * kt_gs_radix_sort_status(NULL, stream) returns KT_ERR_TIMEOUT, until the next
+ * kt_gs_radix_sort_pairs_static clears it. No fault, no hang: the wait is bounded. Shares the
+ * fixed scratch (order it with the static sorts). No counterpart in the reference.
+ */
+kt_status kt_gs_radix_sort_static_timeout_probe(uint32_t spin_limit, void* stream);
 
 #ifdef __cplusplus
 }

@@ -37,6 +37,12 @@ STAGE_VALUES_UNSORTED = 4
 STAGE_KEYS_SORTED = 5
 STAGE_VALUES_SORTED = 6
 STAGE_TILE_RANGES = 7
+STAGE_DEPTH_ORDER = 8
+STAGE_COARSE_INFO = 9
+STAGE_COARSE_LISTS = 10
+STAGE_SEGMENT_COUNTS = 11
+# dumps of the default binning path that are rebuilt on the host (no device buffer holds them)
+HOST_REBUILT_STAGES = (STAGE_OFFSETS, STAGE_KEYS_UNSORTED, STAGE_VALUES_UNSORTED)
 NSTAGES = 7
 STAGE_NAMES = ["project_count", "depth_sort", "coarse_count", "coarse_place", "fine_place", "rasterize", "frame"]
 # the same timer slots when KT_GS_FLAG_SORTED_KEYS selects the reference-structured binning
@@ -50,6 +56,8 @@ EXPORTED_SYMBOLS = [
     "kt_gs_render_batch", "kt_gs_render_projected", "kt_gs_sync", "kt_gs_frame_stats",
     "kt_gs_debug_dump", "kt_gs_stage_times", "kt_gs_stage_times_total", "kt_gs_radix_sort_pairs",
     "kt_gs_set_flags", "kt_gs_counters_take", "kt_gs_spz_decode", "kt_gs_load_ply", "kt_gs_ply_decode",
+    "kt_gs_debug_dump_range", "kt_gs_radix_sort_pairs_static", "kt_gs_radix_sort_status",
+    "kt_gs_radix_sort_static_timeout_probe",
 ]
 
 
@@ -138,9 +146,13 @@ def load() -> C.CDLL:
         "kt_gs_sync": (C.c_int, [vp, u32]),
         "kt_gs_frame_stats": (C.c_int, [vp, u32, C.POINTER(Stats)]),
         "kt_gs_debug_dump": (C.c_int, [vp, u32, C.c_int, vp, u64, C.POINTER(u64)]),
+        "kt_gs_debug_dump_range": (C.c_int, [vp, u32, C.c_int, u64, u64, vp, u64, C.POINTER(u64)]),
         "kt_gs_stage_times": (C.c_int, [vp, u32, C.POINTER(C.c_float)]),
         "kt_gs_stage_times_total": (C.c_int, [vp, u32, C.POINTER(C.c_double), C.POINTER(u64)]),
         "kt_gs_radix_sort_pairs": (C.c_int, [vp, vp, vp, vp, u64, u32, vp, C.POINTER(C.c_size_t), vp]),
+        "kt_gs_radix_sort_pairs_static": (C.c_int, [vp, vp, vp, vp, u64, u32, vp]),
+        "kt_gs_radix_sort_status": (C.c_int, [vp, vp]),
+        "kt_gs_radix_sort_static_timeout_probe": (C.c_int, [u32, vp]),
         "kt_gs_set_flags": (C.c_int, [vp, u32]),
         "kt_gs_counters_take": (C.c_int, [vp, u32, C.POINTER(Counters)]),
     }

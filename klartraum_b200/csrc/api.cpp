@@ -126,6 +126,7 @@ struct PathWs {
     bool timed = false;
     bool have_frame = false;
     uint64_t frame_n = 0;
+    uint32_t last_ncoarse = 0;  // coarse bins of the last frame's pair placement
     // device image for kt_gs_render_host
     uchar4* img = nullptr;
     // device copy of caller-supplied projected records
@@ -585,6 +586,7 @@ kt_status enqueue_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* ca
     kt_status s = prepare_frame(c, w, n, false, fp, stream);
     if (s != KT_OK) return s;
     w.keys_frame = fp.keys;
+    w.last_ncoarse = fp.keys ? 0u : fp.pg.ncoarse;
     if ((s = record_frame(c, w, src, n, cam, nullptr, img, stream, ev, fp)) != KT_OK) return s;
     KT_TRY_CUDA(c, cudaEventRecord(w.done_ev, stream));
     w.have_frame = true;
@@ -629,6 +631,7 @@ kt_status enqueue_graph_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamPara
     KT_TRY_CUDA(c, cudaGraphLaunch(w.gexec, stream));
     KT_TRY_CUDA(c, cudaEventRecord(w.done_ev, stream));
     w.keys_frame = fp.keys;
+    w.last_ncoarse = fp.keys ? 0u : fp.pg.ncoarse;
     w.timed = false;
     w.have_frame = true;
     w.frame_n = n;
@@ -728,6 +731,172 @@ kt_status upload_scene(kt_gs_ctx* c, const kt_gaussian3d* src, bool src_on_devic
         KT_TRY_CUDA(c, e);
     }
     c->has_scene = true;
+    return KT_OK;
+}
+
+// Elements [first, first + count) of a stage buffer of the path's last frame, copied to host
+// memory (count is clipped to the stage's length). The default binning path has no device
+// buffer for OFFSETS, KEYS_UNSORTED and VALUES_UNSORTED: those dumps are rebuilt here on the
+// host from the device's counts, rectangles and depths (the reference's stage layout, for
+// comparisons), and KEYS_SORTED is assembled from the device's pairs, bin ranges and depths.
+kt_status dump_window(kt_gs_ctx* c, uint32_t path, kt_gs_stage stage, uint64_t first, uint64_t count, void* dst,
+                      uint64_t bytes, uint64_t* written) {
+    if (!c) return KT_ERR_ARG;
+    if (written) *written = 0;
+    if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
+    KT_TRY_CUDA(c, cudaSetDevice(c->device));
+    PathWs& w = c->paths[path];
+    if (!w.have_frame) return fail(c, KT_ERR_STATE, "no frame rendered on this path");
+    KT_TRY_CUDA(c, cudaEventSynchronize(w.done_ev));
+    const FrameCtl& h = *w.host_ctl;
+    const uint64_t n = w.frame_n;
+    const uint64_t K = h.num_keys;
+    const bool sorted_ok = h.plan_ok != 0;
+    const uint32_t tx = c->gp.tiles_x;
+    const bool placed = !w.keys_frame;
+    uint64_t len = 0, esize = 0;  // elements of the stage, bytes per element
+    switch (stage) {
+        case KT_GS_STAGE_PROJECTED: len = n; esize = sizeof(kt_gaussian2d); break;
+        case KT_GS_STAGE_TILE_COUNTS: len = n; esize = 4; break;
+        case KT_GS_STAGE_OFFSETS: len = n; esize = 8; break;
+        case KT_GS_STAGE_KEYS_UNSORTED: len = K; esize = 8; break;
+        case KT_GS_STAGE_VALUES_UNSORTED: len = K; esize = 4; break;
+        case KT_GS_STAGE_KEYS_SORTED: len = K; esize = 8; break;
+        case KT_GS_STAGE_VALUES_SORTED: len = K; esize = 4; break;
+        case KT_GS_STAGE_TILE_RANGES: len = ntiles(c); esize = 8; break;
+        case KT_GS_STAGE_DEPTH_ORDER: len = n; esize = 4; break;
+        case KT_GS_STAGE_COARSE_INFO: len = w.last_ncoarse; esize = 16; break;
+        case KT_GS_STAGE_COARSE_LISTS: len = h.num_entries; esize = 8; break;
+        case KT_GS_STAGE_SEGMENT_COUNTS: len = h.num_segments; esize = 64; break;
+        default: return fail(c, KT_ERR_ARG, "unknown stage");
+    }
+    const bool placement_stage = stage == KT_GS_STAGE_DEPTH_ORDER || stage == KT_GS_STAGE_COARSE_INFO ||
+                                 stage == KT_GS_STAGE_COARSE_LISTS || stage == KT_GS_STAGE_SEGMENT_COUNTS;
+    if (placement_stage && !placed)
+        return fail(c, KT_ERR_STATE, "placement buffers exist only on the default binning path");
+    if ((stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_VALUES_SORTED ||
+         stage == KT_GS_STAGE_COARSE_LISTS || stage == KT_GS_STAGE_SEGMENT_COUNTS) && !sorted_ok)
+        return fail(c, KT_ERR_STATE, "the last frame was not sorted");
+    if (first > len) return fail(c, KT_ERR_ARG, "first element beyond the stage's length");
+    const uint64_t cnt = std::min(count, len - first);
+    const uint64_t need = cnt * esize;
+    if (!dst) {
+        if (written) *written = need;
+        return KT_OK;
+    }
+    if (bytes < need) return fail(c, KT_ERR_ARG, "buffer too small: need " + std::to_string(need) + " bytes");
+    auto fetch = [&](const void* d, size_t nbytes, void* out) -> kt_status {
+        if (nbytes) KT_TRY_CUDA(c, cudaMemcpy(out, d, nbytes, cudaMemcpyDeviceToHost));
+        return KT_OK;
+    };
+    const uint64_t last = first + cnt;
+    kt_status st = KT_OK;
+    if (stage == KT_GS_STAGE_PROJECTED) {
+        std::vector<float4> rec(3 * cnt);
+        if ((st = fetch(w.rec + 3 * first, sizeof(float4) * 3 * cnt, rec.data())) != KT_OK) return st;
+        kt_gaussian2d* o = (kt_gaussian2d*)dst;
+        for (uint64_t i = 0; i < cnt; ++i) {
+            const float4 a = rec[3 * i], b = rec[3 * i + 1], cc = rec[3 * i + 2];
+            o[i].position[0] = a.x;
+            o[i].position[1] = a.y;
+            o[i].z = a.w;
+            o[i].binMask = 0xFFFFFFFFu;
+            o[i].covInv[0] = b.x;
+            o[i].covInv[1] = b.y;
+            o[i].covInv[2] = b.z;
+            o[i].covInv[3] = b.w;
+            o[i].color[0] = cc.x;
+            o[i].color[1] = cc.y;
+            o[i].color[2] = cc.z;
+            o[i].alpha = a.z;
+        }
+    } else if (stage == KT_GS_STAGE_TILE_COUNTS) {
+        if ((st = fetch(w.counts + first, need, dst)) != KT_OK) return st;
+    } else if (stage == KT_GS_STAGE_TILE_RANGES) {
+        if ((st = fetch(w.ranges + first, need, dst)) != KT_OK) return st;
+    } else if (stage == KT_GS_STAGE_COARSE_INFO) {
+        if ((st = fetch(w.cinfo + first, need, dst)) != KT_OK) return st;
+    } else if (stage == KT_GS_STAGE_COARSE_LISTS) {
+        if ((st = fetch(w.clist + first, need, dst)) != KT_OK) return st;
+    } else if (stage == KT_GS_STAGE_SEGMENT_COUNTS) {
+        if ((st = fetch(w.seg_cnt + 16 * first, need, dst)) != KT_OK) return st;
+    } else if (stage == KT_GS_STAGE_DEPTH_ORDER) {
+        // the depth sort's result: (depth - min) << idx_bits | index words in its final buffer
+        FrameCtl cd;
+        if ((st = fetch(w.ctl_depth, offsetof(FrameCtl, hist), &cd)) != KT_OK) return st;
+        std::vector<unsigned long long> words(cnt);
+        if ((st = fetch(w.gsort[cd.final_buf & 1u] + first, cnt * 8, words.data())) != KT_OK) return st;
+        const unsigned long long imask = cd.idx_bits >= 64 ? ~0ull : (1ull << cd.idx_bits) - 1ull;
+        for (uint64_t i = 0; i < cnt; ++i) ((uint32_t*)dst)[i] = (uint32_t)(words[i] & imask);
+    } else if (stage == KT_GS_STAGE_OFFSETS && !placed) {
+        if ((st = fetch(w.offsets + first, need, dst)) != KT_OK) return st;
+    } else if (stage == KT_GS_STAGE_OFFSETS) {
+        // host-rebuilt: the index-order exclusive scan of the device's counts
+        std::vector<uint32_t> cn(last);
+        if ((st = fetch(w.counts, last * 4, cn.data())) != KT_OK) return st;
+        uint64_t run = 0;
+        for (uint64_t i = 0; i < last; ++i) {
+            if (i >= first) ((uint64_t*)dst)[i - first] = run;
+            run += cn[i];
+        }
+    } else if ((stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_VALUES_SORTED) && !placed) {
+        if (stage == KT_GS_STAGE_VALUES_SORTED) {
+            if ((st = fetch(w.vals[h.final_buf] + first, need, dst)) != KT_OK) return st;
+        } else {
+            // bin << depth_bits | (depth - depth_min)  ->  bin << 32 | depth, the reference's key
+            if ((st = fetch(w.keys[h.final_buf] + first, need, dst)) != KT_OK) return st;
+            unsigned long long* k = (unsigned long long*)dst;
+            const uint32_t db = h.depth_bits;
+            const unsigned long long dm = db ? ((1ull << db) - 1ull) : 0ull;
+            for (uint64_t i = 0; i < cnt; ++i)
+                k[i] = ((k[i] >> db) << 32) | (unsigned long long)((uint32_t)(k[i] & dm) + h.depth_min);
+        }
+    } else if (stage == KT_GS_STAGE_VALUES_SORTED) {
+        if ((st = fetch(w.pairs + first, need, dst)) != KT_OK) return st;
+    } else if (stage == KT_GS_STAGE_KEYS_SORTED) {
+        // host-assembled: bin << 32 | depth bits, the bin of each pair read off the device's ranges
+        std::vector<uint32_t> g(cnt), depth(n);
+        std::vector<uint2> rng(ntiles(c));
+        if ((st = fetch(w.pairs + first, cnt * 4, g.data())) != KT_OK) return st;
+        if ((st = fetch(w.depth, n * 4, depth.data())) != KT_OK) return st;
+        if ((st = fetch(w.ranges, rng.size() * 8, rng.data())) != KT_OK) return st;
+        unsigned long long* k = (unsigned long long*)dst;
+        for (uint64_t b = 0; b < rng.size(); ++b) {
+            const uint64_t a = std::max<uint64_t>(rng[b].x, first), e = std::min<uint64_t>(rng[b].y, last);
+            for (uint64_t i = a; i < e; ++i) {
+                const uint32_t gi = g[i - first];
+                k[i - first] = ((unsigned long long)b << 32) | (gi < n ? depth[gi] : 0u);
+            }
+        }
+    } else {
+        // host-rebuilt: pairs as the reference's binning would list them without its atomic
+        // reordering (Gaussians in index order, bins ascending), from the device's rectangles
+        std::vector<uint32_t> cn(n), depth(n);
+        std::vector<uint2> rect(n);
+        const bool is_keys = stage == KT_GS_STAGE_KEYS_UNSORTED;
+        if ((st = fetch(w.counts, n * 4, cn.data())) != KT_OK) return st;
+        if ((st = fetch(w.rect, n * 8, rect.data())) != KT_OK) return st;
+        if ((st = fetch(w.depth, n * 4, depth.data())) != KT_OK) return st;
+        uint64_t o = 0;
+        for (uint64_t g = 0; g < n && o < last; ++g) {
+            if (!cn[g]) continue;
+            if (o + cn[g] <= first) {
+                o += cn[g];
+                continue;
+            }
+            const uint32_t x0 = rect[g].x & 0xFFFFu, x1 = rect[g].x >> 16;
+            const uint32_t y0 = rect[g].y & 0xFFFFu, y1 = rect[g].y >> 16;
+            for (uint32_t y = y0; y < y1; ++y)
+                for (uint32_t x = x0; x < x1 && o < last; ++x, ++o) {
+                    if (o < first) continue;
+                    if (is_keys)
+                        ((unsigned long long*)dst)[o - first] = ((unsigned long long)(y * tx + x) << 32) | depth[g];
+                    else
+                        ((uint32_t*)dst)[o - first] = (uint32_t)g;
+                }
+        }
+    }
+    if (written) *written = need;
     return KT_OK;
 }
 
@@ -981,133 +1150,12 @@ kt_status kt_gs_set_flags(kt_gs_ctx* c, uint32_t flags) {
 
 kt_status kt_gs_debug_dump(kt_gs_ctx* c, uint32_t path, kt_gs_stage stage, void* dst,
                            uint64_t bytes, uint64_t* written) {
-    if (!c) return KT_ERR_ARG;
-    if (written) *written = 0;
-    if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
-    KT_TRY_CUDA(c, cudaSetDevice(c->device));
-    PathWs& w = c->paths[path];
-    if (!w.have_frame) return fail(c, KT_ERR_STATE, "no frame rendered on this path");
-    KT_TRY_CUDA(c, cudaEventSynchronize(w.done_ev));
-    const FrameCtl& h = *w.host_ctl;
-    const uint64_t n = w.frame_n;
-    const uint64_t K = h.num_keys;
-    const bool sorted_ok = h.plan_ok != 0;
-    const uint32_t tx = c->gp.tiles_x;
-    const bool is_keys = stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_KEYS_UNSORTED;
-    const bool is_vals = stage == KT_GS_STAGE_VALUES_SORTED || stage == KT_GS_STAGE_VALUES_UNSORTED;
-    uint64_t need = 0;
-    switch (stage) {
-        case KT_GS_STAGE_PROJECTED: need = n * sizeof(kt_gaussian2d); break;
-        case KT_GS_STAGE_TILE_COUNTS: need = n * 4; break;
-        case KT_GS_STAGE_OFFSETS: need = n * 8; break;
-        case KT_GS_STAGE_KEYS_UNSORTED:
-        case KT_GS_STAGE_VALUES_UNSORTED:
-        case KT_GS_STAGE_KEYS_SORTED:
-        case KT_GS_STAGE_VALUES_SORTED:
-            if ((stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_VALUES_SORTED) && !sorted_ok)
-                return fail(c, KT_ERR_STATE, "the last frame was not sorted");
-            need = K * (is_keys ? 8 : 4);
-            break;
-        case KT_GS_STAGE_TILE_RANGES: need = (uint64_t)ntiles(c) * 8; break;
-        default: return fail(c, KT_ERR_ARG, "unknown stage");
-    }
-    if (!dst) {
-        if (written) *written = need;
-        return KT_OK;
-    }
-    if (bytes < need) return fail(c, KT_ERR_ARG, "buffer too small: need " + std::to_string(need) + " bytes");
-    auto fetch = [&](const void* d, size_t nbytes, void* out) -> kt_status {
-        if (nbytes) KT_TRY_CUDA(c, cudaMemcpy(out, d, nbytes, cudaMemcpyDeviceToHost));
-        return KT_OK;
-    };
-    kt_status st = KT_OK;
-    if (stage == KT_GS_STAGE_PROJECTED) {
-        std::vector<float4> rec(3 * n);
-        if ((st = fetch(w.rec, sizeof(float4) * 3 * n, rec.data())) != KT_OK) return st;
-        kt_gaussian2d* o = (kt_gaussian2d*)dst;
-        for (uint64_t i = 0; i < n; ++i) {
-            const float4 a = rec[3 * i], b = rec[3 * i + 1], cc = rec[3 * i + 2];
-            o[i].position[0] = a.x;
-            o[i].position[1] = a.y;
-            o[i].z = a.w;
-            o[i].binMask = 0xFFFFFFFFu;
-            o[i].covInv[0] = b.x;
-            o[i].covInv[1] = b.y;
-            o[i].covInv[2] = b.z;
-            o[i].covInv[3] = b.w;
-            o[i].color[0] = cc.x;
-            o[i].color[1] = cc.y;
-            o[i].color[2] = cc.z;
-            o[i].alpha = a.z;
-        }
-    } else if (stage == KT_GS_STAGE_TILE_COUNTS) {
-        if ((st = fetch(w.counts, n * 4, dst)) != KT_OK) return st;
-    } else if (stage == KT_GS_STAGE_TILE_RANGES) {
-        if ((st = fetch(w.ranges, need, dst)) != KT_OK) return st;
-    } else if (stage == KT_GS_STAGE_OFFSETS && w.keys_frame) {
-        if ((st = fetch(w.offsets, n * 8, dst)) != KT_OK) return st;
-    } else if (stage == KT_GS_STAGE_OFFSETS) {
-        // the reference algorithm's scan is in Gaussian index order; the default path has no
-        // such scan, so this dump is the index-order exclusive scan of the device's counts
-        std::vector<uint32_t> cnt(n);
-        if ((st = fetch(w.counts, n * 4, cnt.data())) != KT_OK) return st;
-        uint64_t* o = (uint64_t*)dst;
-        uint64_t run = 0;
-        for (uint64_t i = 0; i < n; ++i) {
-            o[i] = run;
-            run += cnt[i];
-        }
-    } else if ((stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_VALUES_SORTED) && w.keys_frame) {
-        if (is_vals) {
-            if ((st = fetch(w.vals[h.final_buf], K * 4, dst)) != KT_OK) return st;
-        } else {
-            // bin << depth_bits | (depth - depth_min)  ->  bin << 32 | depth, the reference's key
-            if ((st = fetch(w.keys[h.final_buf], K * 8, dst)) != KT_OK) return st;
-            unsigned long long* k = (unsigned long long*)dst;
-            const uint32_t db = h.depth_bits;
-            const unsigned long long dm = db ? ((1ull << db) - 1ull) : 0ull;
-            for (uint64_t i = 0; i < K; ++i)
-                k[i] = ((k[i] >> db) << 32) | (unsigned long long)((uint32_t)(k[i] & dm) + h.depth_min);
-        }
-    } else if (stage == KT_GS_STAGE_KEYS_SORTED || stage == KT_GS_STAGE_VALUES_SORTED) {
-        if (is_vals) {
-            if ((st = fetch(w.pairs, K * 4, dst)) != KT_OK) return st;
-        } else {
-            // bin << 32 | depth bits, the bin of each pair read off the bin ranges
-            std::vector<uint32_t> g(K), depth(n);
-            std::vector<uint2> rng(ntiles(c));
-            if ((st = fetch(w.pairs, K * 4, g.data())) != KT_OK) return st;
-            if ((st = fetch(w.depth, n * 4, depth.data())) != KT_OK) return st;
-            if ((st = fetch(w.ranges, rng.size() * 8, rng.data())) != KT_OK) return st;
-            unsigned long long* k = (unsigned long long*)dst;
-            for (uint64_t b = 0; b < rng.size(); ++b)
-                for (uint64_t i = rng[b].x; i < rng[b].y && i < K; ++i)
-                    k[i] = ((unsigned long long)b << 32) | depth[g[i]];
-        }
-    } else {
-        // pairs as the reference's binning would list them without its atomic reordering:
-        // Gaussians in index order, bins ascending; rebuilt from the device's rectangles
-        std::vector<uint32_t> cnt(n), depth(n);
-        std::vector<uint2> rect(n);
-        if ((st = fetch(w.counts, n * 4, cnt.data())) != KT_OK) return st;
-        if ((st = fetch(w.rect, n * 8, rect.data())) != KT_OK) return st;
-        if ((st = fetch(w.depth, n * 4, depth.data())) != KT_OK) return st;
-        uint64_t o = 0;
-        for (uint64_t g = 0; g < n && o < K; ++g) {
-            if (!cnt[g]) continue;
-            const uint32_t x0 = rect[g].x & 0xFFFFu, x1 = rect[g].x >> 16;
-            const uint32_t y0 = rect[g].y & 0xFFFFu, y1 = rect[g].y >> 16;
-            for (uint32_t y = y0; y < y1; ++y)
-                for (uint32_t x = x0; x < x1 && o < K; ++x, ++o) {
-                    if (is_keys)
-                        ((unsigned long long*)dst)[o] = ((unsigned long long)(y * tx + x) << 32) | depth[g];
-                    else
-                        ((uint32_t*)dst)[o] = (uint32_t)g;
-                }
-        }
-    }
-    if (written) *written = need;
-    return KT_OK;
+    return dump_window(c, path, stage, 0, UINT64_MAX, dst, bytes, written);
+}
+
+kt_status kt_gs_debug_dump_range(kt_gs_ctx* c, uint32_t path, kt_gs_stage stage, uint64_t first,
+                                 uint64_t count, void* dst, uint64_t bytes, uint64_t* written) {
+    return dump_window(c, path, stage, first, count, dst, bytes, written);
 }
 
 kt_status kt_gs_stage_times(kt_gs_ctx* c, uint32_t path, float ms[KT_GS_NSTAGES]) {
@@ -1195,6 +1243,8 @@ kt_status kt_gs_radix_sort_pairs(const uint64_t* keys_in, const uint32_t* vals_i
     if (*temp_bytes < total) return KT_ERR_ARG;
     if (n == 0) return KT_OK;
     if (n > kMaxKeyCapacity || !keys_in || !vals_in || !keys_out || !vals_out) return KT_ERR_ARG;
+    if ((const void*)keys_out == (const void*)keys_in || (const void*)vals_out == (const void*)vals_in)
+        return KT_ERR_ARG;  // in place would race between the CTAs of a single-pass sort
     cudaStream_t s = (cudaStream_t)stream;
     unsigned char* t = (unsigned char*)d_temp;
     FrameCtl* ctl = (FrameCtl*)t;

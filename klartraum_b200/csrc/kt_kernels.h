@@ -80,6 +80,10 @@ cudaError_t launch_sort_pass(const SortIO& io, FrameCtl* ctl, unsigned long long
                              uint32_t pass, uint32_t epoch, uint64_t max_keys, bool packed,
                              cudaStream_t stream);
 size_t sort_status_words(uint64_t max_keys);
+// One CTA runs the sort's look-back wait as tile 1 against tile 0's 256 status words (which must
+// hold no live entry): it gives up after spin_limit polls and sets kErrTimeout in ctl.
+cudaError_t launch_lookback_timeout_probe(const unsigned long long* status, FrameCtl* ctl, uint32_t spin_limit,
+                                          cudaStream_t stream);
 size_t sort_table_words(uint64_t max_keys);
 uint32_t sort_pass_launches(uint64_t max_keys, bool packed);  // kernels one pass launches
 

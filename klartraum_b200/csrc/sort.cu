@@ -92,8 +92,11 @@ __device__ __forceinline__ void issue_tile(SortSmem<PACKED>& sm, int b, uint64_t
 constexpr int kLookbackWindow = 16;  // predecessors read per round trip
 
 // Decoupled look-back for one digit: sum of this digit's counts over all earlier tiles.
+// Gives up after `spin_limit` polls without progress: sets kErrTimeout and returns the partial sum,
+// so the CTA finishes and publishes (the frame or sort is then reported as failed).
 __device__ __forceinline__ uint64_t lookback_digit(const unsigned long long* status, uint32_t tile,
-                                                   uint32_t digit, uint32_t epoch, FrameCtl* ctl) {
+                                                   uint32_t digit, uint32_t epoch, FrameCtl* ctl,
+                                                   uint32_t spin_limit = kSpinLimit) {
     uint64_t excl = 0;
     int64_t j = (int64_t)tile - 1;
     uint32_t spins = 0;
@@ -114,7 +117,7 @@ __device__ __forceinline__ uint64_t lookback_digit(const unsigned long long* sta
         }
         if (incl) break;
         if (used == 0) {
-            if (++spins > kSpinLimit) {
+            if (++spins > spin_limit) {
                 atomicOr(&ctl->error_flags, kErrTimeout);
                 break;
             }
@@ -572,6 +575,14 @@ cudaError_t launch_pass(const SortIO& io, FrameCtl* ctl, unsigned long long* sta
     return cudaGetLastError();
 }
 
+// The look-back wait of a sort pass, run by one CTA as tile 1 against tile 0's status words, which
+// nothing publishes: every digit's wait runs out after `spin_limit` polls and records kErrTimeout
+// in `ctl`, as a pass whose predecessor never finished would. Used to check the timeout path.
+__global__ void __launch_bounds__(256) k_lookback_timeout_probe(const unsigned long long* status, FrameCtl* ctl,
+                                                                uint32_t spin_limit) {
+    (void)lookback_digit(status, 1u, threadIdx.x, 1u, ctl, spin_limit);
+}
+
 }  // namespace
 
 size_t sort_status_words(uint64_t max_keys) {
@@ -604,6 +615,12 @@ static bool sort_is_onesweep(uint64_t max_keys, bool packed) {
     const uint64_t tiles = (max_keys + kSortTile - 1) / kSortTile;
     const uint64_t wave = packed ? (uint64_t)rts_grid<true>(dev) : (uint64_t)rts_grid<false>(dev);
     return tiles <= wave;
+}
+
+cudaError_t launch_lookback_timeout_probe(const unsigned long long* status, FrameCtl* ctl, uint32_t spin_limit,
+                                          cudaStream_t stream) {
+    k_lookback_timeout_probe<<<1, 256, 0, stream>>>(status, ctl, spin_limit);
+    return cudaGetLastError();
 }
 
 uint32_t sort_pass_launches(uint64_t max_keys, bool packed) {

@@ -7,15 +7,21 @@
 // memory. They pass their inputs and outputs; the scratch (control block, the second key and
 // value buffers, look-back status words) lives in g_sort_scratch below.
 //
-// The array is KT_GS_STATIC_SORT_SCRATCH_BYTES (about 12.6 MB) and every device that loads this
-// module keeps it until the process exits. In host code the name g_sort_scratch is only a
-// host-side stand-in for the symbol, not a device address; the device address is looked up
-// with cudaGetSymbolAddress on the first call on each device (with that device current) and
-// cached. That first call on a device should therefore come before any stream capture.
+// The array is KT_GS_STATIC_SORT_SCRATCH_BYTES (13,123,840 bytes, 12.5 MiB) and every device that
+// loads this module keeps it until the process exits. In host code the name g_sort_scratch is
+// only a host-side stand-in for the symbol, not a device address: every call looks the device
+// address up with cudaGetSymbolAddress on the current device (the first call on a device also
+// loads the module there, which is why that first call should come before any stream capture;
+// looking it up each time keeps it right after a cudaDeviceReset reloads the module elsewhere).
 // All calls share the one array: calls whose work overlaps on the GPU race on it and must be
 // ordered by the caller (e.g. one stream). Each call clears what must start at zero (the
 // control block and the status words it uses); the rest keeps the previous call's contents
 // and is overwritten before it is read.
+//
+// kt_gs_radix_sort_status reports a sort's device error bits (a look-back wait that ran out)
+// from the control block of either entry point's scratch; kt_gs_radix_sort_static_timeout_probe
+// makes that wait run out on purpose (a status word that nothing publishes), so that the
+// reporting path can be checked without a faulty sort.
 #include "kt_common.cuh"
 #include "kt_gs.h"
 #include "kt_kernels.h"
@@ -34,22 +40,14 @@ static_assert(kStaticMaxPairs % kSortTile == 0, "maximum must be a whole number 
 
 static __device__ __align__(256) unsigned char g_sort_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 128;
-void* g_scratch_addr[kMaxDevices] = {};  // device address of g_sort_scratch per device
-
-// Device address of the scratch on the current device, looked up once per device.
-cudaError_t scratch_address(void** out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+// Device address of the scratch on the current device. Looked up on every call: the lookup is a
+// host-side table read once the module is loaded, and a cached address would go stale when
+// cudaDeviceReset unloads the module.
+cudaError_t scratch_address(unsigned char** out) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_sort_scratch);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    if (!g_scratch_addr[dev]) {
-        void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_sort_scratch);
-        if (e != cudaSuccess) return e;
-        g_scratch_addr[dev] = p;
-    }
-    *out = g_scratch_addr[dev];
+    *out = (unsigned char*)p;
     return cudaSuccess;
 }
 
@@ -65,10 +63,11 @@ extern "C" kt_status kt_gs_radix_sort_pairs_static(const uint64_t* keys_in, cons
     if (n > kStaticMaxPairs) return KT_ERR_CAPACITY;  // more pairs than the fixed scratch holds
     if (n == 0) return KT_OK;
     if (!keys_in || !vals_in || !keys_out || !vals_out) return KT_ERR_ARG;
-    void* base = nullptr;
-    if (scratch_address(&base) != cudaSuccess) return KT_ERR_CUDA;
+    if ((const void*)keys_out == (const void*)keys_in || (const void*)vals_out == (const void*)vals_in)
+        return KT_ERR_ARG;  // in place would race between the CTAs of a single-pass sort
+    unsigned char* t = nullptr;
+    if (scratch_address(&t) != cudaSuccess) return KT_ERR_CUDA;
     cudaStream_t s = (cudaStream_t)stream;
-    unsigned char* t = (unsigned char*)base;
     FrameCtl* ctl = (FrameCtl*)t;
     unsigned long long* alt_k = (unsigned long long*)(t + kCtlBytes);
     uint32_t* alt_v = (uint32_t*)(t + kCtlBytes + kKeyBytes);
@@ -91,5 +90,35 @@ extern "C" kt_status kt_gs_radix_sort_pairs_static(const uint64_t* keys_in, cons
     for (uint32_t p = 0; p < max_passes; ++p)
         if (launch_sort_pass(io, ctl, status, (uint32_t*)status, p, p + 1, n, false, s) != cudaSuccess)
             return KT_ERR_CUDA;
+    return KT_OK;
+}
+
+extern "C" kt_status kt_gs_radix_sort_status(const void* d_temp, void* stream) {
+    const unsigned char* base = (const unsigned char*)d_temp;
+    if (!base) {
+        unsigned char* t = nullptr;
+        if (scratch_address(&t) != cudaSuccess) return KT_ERR_CUDA;
+        base = t;
+    }
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return KT_ERR_CUDA;
+    unsigned int flags = 0;
+    if (cudaMemcpy(&flags, base + offsetof(FrameCtl, error_flags), sizeof(flags), cudaMemcpyDeviceToHost) !=
+        cudaSuccess)
+        return KT_ERR_CUDA;
+    if (flags & kErrTimeout) return KT_ERR_TIMEOUT;
+    return KT_OK;
+}
+
+extern "C" kt_status kt_gs_radix_sort_static_timeout_probe(uint32_t spin_limit, void* stream) {
+    if (spin_limit == 0 || spin_limit > kSpinLimit) return KT_ERR_ARG;
+    unsigned char* t = nullptr;
+    if (scratch_address(&t) != cudaSuccess) return KT_ERR_CUDA;
+    cudaStream_t s = (cudaStream_t)stream;
+    FrameCtl* ctl = (FrameCtl*)t;
+    unsigned long long* status = (unsigned long long*)(t + kCtlBytes + kKeyBytes + kValBytes);
+    // tile 0's words cleared: epoch 0 and no flag, an entry no look-back accepts
+    if (cudaMemsetAsync(ctl, 0, sizeof(FrameCtl), s) != cudaSuccess) return KT_ERR_CUDA;
+    if (cudaMemsetAsync(status, 0, 256 * 8, s) != cudaSuccess) return KT_ERR_CUDA;
+    if (launch_lookback_timeout_probe(status, ctl, spin_limit, s) != cudaSuccess) return KT_ERR_CUDA;
     return KT_OK;
 }

@@ -168,18 +168,34 @@ class Renderer:
         N.STAGE_KEYS_SORTED: np.dtype(np.uint64),
         N.STAGE_VALUES_SORTED: np.dtype(np.uint32),
         N.STAGE_TILE_RANGES: np.dtype(np.uint32),
+        N.STAGE_DEPTH_ORDER: np.dtype(np.uint32),
+        N.STAGE_COARSE_INFO: np.dtype(np.uint32),
+        N.STAGE_COARSE_LISTS: np.dtype(np.uint32),
+        N.STAGE_SEGMENT_COUNTS: np.dtype(np.uint32),
     }
+    # u32 words per element of the stages whose elements are small records
+    _STAGE_WIDTH = {N.STAGE_TILE_RANGES: 2, N.STAGE_COARSE_INFO: 4, N.STAGE_COARSE_LISTS: 2,
+                    N.STAGE_SEGMENT_COUNTS: 16}
 
-    def dump(self, stage: int, path: int = 0) -> np.ndarray:
+    def dump(self, stage: int, path: int = 0, first: int = 0, count: int | None = None) -> np.ndarray:
+        """A stage buffer of the last frame on `path` (kt_gs_debug_dump), or elements
+        [first, first + count) of it (kt_gs_debug_dump_range)."""
         need = C.c_uint64(0)
-        self._check(self._lib.kt_gs_debug_dump(self._ctx, path, stage, None, 0, C.byref(need)))
+        whole = first == 0 and count is None
+        cnt = (1 << 64) - 1 if count is None else count
+
+        def call(ptr, nbytes, out_len):
+            if whole:
+                return self._lib.kt_gs_debug_dump(self._ctx, path, stage, ptr, nbytes, out_len)
+            return self._lib.kt_gs_debug_dump_range(self._ctx, path, stage, first, cnt, ptr, nbytes, out_len)
+
+        self._check(call(None, 0, C.byref(need)))
         dt = self._STAGE_DTYPES[stage]
         out = np.zeros(need.value // dt.itemsize, dtype=dt)
         wrote = C.c_uint64(0)
-        self._check(self._lib.kt_gs_debug_dump(self._ctx, path, stage, out.ctypes.data if out.size else None,
-                                               out.nbytes, C.byref(wrote)))
-        if stage == N.STAGE_TILE_RANGES:
-            out = out.reshape(-1, 2)
+        self._check(call(out.ctypes.data if out.size else None, out.nbytes, C.byref(wrote)))
+        if stage in self._STAGE_WIDTH:
+            out = out.reshape(-1, self._STAGE_WIDTH[stage])
         return out
 
 
@@ -229,12 +245,19 @@ class GaussianSplattingNode:
         self.inputs: dict[int, object] = {}
         self.set_input(image, 0)
         self.set_input(camera, 1)
-        self.renderer = Renderer(image.width, image.height, **cfg)
-        if isinstance(gaussians, str):
-            self.renderer.load_spz(gaussians)
-        else:
-            self.renderer.set_gaussians(gaussians)
+        self._cfg = dict(cfg)
+        self._scene = gaussians
+        self.renderer = self._make_renderer(self._cfg.pop("num_paths", 1))
         self.number_of_paths = 0
+
+    def _make_renderer(self, num_paths: int) -> Renderer:
+        image = self.inputs[0]
+        r = Renderer(image.width, image.height, num_paths=num_paths, **self._cfg)
+        if isinstance(self._scene, str):
+            r.load_spz(self._scene)
+        else:
+            r.set_gaussians(self._scene)
+        return r
 
     def check_input(self, inp, index: int = 0) -> None:
         # src/vulkan_gaussian_splatting.cpp:220-232
@@ -250,12 +273,19 @@ class GaussianSplattingNode:
         self.inputs[index] = inp
 
     def setup(self, number_paths: int) -> None:
+        """_setup(ctx, numberPaths) (src/vulkan_gaussian_splatting.cpp:234-236): one renderer path
+        (its own device workspace) per graph path, so paths can be in flight together."""
+        if number_paths > self.renderer.config.num_paths:
+            self.renderer.close()
+            self.renderer = self._make_renderer(number_paths)
         self.number_of_paths = number_paths
 
     def record(self, stream: int, path: int) -> None:
         """Enqueue the frame of `path` on `stream` (the reference records a command buffer)."""
+        if path >= max(self.number_of_paths, 1):
+            raise RuntimeError("path index out of range!")
         image, camera = self.inputs[0], self.inputs[1]
-        self.renderer.render(camera.get(path), image.get_image(path), path=0, stream=stream)
+        self.renderer.render(camera.get(path), image.get_image(path), path=path, stream=stream)
 
     def get_type(self) -> str:
         return "GaussianSplatting"

@@ -67,7 +67,9 @@ def lib() -> C.CDLL:
             "ko_sort_pairs": (None, [vp, vp, u64, u32]),
             "ko_tile_ranges": (None, [vp, u64, u32, vp]),
             "ko_rasterize": (None, [cfgp, vp, vp, vp, vp]),
-            "ko_rasterize_f64": (None, [cfgp, vp, vp, vp, vp, vp]),
+            "ko_tile_rects": (None, [cfgp, vp, u64, vp]),
+            "ko_project_f64": (None, [cfgp, vp, vp, u64, vp]),
+            "ko_render_frame_f64": (u64, [cfgp, vp, vp, u64, vp, vp]),
             "ko_render_frame": (u64, [cfgp, vp, vp, u64, vp, vp, vp, vp, vp, vp, u64, vp]),
             "ko_render_projected": (u64, [cfgp, vp, u64, vp, vp, vp, u64, vp]),
         }
@@ -152,14 +154,50 @@ def rasterize(cfg, g2d, vals, ranges, image) -> np.ndarray:
     return img
 
 
-def rasterize_f64(cfg, g2d, vals, ranges, image) -> np.ndarray:
+G2D_F64 = np.dtype([("position", "<f8", (2,)), ("z", "<f8"), ("covInv", "<f8", (4,)), ("color", "<f8", (3,)),
+                    ("alpha", "<f8")])
+
+
+def tile_rects(cfg, g2d) -> np.ndarray:
+    """(x0, x1, y0, y1) bin rectangle per Gaussian, half-open; zeros when culled."""
     g2d = np.ascontiguousarray(g2d, G2D)
-    vals = np.ascontiguousarray(vals, np.uint32)
-    ranges = np.ascontiguousarray(ranges, np.uint32)
+    out = np.zeros((len(g2d), 4), np.uint32)
+    lib().ko_tile_rects(C.byref(cfg), _p(g2d), len(g2d), out.ctypes.data)
+    return out
+
+
+def project_f64(cfg, cam, g3d) -> np.ndarray:
+    g3d = np.ascontiguousarray(g3d, G3D)
+    cam = np.ascontiguousarray(cam, CAM)
+    out = np.zeros(len(g3d), G2D_F64)
+    lib().ko_project_f64(C.byref(cfg), cam.ctypes.data, _p(g3d), len(g3d), _p(out))
+    return out
+
+
+def render_frame_f64(cfg, cam, g3d, image) -> tuple[np.ndarray, int]:
+    """Whole frame in double precision; returns (RGBA float64 in [0, 1], pair count)."""
+    g3d = np.ascontiguousarray(g3d, G3D)
+    cam = np.ascontiguousarray(cam, CAM)
     img = np.ascontiguousarray(image, np.uint8)
     out = np.zeros(img.shape, np.float64)
-    lib().ko_rasterize_f64(C.byref(cfg), _p(g2d), _p(vals), ranges.ctypes.data, img.ctypes.data, out.ctypes.data)
-    return out
+    k = lib().ko_render_frame_f64(C.byref(cfg), cam.ctypes.data, _p(g3d), len(g3d), img.ctypes.data,
+                                  out.ctypes.data)
+    if k == 2**64 - 1:
+        raise MemoryError("double-precision oracle: allocation failed")
+    return out, int(k)
+
+
+def divergence(img_u8, ref_f64, rows=None) -> dict:
+    """Distance of an RGBA8 image from the double-precision image, in units of 1/255:
+    max_abs = max |u8 - 255 * ref|, mean_abs, and PSNR against 255 * ref (dB)."""
+    a = np.asarray(img_u8, np.float64)
+    b = np.asarray(ref_f64, np.float64) * 255.0
+    if rows is not None:
+        a, b = a[rows[0]:rows[1]], b[rows[0]:rows[1]]
+    d = np.abs(a - b)
+    mse = float(np.mean(d * d))
+    return {"max_abs": float(d.max()) if d.size else 0.0, "mean_abs": float(d.mean()) if d.size else 0.0,
+            "psnr_db": float("inf") if mse == 0.0 else float(10.0 * np.log10(255.0 * 255.0 / mse))}
 
 
 def render_frame(cfg, cam, g3d, image) -> dict:

@@ -495,53 +495,6 @@ void ko_rasterize(const ko_config* cfg, const ko_gaussian2d* g, const uint32_t* 
     }
 }
 
-void ko_rasterize_f64(const ko_config* cfg, const ko_gaussian2d* g, const uint32_t* vals,
-                      const uint32_t* ranges, const uint8_t* rgba_in, double* rgba_out) {
-    uint32_t tx = ko_tiles_x(cfg), rb, re;
-    row_span(cfg, &rb, &re);
-    uint32_t ypix0 = rb * cfg->bin_height, ypix1 = re * cfg->bin_height;
-    if (ypix1 > cfg->height) ypix1 = cfg->height;
-    const int per_elem = cfg->exit_per_element != 0;
-    const double tmin = 1.0 - 0.9999;
-#pragma omp parallel for schedule(dynamic, 1) num_threads(ko_get_threads())
-    for (int64_t y = ypix0; y < (int64_t)ypix1; ++y) {
-        for (uint32_t x = 0; x < cfg->width; ++x) {
-            uint32_t bin = (uint32_t)(y / cfg->bin_height) * tx + x / cfg->bin_width;
-            uint32_t start = ranges[2 * bin], end = ranges[2 * bin + 1];
-            uint32_t preend = start + ((end - start) / 64) * 64;
-            double C[3] = {0, 0, 0}, T = 1.0;
-            int done = 0;
-            for (uint32_t i = start; i < end && !done; ++i) {
-                const ko_gaussian2d* gg = &g[vals[i]];
-                double dx = (double)x - gg->position[0], dy = (double)y - gg->position[1];
-                double sx = (double)gg->covInv[0] * dx + (double)gg->covInv[2] * dy;
-                double sy = (double)gg->covInv[1] * dx + (double)gg->covInv[3] * dy;
-                double a = exp(-0.5 * (dx * sx + dy * sy)) * (double)gg->alpha;
-                for (int c = 0; c < 3; ++c) C[c] += (double)gg->color[c] * a * T;
-                T *= (1.0 - a);
-                uint32_t pos = i + 1 - start;
-                int at_check = per_elem || i >= preend || (pos % 64) == 0;
-                if (at_check && T <= tmin) {
-                    if (i < preend && !per_elem && preend < end) {
-                        i = preend - 1; /* jump to the tail: one more element, then stop */
-                        continue;
-                    }
-                    done = 1;
-                }
-            }
-            const uint8_t* p = &rgba_in[((size_t)y * cfg->width + x) * 4];
-            double* o = &rgba_out[((size_t)y * cfg->width + x) * 4];
-            double w = 1.0 - T;
-            for (int c = 0; c < 3; ++c) {
-                double v = p[c] / 255.0 + C[c] * w;
-                o[c] = v < 0 ? 0 : (v > 1 ? 1 : v);
-            }
-            double v = p[3] / 255.0 + w;
-            o[3] = v < 0 ? 0 : (v > 1 ? 1 : v);
-        }
-    }
-}
-
 /* ------------------------------------------------------------ whole frame */
 
 static uint32_t bits_for(uint64_t v) {
@@ -596,5 +549,296 @@ uint64_t ko_render_frame(const ko_config* cfg, const ko_camera* cam, const ko_ga
     }
     uint64_t k = ko_render_projected(cfg, g2d, n, rgba, keys, vals, k_cap, ranges);
     if (!g2d_out) free(g2d);
+    return k;
+}
+
+/* -------------------------------------------------------- bin rectangles */
+
+void ko_tile_rects(const ko_config* cfg, const ko_gaussian2d* g, uint64_t n, uint32_t* rects) {
+#pragma omp parallel for schedule(static) num_threads(ko_get_threads())
+    for (int64_t i = 0; i < (int64_t)n; ++i) {
+        uint32_t x0 = 0, x1 = 0, y0 = 0, y1 = 0;
+        if (!(g[i].z < cfg->cull_z)) overlap_spans(cfg, &g[i], &x0, &x1, &y0, &y1);
+        rects[4 * i] = x0;
+        rects[4 * i + 1] = x1;
+        rects[4 * i + 2] = y0;
+        rects[4 * i + 3] = y1;
+    }
+}
+
+/* ======================================================= double precision
+ *
+ * The same five stages with every float operation done in double: projection
+ * (gsplat_projection.comp:37-237), bin rectangles (gsplat_binning.comp:53-81),
+ * the order of the (bin, Gaussian) pairs (bin, then depth, ties by index:
+ * gsplat_radix_sort_include.glsl:51-63 with the stable sort), and splatting with
+ * the reference's exit rules (gsplat_binned_splatting.comp:41-125). The image
+ * stays in double, unquantised, so that a float32 image's distance from it can
+ * be measured. */
+
+typedef struct { double m[3][3]; } dmat3;
+typedef struct { double m[4][4]; } dmat4;
+
+static dmat4 dmat4_load(const float* p) {
+    dmat4 r;
+    for (int c = 0; c < 4; ++c)
+        for (int k = 0; k < 4; ++k) r.m[c][k] = (double)p[4 * c + k];
+    return r;
+}
+
+static dmat4 dmat4_mul(dmat4 a, dmat4 b) {
+    dmat4 r;
+    for (int c = 0; c < 4; ++c)
+        for (int k = 0; k < 4; ++k)
+            r.m[c][k] = a.m[0][k] * b.m[c][0] + a.m[1][k] * b.m[c][1] + a.m[2][k] * b.m[c][2] +
+                        a.m[3][k] * b.m[c][3];
+    return r;
+}
+
+static void dmat4_vec(dmat4 a, const double v[4], double out[4]) {
+    for (int k = 0; k < 4; ++k)
+        out[k] = a.m[0][k] * v[0] + a.m[1][k] * v[1] + a.m[2][k] * v[2] + a.m[3][k] * v[3];
+}
+
+static dmat3 dmat3_mul(dmat3 a, dmat3 b) {
+    dmat3 r;
+    for (int c = 0; c < 3; ++c)
+        for (int k = 0; k < 3; ++k)
+            r.m[c][k] = a.m[0][k] * b.m[c][0] + a.m[1][k] * b.m[c][1] + a.m[2][k] * b.m[c][2];
+    return r;
+}
+
+static dmat3 dmat3_transpose(dmat3 a) {
+    dmat3 r;
+    for (int c = 0; c < 3; ++c)
+        for (int k = 0; k < 3; ++k) r.m[c][k] = a.m[k][c];
+    return r;
+}
+
+static dmat3 dmat3_cols(double a, double b, double c, double d, double e, double f, double g, double h,
+                        double i) {
+    dmat3 r;
+    r.m[0][0] = a; r.m[0][1] = b; r.m[0][2] = c;
+    r.m[1][0] = d; r.m[1][1] = e; r.m[1][2] = f;
+    r.m[2][0] = g; r.m[2][1] = h; r.m[2][2] = i;
+    return r;
+}
+
+/* inverse of a column-major 2x2 given as (c00, c01, c10, c11) */
+static void dmat2_inverse(const double a[4], double r[4]) {
+    double det = a[0] * a[3] - a[2] * a[1];
+    double inv = 1.0 / det;
+    r[0] = a[3] * inv;
+    r[1] = -a[1] * inv;
+    r[2] = -a[2] * inv;
+    r[3] = a[0] * inv;
+}
+
+static double dsh_color(double base, const float coeffs[15], const double dir[3], int deg) {
+    double x = dir[0], y = dir[1], z = dir[2];
+    double x2 = x * x, y2 = y * y, z2 = z * z;
+    double sh[16];
+    sh[0] = 0.282095;
+    sh[1] = -0.488603 * y;
+    sh[2] = -0.488603 * z;
+    sh[3] = -0.488603 * x;
+    sh[4] = 1.092548 * x * y;
+    sh[5] = -1.092548 * y * z;
+    sh[6] = 0.315392 * (2.0 * z2 - x2 - y2);
+    sh[7] = -1.092548 * x * z;
+    sh[8] = 0.546274 * (x2 - y2);
+    sh[9] = -0.590044 * y * (3.0 * x2 - y2);
+    sh[10] = 2.890611 * x * y * z;
+    sh[11] = -0.457046 * y * (4.0 * z2 - x2 - y2);
+    sh[12] = 0.373176 * z * (2.0 * z2 - 3.0 * x2 - 3.0 * y2);
+    sh[13] = -0.457046 * x * (4.0 * z2 - x2 - y2);
+    sh[14] = 1.445306 * z * (x2 - y2);
+    sh[15] = -0.590044 * x * (x2 - 3.0 * y2);
+    int ncoef = (deg + 1) * (deg + 1) - 1;
+    double value = 0.5 + base * sh[0];
+    for (int i = 0; i < ncoef; i++) value += (double)coeffs[i] * sh[i + 1];
+    return value;
+}
+
+void ko_project_f64(const ko_config* cfg, const ko_camera* cam, const ko_gaussian3d* in, uint64_t n,
+                    ko_gaussian2d_f64* out) {
+    dmat4 model = dmat4_load(cam->model), view = dmat4_load(cam->view), proj = dmat4_load(cam->proj);
+    dmat4 pvm = dmat4_mul(dmat4_mul(proj, view), model);
+    dmat4 mv = dmat4_mul(model, view);
+    const double half_w = (double)cfg->width * 0.5, half_h = (double)cfg->height * 0.5;
+    const double sxx = (double)cfg->width * cfg->width, syy = (double)cfg->height * cfg->height;
+    const double sxy = (double)cfg->width * cfg->height;
+    const int deg = cfg->sh_degree < 0 ? 3 : cfg->sh_degree;
+    const double focalX = proj.m[0][0], focalY = proj.m[1][1];
+    const double limx = 1.3 * (1.0 / focalX), limy = 1.3 * (1.0 / focalY);
+#pragma omp parallel for schedule(static) num_threads(ko_get_threads())
+    for (int64_t i = 0; i < (int64_t)n; ++i) {
+        const ko_gaussian3d* g = &in[i];
+        double p4[4] = {g->position[0], g->position[1], g->position[2], 1.0};
+        double pos[4], t4[4];
+        dmat4_vec(pvm, p4, pos);
+        dmat4_vec(mv, p4, t4);
+        ko_gaussian2d_f64 o;
+        o.position[0] = (pos[0] / pos[3] + 1.0) * half_w;
+        o.position[1] = (pos[1] / pos[3] + 1.0) * half_h;
+        o.z = pos[2];
+        /* calculateCovarianceMatrix2D (comp:53-118) */
+        double qx = g->rotation[0], qy = g->rotation[1], qz = g->rotation[2], qw = g->rotation[3];
+        dmat3 R = dmat3_cols(1.0 - 2.0 * (qy * qy + qz * qz), 2.0 * (qx * qy - qw * qz), 2.0 * (qx * qz + qw * qy),
+                             2.0 * (qx * qy + qw * qz), 1.0 - 2.0 * (qx * qx + qz * qz), 2.0 * (qy * qz - qw * qx),
+                             2.0 * (qx * qz - qw * qy), 2.0 * (qy * qz + qw * qx), 1.0 - 2.0 * (qx * qx + qy * qy));
+        dmat3 S = dmat3_cols(g->scale[0], 0, 0, 0, g->scale[1], 0, 0, 0, g->scale[2]);
+        dmat3 M = dmat3_mul(S, R);
+        dmat3 cov3d = dmat3_mul(dmat3_transpose(M), M);
+        double tx = t4[0], ty = t4[1], tz = t4[2];
+        double txtz = tx / tz, tytz = ty / tz;
+        tx = fmin(limx, fmax(-limx, txtz)) * tz;
+        ty = fmax(limy, fmin(-limy, tytz)) * tz; /* the shader's clamp of t.y, kept as written */
+        dmat3 J = dmat3_cols(focalX / tz, 0.0, -(focalX * tx) / (tz * tz),
+                             0.0, focalY / tz, -(focalY * ty) / (tz * tz),
+                             0.0, 0.0, 0.0);
+        dmat3 W = dmat3_cols(mv.m[0][0], mv.m[1][0], mv.m[2][0],
+                             mv.m[0][1], mv.m[1][1], mv.m[2][1],
+                             mv.m[0][2], mv.m[1][2], mv.m[2][2]);
+        dmat3 T = dmat3_mul(W, J);
+        dmat3 cov = dmat3_mul(dmat3_mul(dmat3_transpose(T), dmat3_transpose(cov3d)), T);
+        double c2[4] = {cov.m[0][0] * sxx + 0.3, cov.m[0][1] * sxy, cov.m[1][0] * sxy, cov.m[1][1] * syy + 0.3};
+        dmat2_inverse(c2, o.covInv);
+        double len = sqrt(t4[0] * t4[0] + t4[1] * t4[1] + t4[2] * t4[2]);
+        double dir[3] = {t4[0] / len, t4[1] / len, t4[2] / len};
+        o.color[0] = dsh_color(g->color[0], g->shR, dir, deg);
+        o.color[1] = dsh_color(g->color[1], g->shG, dir, deg);
+        o.color[2] = dsh_color(g->color[2], g->shB, dir, deg);
+        o.alpha = g->alpha;
+        out[i] = o;
+    }
+}
+
+/* bins met by a double record, as overlap_spans: a closed-interval test per column and row */
+static void overlap_spans_f64(const ko_config* cfg, const ko_gaussian2d_f64* g, uint32_t r[4]) {
+    double cov[4];
+    dmat2_inverse(g->covInv, cov);
+    double sx = sqrt(cov[0]) * 2.5, sy = sqrt(cov[3]) * 2.5;
+    double mn[2] = {g->position[0] - sx, g->position[1] - sy};
+    double mx[2] = {g->position[0] + sx, g->position[1] + sy};
+    uint32_t tx = ko_tiles_x(cfg), rb, re;
+    row_span(cfg, &rb, &re);
+    double cw = cfg->bin_width, ch = cfg->bin_height;
+    uint32_t a = tx, b = 0, c = re, d = rb;
+    for (uint32_t gx = 0; gx < tx; ++gx)
+        if (!(mx[0] < gx * cw || mn[0] > (gx + 1) * cw)) {
+            if (a == tx) a = gx;
+            b = gx + 1;
+        }
+    for (uint32_t gy = rb; gy < re; ++gy)
+        if (!(mx[1] < gy * ch || mn[1] > (gy + 1) * ch)) {
+            if (c == re) c = gy;
+            d = gy + 1;
+        }
+    if (a >= b || c >= d) a = b = c = d = 0;
+    r[0] = a; r[1] = b; r[2] = c; r[3] = d;
+}
+
+typedef struct { double z; uint32_t idx; } ko_depth_item;
+
+static int cmp_depth(const void* pa, const void* pb) {
+    const ko_depth_item* a = (const ko_depth_item*)pa;
+    const ko_depth_item* b = (const ko_depth_item*)pb;
+    if (a->z < b->z) return -1;
+    if (a->z > b->z) return 1;
+    return a->idx < b->idx ? -1 : (a->idx > b->idx);
+}
+
+uint64_t ko_render_frame_f64(const ko_config* cfg, const ko_camera* cam, const ko_gaussian3d* in,
+                             uint64_t n, const uint8_t* rgba_in, double* rgba_out) {
+    uint32_t tx = ko_tiles_x(cfg), ntiles = tx * ko_tiles_y(cfg), rb, re;
+    row_span(cfg, &rb, &re);
+    ko_gaussian2d_f64* g = (ko_gaussian2d_f64*)malloc((n ? n : 1) * sizeof(ko_gaussian2d_f64));
+    uint32_t* rect = (uint32_t*)malloc((n ? n : 1) * 4 * sizeof(uint32_t));
+    ko_depth_item* order = (ko_depth_item*)malloc((n ? n : 1) * sizeof(ko_depth_item));
+    uint64_t* start = (uint64_t*)calloc((size_t)ntiles + 1, sizeof(uint64_t));
+    if (!g || !rect || !order || !start) {
+        free(g); free(rect); free(order); free(start);
+        return UINT64_MAX;
+    }
+    ko_project_f64(cfg, cam, in, n, g);
+#pragma omp parallel for schedule(static) num_threads(ko_get_threads())
+    for (int64_t i = 0; i < (int64_t)n; ++i) {
+        uint32_t* r = &rect[4 * i];
+        r[0] = r[1] = r[2] = r[3] = 0;
+        if (!(g[i].z < (double)cfg->cull_z)) overlap_spans_f64(cfg, &g[i], r);
+    }
+    /* pairs by bin, then depth (ties by index): a stable counting sort of the Gaussians in
+     * depth order */
+    uint64_t nv = 0;
+    for (uint64_t i = 0; i < n; ++i) {
+        const uint32_t* r = &rect[4 * i];
+        if (r[1] <= r[0] || r[3] <= r[2]) continue;
+        order[nv].z = g[i].z;
+        order[nv].idx = (uint32_t)i;
+        ++nv;
+        for (uint32_t y = r[2]; y < r[3]; ++y)
+            for (uint32_t x = r[0]; x < r[1]; ++x) start[(uint64_t)y * tx + x + 1]++;
+    }
+    qsort(order, nv, sizeof(ko_depth_item), cmp_depth);
+    for (uint32_t b = 0; b < ntiles; ++b) start[b + 1] += start[b];
+    uint64_t k = start[ntiles];
+    uint32_t* vals = (uint32_t*)malloc((k ? k : 1) * sizeof(uint32_t));
+    uint64_t* cur = (uint64_t*)malloc((size_t)ntiles * sizeof(uint64_t));
+    if (!vals || !cur) {
+        free(g); free(rect); free(order); free(start); free(vals); free(cur);
+        return UINT64_MAX;
+    }
+    memcpy(cur, start, (size_t)ntiles * sizeof(uint64_t));
+    for (uint64_t q = 0; q < nv; ++q) {
+        const uint32_t* r = &rect[4 * order[q].idx];
+        for (uint32_t y = r[2]; y < r[3]; ++y)
+            for (uint32_t x = r[0]; x < r[1]; ++x) vals[cur[(uint64_t)y * tx + x]++] = order[q].idx;
+    }
+    const double tmin = 1.0 - 0.9999;
+    const int per_elem = cfg->exit_per_element != 0;
+    uint32_t ypix0 = rb * cfg->bin_height, ypix1 = re * cfg->bin_height;
+    if (ypix1 > cfg->height) ypix1 = cfg->height;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(ko_get_threads())
+    for (int64_t y = 0; y < (int64_t)cfg->height; ++y) {
+        for (uint32_t x = 0; x < cfg->width; ++x) {
+            const uint8_t* p = &rgba_in[((size_t)y * cfg->width + x) * 4];
+            double* o = &rgba_out[((size_t)y * cfg->width + x) * 4];
+            if (y < (int64_t)ypix0 || y >= (int64_t)ypix1) { /* rows outside the band: untouched */
+                for (int c = 0; c < 4; ++c) o[c] = p[c] / 255.0;
+                continue;
+            }
+            uint32_t bin = (uint32_t)(y / cfg->bin_height) * tx + x / cfg->bin_width;
+            uint64_t s0 = start[bin], s1 = start[bin + 1];
+            uint64_t preend = s0 + ((s1 - s0) / 64) * 64;
+            double C[3] = {0, 0, 0}, T = 1.0;
+            int done = 0;
+            for (uint64_t i = s0; i < s1; ++i) {
+                const ko_gaussian2d_f64* gg = &g[vals[i]];
+                double dx = (double)x - gg->position[0], dy = (double)y - gg->position[1];
+                double sx = gg->covInv[0] * dx + gg->covInv[2] * dy;
+                double sy = gg->covInv[1] * dx + gg->covInv[3] * dy;
+                double a = exp(-0.5 * (dx * sx + dy * sy)) * gg->alpha;
+                for (int c = 0; c < 3; ++c) C[c] += gg->color[c] * a * T;
+                T *= (1.0 - a);
+                if (per_elem || i >= preend) {
+                    if (T <= tmin) { done = 1; break; }
+                } else if ((i + 1 - s0) % 64 == 0 && T <= tmin) {
+                    /* batch-end exit (comp:98); the tail loop (comp:104-117) still runs */
+                    i = preend - 1;
+                    if (preend == s1) { done = 1; break; }
+                }
+            }
+            (void)done;
+            double w = 1.0 - T;
+            for (int c = 0; c < 3; ++c) {
+                double v = p[c] / 255.0 + C[c] * w;
+                o[c] = v < 0 ? 0 : (v > 1 ? 1 : v);
+            }
+            double v = p[3] / 255.0 + w;
+            o[3] = v < 0 ? 0 : (v > 1 ? 1 : v);
+        }
+    }
+    free(g); free(rect); free(order); free(start); free(vals); free(cur);
     return k;
 }

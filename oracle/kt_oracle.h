@@ -14,6 +14,8 @@
  *   ko_sort_pairs     shaders/gsplat/gsplat_radix_sort_{histogram,hist_prefix_sum,hist_scatter}.comp
  *   ko_tile_ranges    shaders/gsplat/gsplat_bin_bounds.comp:30-72
  *   ko_rasterize      shaders/gsplat/gsplat_binned_splatting.comp:41-125
+ * ko_project_f64 / ko_render_frame_f64 repeat the same stages in double precision, the
+ * reference's algorithm without float32 rounding, to log how far float32 images drift.
  * The reference's screen (512x512), 4x4 bin grid and 2N key cap are generalised to a
  * W x H screen with bin_width x bin_height cells and an exactly sized key list; with
  * W = H = 512 and 128-px bins the geometry is the reference's.
@@ -97,10 +99,29 @@ void ko_tile_ranges(const uint64_t* keys, uint64_t k, uint32_t ntiles, uint32_t*
 void ko_rasterize(const ko_config* cfg, const ko_gaussian2d* g, const uint32_t* vals,
                   const uint32_t* ranges, uint8_t* rgba);
 
-/* Stage 6 in double precision (same records, same order), float RGBA output in [0,1]
- * before quantisation, to log how far float32 results drift. */
-void ko_rasterize_f64(const ko_config* cfg, const ko_gaussian2d* g, const uint32_t* vals,
-                      const uint32_t* ranges, const uint8_t* rgba_in, double* rgba_out);
+/* Bin rectangle of every projected Gaussian: rects[4i..4i+3] = x0, x1, y0, y1 (half-open, bins;
+ * rows clipped to the binned rows), all zero when culled (gsplat_binning.comp:53-81,113). */
+void ko_tile_rects(const ko_config* cfg, const ko_gaussian2d* g, uint64_t n, uint32_t* rects);
+
+/* A projected Gaussian in double precision (same fields as ko_gaussian2d, no bin mask). */
+typedef struct ko_gaussian2d_f64 {
+    double position[2];
+    double z;
+    double covInv[4];
+    double color[3];
+    double alpha;
+} ko_gaussian2d_f64;
+
+/* Projection in double precision: the same operations as ko_project, every one in double. */
+void ko_project_f64(const ko_config* cfg, const ko_camera* cam, const ko_gaussian3d* in, uint64_t n,
+                    ko_gaussian2d_f64* out);
+
+/* Whole frame in double precision: projection, bin rectangles, pairs by (bin, depth, index),
+ * splatting with the reference's exit rules; rgba_out = unquantised RGBA in [0, 1] (rows outside
+ * the binned rows keep rgba_in / 255). Returns the pair count, UINT64_MAX on allocation failure.
+ * Used to measure how far float32 images (the GPU's and ko_render_frame's) drift. */
+uint64_t ko_render_frame_f64(const ko_config* cfg, const ko_camera* cam, const ko_gaussian3d* in,
+                             uint64_t n, const uint8_t* rgba_in, double* rgba_out);
 
 /*
  * Whole frame from 3D Gaussians. Scratch is allocated inside. Returns the key count, or

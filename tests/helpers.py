@@ -77,3 +77,23 @@ def compare_projected(gpu: np.ndarray, ref: np.ndarray) -> None:
         g, r = bits(gpu[f]), bits(ref[f])
         bad = np.nonzero((g != r).reshape(len(g), -1).any(axis=1))[0]
         assert bad.size == 0, f"{f}: {bad.size} records differ, first {bad[:5]}: gpu {gpu[f][bad[:3]]} ref {ref[f][bad[:3]]}"
+
+
+# Divergence of float32 images from the double-precision oracle, collected over the session and
+# printed by tests/conftest.py at the end of the run.
+DIVERGENCE: list[dict] = []
+
+
+def log_divergence(case: str, gpu_img: np.ndarray, f32_img: np.ndarray, f64_img: np.ndarray,
+                   rows: tuple | None = None) -> dict:
+    """Measure the GPU image and the float32 oracle's image against the double-precision
+    oracle's (in units of 1/255), record both, and check that the GPU drifts no further from the
+    double-precision result than the float32 oracle does plus one quantisation step."""
+    import oracle
+
+    g = oracle.divergence(gpu_img, f64_img, rows)
+    f = oracle.divergence(f32_img, f64_img, rows)
+    entry = {"case": case, "gpu": g, "f32_oracle": f}
+    DIVERGENCE.append(entry)
+    assert g["max_abs"] <= f["max_abs"] + 1.0, entry
+    return entry

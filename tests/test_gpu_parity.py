@@ -11,7 +11,7 @@ import oracle
 from klartraum_b200 import Renderer, make_scene, native as N, orbit_camera, workload_camera
 from klartraum_b200.scenes import WORKLOADS
 
-from helpers import background, compare_projected, kat_bin_records, kat_project_scene, psnr
+from helpers import background, compare_projected, kat_bin_records, kat_project_scene, log_divergence, psnr
 
 pytestmark = pytest.mark.gpu
 
@@ -55,6 +55,7 @@ def run_case(name, wname, n, wh, bin_size, sh, flags, rows, bg_kind, dist):
     cfg = oracle.config(W, H, bin_size=bin_size, sh_degree=sh, exit_per_element=bool(flags & N.FLAG_EXIT_PER_ELEMENT),
                         tile_rows=rows)
     ref = oracle.render_frame(cfg, cam, g3d, bg)
+    ref["cfg"], ref["cam"], ref["g3d"] = cfg, cam, g3d
     return r, out, ref, bg
 
 
@@ -62,7 +63,11 @@ def run_case(name, wname, n, wh, bin_size, sh, flags, rows, bg_kind, dist):
 @pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
 def test_frame_parity(case, keys):
     """Every stage buffer against the oracle, for the default path (pairs placed in bin order)
-    and the reference-structured one (scan, key emission, radix sort, boundary search)."""
+    and the reference-structured one (scan, key emission, radix sort, boundary search). On the
+    default path OFFSETS and the unsorted keys/values are rebuilt on the host from the device's
+    counts and rectangles (no device buffer holds them), so their equalities check the counts and
+    rectangles, not a kernel of their own; the placement's device buffers are checked in
+    test_gpu_placement.py. The image is also measured against the double-precision oracle."""
     case = list(case)
     if keys:
         case[6] |= N.FLAG_SORTED_KEYS
@@ -83,6 +88,8 @@ def test_frame_parity(case, keys):
     assert psnr(out, ref["image"]) >= 50.0
     if st["num_keys"]:
         assert not np.array_equal(out, bg), "nothing was drawn"
+    f64, _ = oracle.render_frame_f64(ref["cfg"], ref["cam"], ref["g3d"], bg)
+    log_divergence(f"{case[0]}-{'sorted_keys' if keys else 'placed'}", out, ref["image"], f64)
 
 
 def test_projection_known_answer_on_gpu():

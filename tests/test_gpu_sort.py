@@ -69,3 +69,44 @@ def test_sort_constant_and_zero_width_keys_are_stable_copies():
     for bits in (0, 8, 64):
         sk, sv = gpu_sort(keys, vals, bits)
         assert np.array_equal(sv, vals) and np.array_equal(sk, keys)
+
+
+def test_sort_status_is_ok_after_a_sort_and_aliasing_is_refused():
+    lib = N.load()
+    n = 100_000
+    rng = np.random.default_rng(9)
+    kin = torch.from_numpy(rng.integers(0, 1 << 40, size=n, dtype=np.uint64).view(np.int64)).cuda()
+    vin = torch.arange(n, dtype=torch.int32, device="cuda")
+    kout, vout = torch.empty_like(kin), torch.empty_like(vin)
+    size = N.radix_sort_pairs(None, None, None, None, n, 40)
+    temp = torch.empty(size, dtype=torch.uint8, device="cuda")
+    N.radix_sort_pairs(kin, vin, kout, vout, n, 40, temp)
+    assert lib.kt_gs_radix_sort_status(temp.data_ptr(), None) == N.KT_OK
+    # in place is refused before anything is enqueued
+    with pytest.raises(N.KtError) as e:
+        N.radix_sort_pairs(kin, vin, kin, vout, n, 40, temp)
+    assert e.value.status == N.KT_ERR_ARG
+
+
+def test_lookback_timeout_reaches_the_sort_status():
+    """The bounded look-back wait of a sort pass, run against status words that nothing
+    publishes (kt_gs_radix_sort_static_timeout_probe), gives up after its poll limit and records
+    the timeout where a sort records it; kt_gs_radix_sort_status then reports KT_ERR_TIMEOUT, the
+    context stays usable, and the next static sort clears the flag."""
+    lib = N.load()
+    assert lib.kt_gs_radix_sort_static_timeout_probe(0, None) == N.KT_ERR_ARG
+    assert lib.kt_gs_radix_sort_static_timeout_probe(4096, None) == N.KT_OK
+    assert lib.kt_gs_radix_sort_status(None, None) == N.KT_ERR_TIMEOUT
+    n = 5000
+    kin = torch.arange(n, 0, -1, dtype=torch.int64, device="cuda")
+    vin = torch.arange(n, dtype=torch.int32, device="cuda")
+    kout, vout = torch.empty_like(kin), torch.empty_like(vin)
+    fn = lib.kt_gs_radix_sort_pairs_static
+    import ctypes as C
+
+    fn.restype = C.c_int
+    fn.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint32, C.c_void_p]
+    assert fn(kin.data_ptr(), vin.data_ptr(), kout.data_ptr(), vout.data_ptr(), n, 16, None) == N.KT_OK
+    assert lib.kt_gs_radix_sort_status(None, None) == N.KT_OK
+    assert torch.equal(vout, torch.arange(n - 1, -1, -1, dtype=torch.int32, device="cuda"))
+    assert fn(kin.data_ptr(), vin.data_ptr(), kin.data_ptr(), vout.data_ptr(), n, 16, None) == N.KT_ERR_ARG
