@@ -9,18 +9,26 @@ scaling). Inputs are larger than L2: 240 MB of scene planes and ~390 MB of key b
 frame, so no L2 flush is needed between frames.
 
 Frames are kept in flight as klartraum's engine keeps its paths: frame s renders on path
-s mod 3 with its own stream, so consecutive frames overlap on the GPU.
+s mod 3 with its own stream, so consecutive frames overlap on the GPU. A timed window is
+exactly `--steps` frames between a barrier + synchronize on both sides (CUDA events, max over
+ranks); windows repeat until about a second of device time has passed and the median window
+gives `value` and `ms_per_step`. `e2e` is the same through kt_gs_render_host_clear (camera up,
+image cleared on the device as the reference's render pass clears it, frame copied to pinned
+host memory); `e2e.image_in` copies a host image in as well (kt_gs_render_host).
+
+The same line also carries, measured the same way at the same N:
+  multiview_3m   the 3,000,000-Gaussian SH3 scene over the 64-view orbit at 1920x1080 (weak)
+  bands_6m       the 6,000,000-Gaussian SH3 4K frame split into bin-row bands, one per rank,
+                 balanced on measured time, strips all-gathered over NCCL every step (strong)
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-    python bench.py --mode bands [--workload large_6m]   # one 4K frame split over the GPUs
+    python bench.py --workload stress_2m --paths 1          # another scene as the main workload
+    python bench.py --mode bands [--workload large_6m]      # the banded frame as the main line
 
-``--mode bands`` splits every frame into bin-row bands, one per rank, balanced on per-row pair
-counts, and all-gathers the strips each step (strong scaling). ``--launch`` (default graph)
-replays each frame as a captured CUDA graph; ``--sorted-keys`` bins through the
-reference-structured path.
-``--impl reference`` times the CPU restatement of the reference algorithm (the oracle, C +
-OpenMP on all host cores) on the same workload; under torchrun only rank 0 runs it.
-Prints one JSON line (rank 0).
+``--launch`` (default graph) replays each frame as a captured CUDA graph; ``--sorted-keys`` bins
+through the reference-structured path. ``--impl reference`` times the CPU restatement of the
+reference algorithm (the oracle, C + OpenMP on all host cores) on the same workload; under
+torchrun only rank 0 runs it. Prints one JSON line (rank 0).
 """
 
 from __future__ import annotations
@@ -49,7 +57,7 @@ PATHS = 3  # frames in flight, each on its own path and stream, as klartraum's e
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=400)
+    p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--paths", type=int, default=PATHS,
@@ -59,6 +67,8 @@ def parse():
                    help="repeat the timed window of `steps` frames until this much device time has passed")
     p.add_argument("--no-multiview", dest="multiview", action="store_false",
                    help="skip the 3M-Gaussian multi-view batch measured after the main workload")
+    p.add_argument("--no-bands", dest="bands", action="store_false",
+                   help="skip the 6M-Gaussian 4K frame split into bands measured after the main workload")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--small", action="store_true", help="tiny frame for profiler captures")
     p.add_argument("--mode", choices=["views", "bands"], default="views",
@@ -434,33 +444,41 @@ def measure_views(args, w, rank, world, local_rank, dev, dist, cams, scene, stag
         h.copy_(bg.cpu())
     r.set_flags(run_flags)
 
-    def frame_host(s, first_of_window):
+    def frame_host(s, first_of_window, clear):
         p = s % paths
         if not first_of_window or s >= paths:
             r.sync(p)
-        r.render_host(cams[view_of(s)], hosts[p].data_ptr(), path=p, stream=streams[p].cuda_stream)
+        if clear:  # the render pass's clear colour, set on the device; only the camera goes up
+            r.render_host_clear(cams[view_of(s)], hosts[p].data_ptr(), clear=(0, 0, 0, 255), path=p,
+                                stream=streams[p].cuda_stream)
+        else:  # the host image copied in, blended into, copied out
+            r.render_host(cams[view_of(s)], hosts[p].data_ptr(), path=p, stream=streams[p].cuda_stream)
 
-    for s in range(2 * paths):
-        frame_host(s, False)
-    for p in range(paths):
-        r.sync(p)
-
-    def window_host():
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(streams[0])
-        for strm in streams[1:]:
-            strm.wait_event(e0)
-        for s in range(e2e_steps):
-            frame_host(s, True)
+    def e2e_pass(clear):
+        for s in range(2 * paths):
+            frame_host(s, False, clear)
         for p in range(paths):
             r.sync(p)
-        join_streams()
-        e1.record(streams[0])
-        return e0, e1
 
-    ems, _ = timed_windows(window_host, world, dev, dist, local_rank, args.min_window_ms)
+        def window_host():
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(streams[0])
+            for strm in streams[1:]:
+                strm.wait_event(e0)
+            for s in range(e2e_steps):
+                frame_host(s, True, clear)
+            for p in range(paths):
+                r.sync(p)
+            join_streams()
+            e1.record(streams[0])
+            return e0, e1
+
+        ems, _ = timed_windows(window_host, world, dev, dist, local_rank, args.min_window_ms)
+        return window_stats(ems, e2e_steps)
+
+    ewins = e2e_pass(True)
+    iwins = e2e_pass(False)
     clock.stop()
-    ewins = window_stats(ems, e2e_steps)
     e2e_fps = world / (ewins["ms_per_step_median"] / 1000.0)
     img_bytes = w.width * w.height * 4
     view0 = None
@@ -474,10 +492,16 @@ def measure_views(args, w, rank, world, local_rank, dev, dist, cams, scene, stag
     out = {
         "value": fps, "ms_per_step": ms_step, "windows": wins, "st": st, "K_avg": K_avg, "passes_avg": passes_avg,
         "stages": stages, "roofline": roofline, "clocks": clocks, "view0": view0,
-        "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": img_bytes + 192,
+        "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": 192,
                 "d2h_bytes_per_step": img_bytes + st["status_bytes"], "steps": e2e_steps, "windows": ewins,
-                "api": f"kt_gs_render_host (pinned host image in, rendered image out) with {paths} frames in "
-                       "flight on their own paths and streams; kt_gs_sync(path) before a host image is reused"},
+                "api": f"kt_gs_render_host_clear (camera from host, image cleared to (0,0,0,1) on the device as "
+                       f"the reference's render pass clears it, rendered image copied to pinned host memory) "
+                       f"with {paths} frames in flight on their own paths and streams; kt_gs_sync(path) before a "
+                       "host image is reused",
+                "image_in": {"value": world / (iwins["ms_per_step_median"] / 1000.0), "unit": "frames/s",
+                             "h2d_bytes_per_step": img_bytes + 192,
+                             "d2h_bytes_per_step": img_bytes + st["status_bytes"], "windows": iwins,
+                             "api": "kt_gs_render_host: the host image copied in, blended into, copied out"}},
         "gpu_launches": st["launches"] * args.steps * world * wins["windows"],
     }
     r.close()
@@ -529,6 +553,22 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
               "windows": mm["windows"], "keys_per_frame": mm["K_avg"], "e2e": mm["e2e"], "clocks": mm["clocks"],
               "scaling": "weak", "n_gpus": world}
 
+    # the 6M-Gaussian 4K frame split into bin-row bands over the ranks (strong scaling), at every N
+    bd = None
+    if args.bands and not args.small:
+        wb = WORKLOADS["large_6m"]
+        cams_b = orbit_views(N_VIEWS, wb.distance, wb.width, wb.height, fovy_deg=wb.fovy_deg)
+        keep, scene = scene_of(wb)
+        mb = measure_bands(args, wb, rank, world, local_rank, dev, dist, cams_b, scene)
+        del keep, scene
+        bd = {"workload": f"{wb.name}: {wb.n:,} Gaussians SH{wb.sh_degree} {wb.width}x{wb.height}, one frame per "
+                          f"step split into {world} bin-row bands (time-balanced), strips all-gathered over NCCL",
+              "value": mb["value"], "unit": "frames/s", "gaussians_per_s": mb["value"] * wb.n,
+              "ms_per_step": mb["ms_per_step"], "steps": args.steps, "windows": mb["windows"], "scaling": "strong",
+              "n_gpus": world, "bands": mb["bands"], "band_frame_ms": mb["band_frame_ms"],
+              "band_history": mb["band_history"], "gather_bytes_per_step": mb["gather_bytes_per_step"],
+              "stages_rank0": mb["stages_rank0"], "e2e": mb["e2e"], "clocks": mb["clocks"]}
+
     st = m["st"]
     launches_per_frame = st["launches"]
     line = {
@@ -553,6 +593,8 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
     }
     if mv is not None:
         line["multiview_3m"] = mv
+    if bd is not None:
+        line["bands_6m"] = bd
     if world == 1 and rank == 0 and not args.no_cpu_baseline and not args.small:
         line["cpu_baseline"] = cpu_baseline(w, cams, m["view0"])
     if rank == 0:
@@ -561,44 +603,31 @@ def run_ours(args, w, cfg_block, rank, world, local_rank):
         dist.destroy_process_group()
 
 
-def run_bands(args, w, rank, world, local_rank):
+def measure_bands(args, w, rank, world, local_rank, dev, dist, cams, scene) -> dict:
     """One frame split into bin-row bands over the ranks (strong scaling). Every rank projects
-    the whole scene but bins, sorts and draws only its band; the strips are all-gathered over
-    NCCL every step, so every rank ends the step holding the full frame. Bands are balanced once
-    on the per-row pair counts of view 0 (each rank's rows summed with one all_reduce)."""
-    import datetime
+    the whole scene but sorts, places and draws only the Gaussians that meet its band; the strips
+    are all-gathered over NCCL every step, so every rank ends the step holding the full frame.
 
+    Bands start balanced on the pairs per bin row of view 0 (each rank's rows summed with one
+    all_reduce) and are then rebalanced twice on measured time: every rank times its own band's
+    frames (CUDA events, no gather), the times are all-gathered, and each band's rows are weighted
+    by its measured time per pair, so the cuts follow time rather than pair counts."""
     import torch
-    import torch.distributed as dist
 
-    from klartraum_b200 import Renderer, make_scene, native as N, orbit_views
-    from klartraum_b200.multigpu import StripGather, band_pixel_rows, band_rows, broadcast_scene, row_pair_counts
+    from klartraum_b200 import Renderer, native as N
+    from klartraum_b200.multigpu import StripGather, band_pixel_rows, band_rows, rebalance_bands, row_pair_counts
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    if args.small:
-        w = type(w)(**{**w.__dict__, "n": 20000, "width": 640, "height": 360})
-    cams = orbit_views(N_VIEWS, w.distance, w.width, w.height, fovy_deg=w.fovy_deg)
     tx, ty = (w.width + 15) // 16, (w.height + 15) // 16
-    if world > 1:
-        scene_dev, n_rec = broadcast_scene(make_scene(w) if rank == 0 else None, dist, rank, dev)
-        torch.cuda.synchronize()
-        scene_host = None
-    else:
-        scene_dev, scene_host = None, make_scene(w)
-
     base_flags = N.FLAG_SORTED_KEYS if args.sorted_keys else 0
 
     def renderer(band):
         r = Renderer(w.width, w.height, bin_size=16, sh_degree=w.sh_degree, device=local_rank,
                      flags=N.FLAG_TIMING | base_flags, tile_rows=band)
-        if scene_dev is not None:
-            r.set_gaussians_device(scene_dev.data_ptr(), n_rec)
+        if isinstance(scene, tuple):
+            r.set_gaussians_device(*scene)
             torch.cuda.synchronize()
         else:
-            r.set_gaussians(scene_host)
+            r.set_gaussians(scene)
         return r
 
     bg = torch.zeros((w.height, w.width, 4), dtype=torch.uint8, device=dev)
@@ -607,18 +636,46 @@ def run_bands(args, w, rank, world, local_rank):
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
 
-    # balance: equal bands render view 0, their per-row pair counts are summed over the ranks
+    def all_ranks(vals):
+        t = torch.tensor(vals, dtype=torch.float64, device=dev)
+        if world > 1:
+            out = torch.empty((world, len(vals)), dtype=torch.float64, device=dev)
+            dist.all_gather_into_tensor(out, t)
+            return out.cpu().numpy()
+        return t.cpu().numpy()[None, :]
+
+    # pairs per bin row of view 0 (equal bands, summed over the ranks)
     bands = band_rows(ty, world)
     r = renderer(bands[rank])
     r.render(cams[0], img, stream=sptr)
     torch.cuda.synchronize()
-    rows = torch.from_numpy(row_pair_counts(r.dump(N.STAGE_TILE_RANGES), tx, ty)).to(dev)
+    rows = torch.from_numpy(row_pair_counts(r.dump(N.STAGE_TILE_RANGES), tx, ty).astype(np.float64)).to(dev)
     r.close()
     if world > 1:
         dist.all_reduce(rows)
-    bands = band_rows(ty, world, rows.cpu().numpy())
+    rows = rows.cpu().numpy() + 1.0
+    bands = band_rows(ty, world, rows)
+    history = [{"bands": bands}]
+    calib = 24
+    for it in range(2 if world > 1 else 0):
+        r = renderer(bands[rank])
+        for v in range(calib):  # checked frames size the buffers
+            r.render(cams[v % N_VIEWS], img, stream=sptr)
+        torch.cuda.synchronize()
+        r.set_flags(base_flags | N.FLAG_ASYNC)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for v in range(calib):
+            r.render(cams[v % N_VIEWS], img, stream=sptr)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        r.sync()
+        r.close()
+        t = all_ranks([e0.elapsed_time(e1) / calib])[:, 0]
+        history[-1]["ms_per_band"] = [float(x) for x in t]
+        bands = rebalance_bands(rows, bands, t)
+        history.append({"bands": bands})
     r = renderer(bands[rank])
-    del scene_dev
     px = [band_pixel_rows(b, 16, w.height) for b in bands]
     gather = StripGather(px, w.width, w.height, dist, rank, dev) if world > 1 else (lambda x: x)
 
@@ -629,7 +686,7 @@ def run_bands(args, w, rank, world, local_rank):
 
     for s in range(max(args.warmup, 3)):
         frame(s)
-    for v in sorted({s % N_VIEWS for s in range(args.steps)}):
+    for v in sorted({s % N_VIEWS for s in range(max(args.steps, 64))}):
         r.render(cams[v], img, stream=sptr)  # checked frames size the key buffers for every view
     torch.cuda.synchronize()
     r.stage_times_total()
@@ -653,13 +710,12 @@ def run_bands(args, w, rank, world, local_rank):
     clocks = clock.summary(tw0, tw1)
     wins = window_stats(ms_list, args.steps)
     ms_step = wins["ms_per_step_median"]
-    fps = 1000.0 / ms_step
     stage_ms, timed_frames = r.stage_times_total()
     cnt = r.counters()
     st = r.stats()
     nplanes = (3 * (w.sh_degree + 1) ** 2 + 3) // 4
-    stages, roofline, K_avg, passes_avg = stage_report(w, cnt, st, stage_ms, timed_frames, nplanes,
-                                                       r.stage_names)
+    stages, roofline, K_avg, passes_avg = stage_report(w, cnt, st, stage_ms, timed_frames, nplanes, r.stage_names)
+    band_ms = all_ranks([stage_ms["frame"] / max(timed_frames, 1)])[:, 0]
 
     # end to end: camera from host through the API, band render, strip gather, frame to host
     r.set_flags(base_flags)
@@ -681,34 +737,67 @@ def run_bands(args, w, rank, world, local_rank):
         return e0, e1
 
     ems, _ = timed_windows(window_host, world, dev, dist, local_rank, args.min_window_ms)
-    ewins = window_stats(ems, e2e_steps)
-    e2e_fps = 1000.0 / ewins["ms_per_step_median"]
     clock.stop()
+    ewins = window_stats(ems, e2e_steps)
     img_bytes = w.width * w.height * 4
+    r.close()
+    return {
+        "value": 1000.0 / ms_step, "ms_per_step": ms_step, "windows": wins, "clocks": clocks,
+        "bands": bands, "band_history": history, "band_frame_ms": [float(x) for x in band_ms],
+        "keys_per_frame_this_rank": K_avg, "sort_passes_per_frame": passes_avg, "stages_rank0": stages,
+        "roofline": roofline, "gather_bytes_per_step": gather.bytes_per_frame if world > 1 else 0,
+        "e2e": {"value": 1000.0 / ewins["ms_per_step_median"], "unit": "frames/s", "h2d_bytes_per_step": 192 * world,
+                "d2h_bytes_per_step": img_bytes, "steps": e2e_steps, "windows": ewins,
+                "api": "kt_gs_render (camera from host) + strip all_gather + frame copied to pinned host on rank 0"},
+        "launches_per_step": st["launches"] * world,
+    }
+
+
+def run_bands(args, w, rank, world, local_rank):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from klartraum_b200 import make_scene, orbit_views
+    from klartraum_b200.multigpu import broadcast_scene
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if args.small:
+        w = type(w)(**{**w.__dict__, "n": 20000, "width": 640, "height": 360})
+    cams = orbit_views(N_VIEWS, w.distance, w.width, w.height, fovy_deg=w.fovy_deg)
+    keep = None
+    if world > 1:
+        keep, n_rec = broadcast_scene(make_scene(w) if rank == 0 else None, dist, rank, dev)
+        torch.cuda.synchronize()
+        scene = (keep.data_ptr(), n_rec)
+    else:
+        scene = make_scene(w)
+    m = measure_bands(args, w, rank, world, local_rank, dev, dist, cams, scene)
+    del keep
     line = {
         "metric": f"frames/s, {w.n:,}-splat SH{w.sh_degree} {w.width}x{w.height} split into bin-row bands",
-        "value": fps, "unit": "frames/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "value": m["value"], "unit": "frames/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": m["ms_per_step"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{w.name}: {w.n:,} Gaussians SH{w.sh_degree} {w.width}x{w.height}, 16x16-px bins, "
                                f"{N_VIEWS}-view orbit, one frame per step split into {world} bin-row bands",
-                   "bands": bands, "parallelism": f"bands{world}: projection replicated, binning/sort/splat per band, "
-                                                  "strips all-gathered (NCCL) every step",
+                   "bands": m["bands"], "parallelism": f"bands{world}: projection replicated, depth sort, placement "
+                                                       "and splatting of the Gaussians that meet each band, strips "
+                                                       "all-gathered (NCCL) every step",
                    "l2": "inputs larger than L2; no flush", "seed": w.seed},
         "timing": {"protocol": f"windows of exactly {args.steps} frames repeated for >= {args.min_window_ms:.0f} ms "
-                               "of device time (max over ranks), median window", **wins},
-        "keys_per_frame_this_rank": K_avg, "sort_passes_per_frame": passes_avg, "stages_rank0": stages,
-        "roofline": roofline,
-        "gather_bytes_per_step": gather.bytes_per_frame if world > 1 else 0,
-        "e2e": {"value": e2e_fps, "unit": "frames/s", "h2d_bytes_per_step": 192 * world,
-                "d2h_bytes_per_step": img_bytes, "steps": e2e_steps, "windows": ewins,
-                "api": "kt_gs_render (camera from host) + strip all_gather + frame copied to pinned host on rank 0"},
-        "gpu_launches": st["launches"] * args.steps * world, "gpu_launches_per_step": st["launches"] * world,
-        "clocks": clocks,
+                               "of device time (max over ranks), median window", **m["windows"]},
+        **{k: m[k] for k in ("band_history", "band_frame_ms", "keys_per_frame_this_rank", "sort_passes_per_frame",
+                             "stages_rank0", "roofline", "gather_bytes_per_step", "e2e")},
+        "gpu_launches": m["launches_per_step"] * args.steps, "gpu_launches_per_step": m["launches_per_step"],
+        "clocks": m["clocks"],
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    r.close()
     if world > 1:
         dist.destroy_process_group()
 

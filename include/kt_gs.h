@@ -184,9 +184,9 @@ typedef enum kt_gs_stage {
     KT_GS_STAGE_VALUES_SORTED = 6,   /* uint32[K] Gaussian index of every pair in sorted order */
     KT_GS_STAGE_TILE_RANGES = 7,     /* uint32[2 * tiles] {start, end} per bin (StartAndEnd,
                                         gsplat_types.glsl:21-24); empty bins {0, 0} */
-    KT_GS_STAGE_DEPTH_ORDER = 8,     /* uint32[N] Gaussian index at each position of the depth sort's
-                                        output (stable by depth; Gaussians without bins sort as the
-                                        deepest) */
+    KT_GS_STAGE_DEPTH_ORDER = 8,     /* uint32[num_visible] Gaussian index at each position of the depth
+                                        sort's output: the Gaussians that meet a bin, stably by depth
+                                        (the sort drops the others) */
     KT_GS_STAGE_COARSE_INFO = 9,     /* uint32[4 * coarse bins] per coarse bin (4x4 bins, over the binned
                                         rows): list start, entries, first segment, 0 */
     KT_GS_STAGE_COARSE_LISTS = 10,   /* uint32[2 * entries] (Gaussian index, mask of the 4x4 bins met:
@@ -293,6 +293,15 @@ kt_status kt_gs_render(kt_gs_ctx* ctx, const kt_camera_mvp* cam, void* d_rgba8, 
 kt_status kt_gs_render_host(kt_gs_ctx* ctx, const kt_camera_mvp* cam, void* h_rgba8,
                             uint32_t path, void* stream);
 
+/*
+ * The same with the image cleared on the device to `clear_rgba` before the splatting, as the
+ * reference's render pass clears the swap-chain image to (0, 0, 0, 1) before the compute pass
+ * blends into it (include/klartraum/renderpass.hpp:170, gsplat_binned_splatting.comp:119-124):
+ * nothing is copied to the device but the camera; the rendered image is copied out.
+ */
+kt_status kt_gs_render_host_clear(kt_gs_ctx* ctx, const kt_camera_mvp* cam, const uint8_t clear_rgba[4],
+                                  void* h_rgba8, uint32_t path, void* stream);
+
 /* Render n_views cameras, view v into d_rgba8[v] (device pointers), on `stream`. */
 kt_status kt_gs_render_batch(kt_gs_ctx* ctx, const kt_camera_mvp* cams, uint32_t n_views,
                              void* const* d_rgba8, void* stream);
@@ -356,7 +365,7 @@ kt_status kt_gs_radix_sort_pairs(const uint64_t* d_keys_in, const uint32_t* d_va
  * memory pool already holds the device's free memory. No counterpart in the reference.
  *
  * The caller passes inputs and outputs only; the scratch is one fixed array of
- * KT_GS_STATIC_SORT_SCRATCH_BYTES (13,123,840 bytes, 12.5 MiB) in the library, kept on every
+ * KT_GS_STATIC_SORT_SCRATCH_BYTES (13,127,680 bytes, 12.52 MiB) in the library, kept on every
  * device that loads it until the process exits. n above KT_GS_STATIC_SORT_MAX_PAIRS returns
  * KT_ERR_CAPACITY without doing anything. keys_out/vals_out must not alias keys_in/vals_in
  * (KT_ERR_ARG). Every call looks up the array's device address on the current device; the first
@@ -366,7 +375,7 @@ kt_status kt_gs_radix_sort_pairs(const uint64_t* d_keys_in, const uint32_t* d_va
  * A look-back wait that runs out is reported by kt_gs_radix_sort_status(NULL, stream).
  */
 #define KT_GS_STATIC_SORT_MAX_PAIRS 1048576u
-#define KT_GS_STATIC_SORT_SCRATCH_BYTES 13123840u
+#define KT_GS_STATIC_SORT_SCRATCH_BYTES 13127680u
 kt_status kt_gs_radix_sort_pairs_static(const uint64_t* d_keys_in, const uint32_t* d_vals_in,
                                         uint64_t* d_keys_out, uint32_t* d_vals_out, uint64_t n,
                                         uint32_t key_bits, void* stream);

@@ -57,7 +57,7 @@ EXPORTED_SYMBOLS = [
     "kt_gs_debug_dump", "kt_gs_stage_times", "kt_gs_stage_times_total", "kt_gs_radix_sort_pairs",
     "kt_gs_set_flags", "kt_gs_counters_take", "kt_gs_spz_decode", "kt_gs_load_ply", "kt_gs_ply_decode",
     "kt_gs_debug_dump_range", "kt_gs_radix_sort_pairs_static", "kt_gs_radix_sort_status",
-    "kt_gs_radix_sort_static_timeout_probe",
+    "kt_gs_radix_sort_static_timeout_probe", "kt_gs_render_host_clear",
 ]
 
 
@@ -141,6 +141,7 @@ def load() -> C.CDLL:
         "kt_gs_ply_decode": (C.c_int, [C.c_char_p, vp, C.c_uint64, C.POINTER(C.c_uint64)]),
         "kt_gs_render": (C.c_int, [vp, vp, vp, u32, vp]),
         "kt_gs_render_host": (C.c_int, [vp, vp, vp, u32, vp]),
+        "kt_gs_render_host_clear": (C.c_int, [vp, vp, C.POINTER(C.c_uint8), vp, u32, vp]),
         "kt_gs_render_batch": (C.c_int, [vp, vp, u32, vp, vp]),
         "kt_gs_render_projected": (C.c_int, [vp, vp, u64, vp, u32, vp]),
         "kt_gs_sync": (C.c_int, [vp, u32]),

@@ -734,6 +734,41 @@ kt_status upload_scene(kt_gs_ctx* c, const kt_gaussian3d* src, bool src_on_devic
     return KT_OK;
 }
 
+// A frame rendered into a host image. With `clear` the device image is first set to that colour
+// (the render pass's clear, renderpass.hpp:170) instead of being copied in from the host image.
+kt_status render_host_impl(kt_gs_ctx* c, const kt_camera_mvp* cam, const uint8_t* clear, void* h_rgba8,
+                           uint32_t path, void* stream) {
+    if (!c) return KT_ERR_ARG;
+    if (!cam || !h_rgba8) return fail(c, KT_ERR_ARG, "NULL camera or image");
+    if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
+    KT_TRY_CUDA(c, cudaSetDevice(c->device));
+    PathWs& w = c->paths[path];
+    const uint64_t pixels = (uint64_t)c->cfg.width * c->cfg.height;
+    const size_t bytes = pixels * 4;
+    if (!w.img) KT_TRY_CUDA(c, cudaMalloc(&w.img, bytes));
+    cudaStream_t s = (cudaStream_t)stream;
+    if (clear)
+        KT_TRY_CUDA(c, launch_fill_image(w.img, pixels, make_uchar4(clear[0], clear[1], clear[2], clear[3]), s));
+    else
+        KT_TRY_CUDA(c, cudaMemcpyAsync(w.img, h_rgba8, bytes, cudaMemcpyHostToDevice, s));
+    if (c->cfg.flags & KT_GS_FLAG_ASYNC) {
+        // frames in flight: everything is enqueued; kt_gs_sync(path) waits for the image copy too
+        kt_status st = render_impl(c, path, Source::Scene, cam, w.img, s);
+        if (st != KT_OK) return st;
+        KT_TRY_CUDA(c, cudaMemcpyAsync(h_rgba8, w.img, bytes, cudaMemcpyDeviceToHost, s));
+        KT_TRY_CUDA(c, cudaEventRecord(w.done_ev, s));
+        return KT_OK;
+    }
+    const uint32_t saved = c->cfg.flags;
+    c->cfg.flags &= ~KT_GS_FLAG_ASYNC;
+    kt_status st = render_impl(c, path, Source::Scene, cam, w.img, s);
+    c->cfg.flags = saved;
+    if (st != KT_OK) return st;
+    KT_TRY_CUDA(c, cudaMemcpyAsync(h_rgba8, w.img, bytes, cudaMemcpyDeviceToHost, s));
+    KT_TRY_CUDA(c, cudaStreamSynchronize(s));
+    return KT_OK;
+}
+
 // Elements [first, first + count) of a stage buffer of the path's last frame, copied to host
 // memory (count is clipped to the stage's length). The default binning path has no device
 // buffer for OFFSETS, KEYS_UNSORTED and VALUES_UNSORTED: those dumps are rebuilt here on the
@@ -764,7 +799,7 @@ kt_status dump_window(kt_gs_ctx* c, uint32_t path, kt_gs_stage stage, uint64_t f
         case KT_GS_STAGE_KEYS_SORTED: len = K; esize = 8; break;
         case KT_GS_STAGE_VALUES_SORTED: len = K; esize = 4; break;
         case KT_GS_STAGE_TILE_RANGES: len = ntiles(c); esize = 8; break;
-        case KT_GS_STAGE_DEPTH_ORDER: len = n; esize = 4; break;
+        case KT_GS_STAGE_DEPTH_ORDER: len = std::min<uint64_t>(h.num_visible, n); esize = 4; break;
         case KT_GS_STAGE_COARSE_INFO: len = w.last_ncoarse; esize = 16; break;
         case KT_GS_STAGE_COARSE_LISTS: len = h.num_entries; esize = 8; break;
         case KT_GS_STAGE_SEGMENT_COUNTS: len = h.num_segments; esize = 64; break;
@@ -1009,31 +1044,13 @@ kt_status kt_gs_render(kt_gs_ctx* c, const kt_camera_mvp* cam, void* d_rgba8, ui
 
 kt_status kt_gs_render_host(kt_gs_ctx* c, const kt_camera_mvp* cam, void* h_rgba8, uint32_t path,
                             void* stream) {
-    if (!c) return KT_ERR_ARG;
-    if (!cam || !h_rgba8) return fail(c, KT_ERR_ARG, "NULL camera or image");
-    if (path >= c->paths.size()) return fail(c, KT_ERR_ARG, "path index out of range");
-    KT_TRY_CUDA(c, cudaSetDevice(c->device));
-    PathWs& w = c->paths[path];
-    const size_t bytes = (size_t)c->cfg.width * c->cfg.height * 4;
-    if (!w.img) KT_TRY_CUDA(c, cudaMalloc(&w.img, bytes));
-    cudaStream_t s = (cudaStream_t)stream;
-    KT_TRY_CUDA(c, cudaMemcpyAsync(w.img, h_rgba8, bytes, cudaMemcpyHostToDevice, s));
-    if (c->cfg.flags & KT_GS_FLAG_ASYNC) {
-        // frames in flight: everything is enqueued; kt_gs_sync(path) waits for the image copy too
-        kt_status st = render_impl(c, path, Source::Scene, cam, w.img, s);
-        if (st != KT_OK) return st;
-        KT_TRY_CUDA(c, cudaMemcpyAsync(h_rgba8, w.img, bytes, cudaMemcpyDeviceToHost, s));
-        KT_TRY_CUDA(c, cudaEventRecord(w.done_ev, s));
-        return KT_OK;
-    }
-    const uint32_t saved = c->cfg.flags;
-    c->cfg.flags &= ~KT_GS_FLAG_ASYNC;
-    kt_status st = render_impl(c, path, Source::Scene, cam, w.img, s);
-    c->cfg.flags = saved;
-    if (st != KT_OK) return st;
-    KT_TRY_CUDA(c, cudaMemcpyAsync(h_rgba8, w.img, bytes, cudaMemcpyDeviceToHost, s));
-    KT_TRY_CUDA(c, cudaStreamSynchronize(s));
-    return KT_OK;
+    return render_host_impl(c, cam, nullptr, h_rgba8, path, stream);
+}
+
+kt_status kt_gs_render_host_clear(kt_gs_ctx* c, const kt_camera_mvp* cam, const uint8_t clear_rgba[4],
+                                  void* h_rgba8, uint32_t path, void* stream) {
+    if (!clear_rgba) return c ? fail(c, KT_ERR_ARG, "NULL clear colour") : KT_ERR_ARG;
+    return render_host_impl(c, cam, clear_rgba, h_rgba8, path, stream);
 }
 
 kt_status kt_gs_render_batch(kt_gs_ctx* c, const kt_camera_mvp* cams, uint32_t n_views,
@@ -1116,7 +1133,7 @@ kt_status kt_gs_frame_stats(kt_gs_ctx* c, uint32_t path, kt_gs_stats* out) {
     PlaceGeom pg{};
     if (place_geometry(c->gp, w.frame_n, w.cap, &pg) == cudaSuccess) {
         out->place_chunks = pg.nchunks;
-        out->place_bands = pg.nbands;
+        out->place_bands = h.place_nbands ? h.place_nbands : pg.nbands;  // the device's choice for the frame
     }
     return KT_OK;
 }

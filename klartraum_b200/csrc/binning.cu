@@ -59,9 +59,11 @@ __global__ void k_frame_init(FrameCtl* ctl, FrameCtl* ctl_depth, uint2* ranges, 
 }
 
 // Depth key of every Gaussian, (depth - depth_min) << idx_bits | index, with the digit
-// histograms of the depth sort. Gaussians that touch no bin take the largest depth; they
-// emit nothing, so where they land does not matter. The last CTA to finish plans the passes.
-__device__ void plan_passes(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes, int mode);
+// histograms of the depth sort. A Gaussian that meets no bin is written as kDropKey and left out
+// of the histograms: the sort's first executed pass drops it, so the sorted order holds the
+// visible Gaussians only. The last CTA to finish plans the passes.
+__device__ void plan_passes(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes, int mode,
+                            uint64_t keep);
 
 __global__ void __launch_bounds__(256) k_depth_keys(FrameBufs fb, uint64_t n, uint32_t max_passes) {
     __shared__ uint32_t s_last;
@@ -95,17 +97,18 @@ __global__ void __launch_bounds__(256) k_depth_keys(FrameBufs fb, uint64_t n, ui
             const uint64_t i = i0 + (uint64_t)u * stride;
             if (i >= n_up) break;  // uniform over the warp
             const bool live = i < n;
-            const uint32_t dk = live ? (cnt[u] != 0u ? dep[u] - dmin : dtop) : 0u;
-            if (live) out[i] = ((unsigned long long)dk << ibits) | i;
-            const uint32_t act = __ballot_sync(0xFFFFFFFFu, live);
+            const bool vis = live && cnt[u] != 0u;
+            const uint32_t dk = vis ? dep[u] - dmin : 0u;
+            if (live) out[i] = vis ? (((unsigned long long)dk << ibits) | i) : kDropKey;
+            const uint32_t act = __ballot_sync(0xFFFFFFFFu, vis);
             for (uint32_t p = 0; p < npass; ++p) {
                 if (dbits - 8 * p == 1) {  // a one-bit digit (the top of a 25-bit range): two counts
-                    const uint32_t ones = __ballot_sync(0xFFFFFFFFu, live && ((dk >> (8 * p)) & 1u));
+                    const uint32_t ones = __ballot_sync(0xFFFFFFFFu, vis && ((dk >> (8 * p)) & 1u));
                     if (lane == 0) {
                         hw[p][0] += (uint32_t)__popc(act & ~ones);
                         hw[p][1] += (uint32_t)__popc(ones);
                     }
-                } else if (live) {  // warp-private counters: only lanes of this warp collide
+                } else if (vis) {  // warp-private counters: only lanes of this warp collide
                     atomicAdd(&hw[p][(dk >> (8 * p)) & 255u], 1u);
                 }
             }
@@ -130,12 +133,15 @@ __global__ void __launch_bounds__(256) k_depth_keys(FrameBufs fb, uint64_t n, ui
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    plan_passes(cd, n, max_passes, 0);
+    plan_passes(cd, n, max_passes, 0, __ldcg(&ctl->num_visible));
 }
 
 // One CTA of 256 threads: which passes move data, their bucket bases and buffer order. The
-// histograms may come from other CTAs of the calling kernel (read at L2).
-__device__ void plan_passes(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes, int mode) {
+// histograms may come from other CTAs of the calling kernel (read at L2). keep < num_keys: only
+// `keep` elements are not kDropKey; the first executed pass drops the others (a pass is forced
+// if none would run) and the later passes read `keep` elements.
+__device__ void plan_passes(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes, int mode,
+                            uint64_t keep) {
     __shared__ uint32_t s_warp[8];
     const int tid = threadIdx.x;
     const uint64_t K = __ldcg(&ctl->num_keys);
@@ -162,15 +168,23 @@ __device__ void plan_passes(FrameCtl* ctl, uint64_t capacity, uint32_t max_passe
         executed += run[p];
     }
     if (tid == 0) {
-        if (mode == 1 && executed == 0 && K > 0) {
-            run[0] = 1u;  // a single-bucket pass is a stable copy into the output
+        const bool dropping = keep < K;
+        if ((mode == 1 || dropping) && executed == 0 && K > 0) {
+            run[0] = 1u;  // a single-bucket pass is a stable copy into the output (and drops)
             executed = 1;
         }
         uint32_t cur = 0, e = 0;
+        bool dropped = false;
         for (uint32_t p = 0; p < max_passes; ++p) {
             ctl->pass_run[p] = run[p];
             ctl->pass_ticket[p] = 0u;
+            ctl->pass_in[p] = dropped ? keep : K;
+            ctl->pass_drop[p] = 0u;
             if (!run[p]) continue;
+            if (dropping && !dropped) {
+                ctl->pass_drop[p] = 1u;
+                dropped = true;
+            }
             uint32_t dst;
             if (mode == 0) {
                 dst = cur ^ 1u;
@@ -194,7 +208,7 @@ __device__ void plan_passes(FrameCtl* ctl, uint64_t capacity, uint32_t max_passe
 
 __global__ void __launch_bounds__(256) k_plan(FrameCtl* ctl, uint64_t capacity, uint32_t max_passes,
                                               int mode) {
-    plan_passes(ctl, capacity, max_passes, mode);
+    plan_passes(ctl, capacity, max_passes, mode, ~0ull);
 }
 
 // After the pair placement: fold the frame's error bits and sizes into the running totals
@@ -212,7 +226,10 @@ __global__ void k_frame_totals(const FrameCtl* ctl, const FrameCtl* ctl_depth, F
         totals->sort_bytes += ctl->passes_run ? ctl->num_keys * (unsigned long long)ctl->passes_run *
                                                     (ctl->packed ? 16ull : 24ull)
                                               : ctl->num_keys * 4ull + ctl->num_entries * 8ull;
-        totals->depth_sort_bytes += ctl_depth->num_keys * (unsigned long long)ctl_depth->passes_run * 16ull;
+        unsigned long long moved = 0;
+        for (int p = 0; p < kMaxPasses; ++p)
+            if (ctl_depth->pass_run[p]) moved += ctl_depth->pass_in[p];
+        totals->depth_sort_bytes += moved * 16ull;
     }
 }
 

@@ -26,6 +26,8 @@ constexpr int kMaxPasses = 8;          // 8-bit digits over at most 64 key bits
 constexpr uint32_t kErrCapacity = 1u;  // key count above the key buffers' capacity
 constexpr uint32_t kErrTimeout = 2u;   // a look-back wait ran out of iterations
 constexpr uint32_t kSpinLimit = 1u << 22;  // look-back polls before giving up (~seconds)
+// Element of the depth sort for a Gaussian that meets no bin: the first executed pass drops it.
+constexpr unsigned long long kDropKey = ~0ull;
 
 // Look-back status word: [epoch:24][flag:2][value:38].
 constexpr uint64_t kFlagAggregate = 1ull;
@@ -61,11 +63,15 @@ struct FrameCtl {
     unsigned int num_segments;        // segments of the coarse lists (second placement level)
     unsigned int done_scan;           // CTAs of the coarse scan that finished
     unsigned int done_count;          // CTAs of the bin count that finished
+    unsigned int place_band_rows;     // coarse rows per band of the coarse placement, this frame
+    unsigned int place_nbands;        // bands of the coarse placement, this frame
     unsigned int pass_ticket[kMaxPasses];
     unsigned int pass_run[kMaxPasses];
     unsigned int pass_src[kMaxPasses];
     unsigned int pass_dst[kMaxPasses];
     unsigned int pass_mask[kMaxPasses];  // digit mask: 255, or fewer bits in the last pass
+    unsigned int pass_drop[kMaxPasses];  // 1: the pass drops elements equal to kDropKey (packed sorts)
+    unsigned long long pass_in[kMaxPasses];  // elements the pass reads
     unsigned int hist[kMaxPasses][256];   // digit histograms of the keys
     unsigned int base[kMaxPasses][256];   // exclusive scans of hist
 };

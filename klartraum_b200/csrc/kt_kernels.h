@@ -88,6 +88,8 @@ size_t sort_table_words(uint64_t max_keys);
 uint32_t sort_pass_launches(uint64_t max_keys, bool packed);  // kernels one pass launches
 
 // raster.cu
+// every pixel of an RGBA8 image set to `value` (the render pass's clear before the splatting)
+cudaError_t launch_fill_image(uchar4* img, uint64_t pixels, uchar4 value, cudaStream_t stream);
 cudaError_t launch_rasterize(const float4* rec, const SortIO& io, const uint2* ranges,
                              const FrameCtl* ctl, const GridParams& gp, uchar4* img,
                              bool per_element_exit, cudaStream_t stream);

@@ -49,8 +49,20 @@ constexpr uint32_t kMaxChunks = 8192;
 constexpr uint32_t kCountThreads = 512;
 constexpr uint32_t kCoarseMax = 16384;         // coarse bins x chunks of a count CTA (64 KB of counters)
 constexpr uint32_t kGroupMax = 8;              // chunks of a count CTA
-constexpr uint32_t kBandMax = 1024;            // coarse bins of a placement band (4 KB of cursors per warp)
+#ifndef KT_PLACE_BAND_MAX
+#define KT_PLACE_BAND_MAX 1024
+#endif
+constexpr uint32_t kBandMax = KT_PLACE_BAND_MAX;  // coarse bins of a placement band (4 B of cursor per warp each)
 constexpr uint32_t kPlaceWarps = 16;           // warps of a coarse-placement CTA
+// Coarse bins of a placement band when the lists get long runs: every warp of the coarse placement
+// writes each list of its band at its own cursor, so the partly written 32-B sectors in flight are
+// about (warps in flight) x (bins of a band); when a (chunk, coarse bin) run holds several entries,
+// a small band keeps those sectors in L2 until they are whole.
+#ifndef KT_PLACE_LONG_RUN_BAND
+#define KT_PLACE_LONG_RUN_BAND 64
+#endif
+constexpr uint32_t kLongRunBand = KT_PLACE_LONG_RUN_BAND;
+constexpr uint32_t kLongRun = 4;               // entries per (chunk, coarse bin) that count as long runs
 constexpr uint32_t kPlaceCtasPerSm = 2;
 constexpr uint32_t kPlaceSmem = 2 * kPlaceWarps * kBandMax * 4;  // cursors and lane bits
 constexpr uint32_t kSegLen = 256;              // entries of a segment of a coarse list
@@ -101,8 +113,10 @@ __global__ void __launch_bounds__(kCountThreads) k_coarse_count(FrameBufs fb, Gr
     const FrameCtl* cd = fb.ctl_depth;
     const unsigned long long* __restrict__ order = io_select(fb.gsort, cd->final_buf);
     const unsigned long long imask = (1ull << cd->idx_bits) - 1ull;
+    // the depth order holds the Gaussians that meet a bin (the sort dropped the others)
+    const uint64_t nsorted = min((uint64_t)fb.ctl->num_visible, n);
     const uint64_t q0 = (uint64_t)c0 * pg.chunk_len;
-    const uint64_t q1 = min(q0 + (uint64_t)gk * pg.chunk_len, n);
+    const uint64_t q1 = min(q0 + (uint64_t)gk * pg.chunk_len, nsorted);
     constexpr int kU = 4;  // Gaussians in flight per thread
     for (uint64_t qb = q0 + threadIdx.x; qb < q1; qb += kU * kCountThreads) {
         uint32_t g[kU];
@@ -145,7 +159,7 @@ __global__ void __launch_bounds__(kCountThreads) k_coarse_count(FrameBufs fb, Gr
 // 32 coarse bins per CTA (lanes), the groups split into 32 slices (warps): gtable becomes the
 // exclusive prefix over groups, cinfo[bin].y the bin's entry total. The last CTA to finish then
 // computes the coarse list starts and segments (coarse_ranges, below).
-__device__ void coarse_ranges(const FrameBufs& fb, const GridParams& gp, uint32_t ncoarse);
+__device__ void coarse_ranges(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint32_t ncoarse);
 
 __global__ void __launch_bounds__(1024) k_coarse_scan(FrameBufs fb, GridParams gp, PlaceGeom pg) {
     __shared__ uint32_t s_seg[32][33];
@@ -208,7 +222,7 @@ __global__ void __launch_bounds__(1024) k_coarse_scan(FrameBufs fb, GridParams g
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    coarse_ranges(fb, gp, pg.ncoarse);
+    coarse_ranges(fb, gp, pg, pg.ncoarse);
 }
 
 // Exclusive block scan of two counters per thread; returns the prefixes, adds the block totals
@@ -257,7 +271,7 @@ __device__ __forceinline__ uint2 block_scan2(uint32_t a, uint32_t b, uint32_t* s
 
 // K and the capacity check; list starts and segments of the coarse bins (entry totals in
 // cinfo[.].y, written by other CTAs of the same kernel or by an earlier one). One CTA.
-__device__ void coarse_ranges(const FrameBufs& fb, const GridParams& gp, uint32_t ncoarse) {
+__device__ void coarse_ranges(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint32_t ncoarse) {
     __shared__ uint32_t s_a[32], s_b[32];
     __shared__ uint32_t s_ok;
     FrameCtl* ctl = fb.ctl;
@@ -309,12 +323,25 @@ __device__ void coarse_ranges(const FrameBufs& fb, const GridParams& gp, uint32_
     if (tid == 0) {
         ctl->num_entries = (uint32_t)carry_e;
         ctl->num_segments = (uint32_t)carry_s;
+        // bands of the coarse placement: the widest the shared memory holds, or small ones when
+        // the (chunk, coarse bin) runs are long (their partly written sectors then stay in L2)
+        uint32_t rows = pg.band_rows, nb = pg.nbands;
+        const unsigned long long cells = (unsigned long long)pg.nchunks * (ncoarse > 0u ? ncoarse : 1u);
+        if (pg.ctx > 0u && carry_e >= (unsigned long long)kLongRun * cells) {
+            const uint32_t r = kLongRunBand / pg.ctx > 0u ? kLongRunBand / pg.ctx : 1u;
+            if (r < rows) {
+                rows = r;
+                nb = (pg.cty + rows - 1) / rows;
+            }
+        }
+        ctl->place_band_rows = rows;
+        ctl->place_nbands = nb;
     }
 }
 
 // Frames with nothing to bin: K, the flags and plan_ok.
-__global__ void __launch_bounds__(kRangesThreads) k_coarse_ranges(FrameBufs fb, GridParams gp) {
-    coarse_ranges(fb, gp, 0u);
+__global__ void __launch_bounds__(kRangesThreads) k_coarse_ranges(FrameBufs fb, GridParams gp, PlaceGeom pg) {
+    coarse_ranges(fb, gp, pg, 0u);
 }
 
 // Persistent: every warp takes (band, chunk) items from a ticket, band-major. For an item, the
@@ -338,17 +365,18 @@ __global__ void __launch_bounds__(kPlaceWarps * 32, kPlaceCtasPerSm) k_coarse_pl
     const unsigned long long* __restrict__ order = io_select(fb.gsort, cd->final_buf);
     const unsigned long long imask = (1ull << cd->idx_bits) - 1ull;
     uint2* __restrict__ out = fb.clist;
-    const uint32_t ctx = pg.ctx, items = pg.nbands * pg.nchunks;
+    const uint64_t nsorted = min((uint64_t)ctl->num_visible, n);  // Gaussians in the depth order
+    const uint32_t ctx = pg.ctx, band_rows = ctl->place_band_rows, items = ctl->place_nbands * pg.nchunks;
     for (;;) {
         uint32_t item = 0;
         if (lane == 0) item = atomicAdd(&ctl->scan_ticket, 1u);
         item = __shfl_sync(0xFFFFFFFFu, item, 0);
         if (item >= items) break;
         const uint32_t band = item / pg.nchunks, chunk = item - band * pg.nchunks;
-        const uint32_t cb0 = band * pg.band_rows, cb1 = min(cb0 + pg.band_rows, pg.cty);
+        const uint32_t cb0 = band * band_rows, cb1 = min(cb0 + band_rows, pg.cty);
         const uint32_t nb = (cb1 - cb0) * ctx, bin0 = cb0 * ctx;
         const uint64_t q0 = (uint64_t)chunk * pg.chunk_len;
-        const uint64_t q1 = min(q0 + (uint64_t)pg.chunk_len, n);
+        const uint64_t q1 = min(q0 + (uint64_t)pg.chunk_len, nsorted);
         const uint32_t* __restrict__ trow = fb.ctable + (uint64_t)chunk * pg.ncoarse + bin0;
         const uint32_t* __restrict__ grow = fb.gtable + (uint64_t)(chunk / pg.group) * pg.ncoarse + bin0;
         __syncwarp();  // the previous item is done with the cursors
@@ -662,7 +690,7 @@ cudaError_t place_geometry(const GridParams& gp, uint64_t n, uint64_t capacity, 
 cudaError_t launch_coarse_count(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
                                 cudaStream_t stream) {
     if (n == 0 || gp.row_end <= gp.row_begin) {  // nothing to bin: K, the flags and plan_ok
-        k_coarse_ranges<<<1, kRangesThreads, 0, stream>>>(fb, gp);
+        k_coarse_ranges<<<1, kRangesThreads, 0, stream>>>(fb, gp, pg);
         return cudaGetLastError();
     }
     k_coarse_count<<<pg.ngroups, kCountThreads, pg.count_smem, stream>>>(fb, gp, pg, n);

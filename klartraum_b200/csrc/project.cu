@@ -5,8 +5,10 @@
 // atomics). This file is compiled with -fmad=false and IEEE division / square root, so every
 // float result is the correctly rounded value of the shader's own operation sequence.
 //
-// Roofline: HBM bound. Per Gaussian it reads the scene planes (48 B geometry + 16 B per SH
-// float4 plane: 240 B at SH3) and writes 48 B record + 4 B count + 8 B rect + 4 B depth.
+// Roofline: HBM bound. Per Gaussian it reads the geometry planes (48 B) and, for a Gaussian that
+// meets a bin, its SH planes (16 B per float4 plane: 192 B at SH3); it writes 48 B record + 4 B
+// count + 8 B rect + 4 B depth. The colour of a Gaussian that meets no bin is stored as 0 (the
+// reference computes it but no later stage reads it).
 #include "kt_common.cuh"
 #include "kt_kernels.h"
 
@@ -161,15 +163,6 @@ __global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams
         const float4 P = __ldg(&sc.pos[i]);
         const float4 Q = __ldg(&sc.rot[i]);
         const float4 S = __ldg(&sc.scale[i]);
-        float f[4 * kPlanes];
-#pragma unroll
-        for (int p = 0; p < kPlanes; ++p) {
-            const float4 v = __ldg(&sc.sh[(uint64_t)p * sc.n + i]);
-            f[4 * p + 0] = v.x;
-            f[4 * p + 1] = v.y;
-            f[4 * p + 2] = v.z;
-            f[4 * p + 3] = v.w;
-        }
 
         // comp:198-203: clip position, pixel position, depth
         float pos[4];
@@ -238,7 +231,22 @@ __global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams
         float ci[4];
         mat2_inverse(cov, ci);
 
-        // comp:218-224: view direction and SH colour
+        uint2 rect;
+        count = bin_span(px, py, z, ci, gp, rect);
+        flip = __float_as_uint(z) ^ 0x80000000u;
+        // comp:218-224: view direction and SH colour, for Gaussians that meet a bin: no later
+        // stage reads the colour of the others (stored as 0), so their SH planes are not read
+        float rgb[3] = {0.0f, 0.0f, 0.0f};
+        if (count != 0u) {
+        float f[4 * kPlanes];
+#pragma unroll
+        for (int p = 0; p < kPlanes; ++p) {
+            const float4 v = __ldg(&sc.sh[(uint64_t)p * sc.n + i]);
+            f[4 * p + 0] = v.x;
+            f[4 * p + 1] = v.y;
+            f[4 * p + 2] = v.z;
+            f[4 * p + 3] = v.w;
+        }
         const float len = sqrtf(t4[0] * t4[0] + t4[1] * t4[1] + t4[2] * t4[2]);
         const float dx = t4[0] / len, dy = t4[1] / len, dz = t4[2] / len;
         float sh[16];
@@ -262,7 +270,6 @@ __global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams
             sh[14] = 1.445306f * zz * (x2 - y2);
             sh[15] = -0.590044f * x * (x2 - 3.0f * y2);
         }
-        float rgb[3];
 #pragma unroll
         for (int ch = 0; ch < 3; ++ch) {
             float value = 0.5f + f[ch] * sh[0];
@@ -270,10 +277,7 @@ __global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams
             for (int k = 1; k < kCoef; ++k) value += f[3 * k + ch] * sh[k];
             rgb[ch] = value;
         }
-
-        uint2 rect;
-        count = bin_span(px, py, z, ci, gp, rect);
-        flip = __float_as_uint(z) ^ 0x80000000u;
+        }
         store_outputs(i, px, py, z, ci, rgb[0], rgb[1], rgb[2], P.w, count, rect, fb);
     }
     reduce_depth(count, flip, fb.ctl);

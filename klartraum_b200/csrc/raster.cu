@@ -227,7 +227,28 @@ k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__
     if (px < gp.width && py1 < gp.height) write_pixel(img, gp, px, py1, p1);
 }
 
+// Every pixel of an RGBA8 image set to one colour, 16 bytes per store where the image allows.
+__global__ void __launch_bounds__(256) k_fill_image(uchar4* __restrict__ img, uint64_t n, uchar4 v) {
+    const uint32_t w = (uint32_t)v.x | (uint32_t)v.y << 8 | (uint32_t)v.z << 16 | (uint32_t)v.w << 24;
+    const uint4 q = make_uint4(w, w, w, w);
+    const uint64_t nq = ((reinterpret_cast<uintptr_t>(img) & 15u) == 0) ? n / 4 : 0;
+    uint4* __restrict__ img4 = reinterpret_cast<uint4*>(img);
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nq; i += stride) img4[i] = q;
+    for (uint64_t i = nq * 4 + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) img[i] = v;
+}
+
 }  // namespace
+
+cudaError_t launch_fill_image(uchar4* img, uint64_t pixels, uchar4 value, cudaStream_t stream) {
+    if (pixels == 0) return cudaSuccess;
+    uint64_t blocks = (pixels / 4 + 255) / 256;
+    const uint64_t cap = (uint64_t)device_sm_count() * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    k_fill_image<<<(unsigned)blocks, 256, 0, stream>>>(img, pixels, value);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_rasterize(const float4* rec, const SortIO& io, const uint2* ranges,
                              const FrameCtl* ctl, const GridParams& gp, uchar4* img,

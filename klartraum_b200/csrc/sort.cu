@@ -55,13 +55,14 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
 // part through whist only; rank[j] is the position among equal digits within the warp.
 template <int DBITS, bool PACKED>
 __device__ __forceinline__ void rank_warp(SortSmem<PACKED>& sm, int cur, uint32_t wpos, uint32_t valid_items,
-                                          uint32_t shift, uint32_t mask, uint32_t lane, uint32_t lt, uint16_t* whist,
-                                          uint16_t (&rank)[kSortItems]) {
+                                          bool drop, uint32_t shift, uint32_t mask, uint32_t lane, uint32_t lt,
+                                          uint16_t* whist, uint16_t (&rank)[kSortItems]) {
     const uint32_t kMask = mask & ((1u << DBITS) - 1u);  // the pass's digit bits
 #pragma unroll
     for (int j = 0; j < kSortItems; ++j) {
-        const bool valid = (uint32_t)j < valid_items;
-        const uint32_t d = (uint32_t)(sm.keys[cur][wpos + j * 32] >> shift) & kMask;
+        const unsigned long long key = sm.keys[cur][wpos + j * 32];
+        const bool valid = (uint32_t)j < valid_items && !(drop && key == kDropKey);
+        const uint32_t d = (uint32_t)(key >> shift) & kMask;
         uint32_t peers = __ballot_sync(0xFFFFFFFFu, valid);
 #pragma unroll
         for (int b = 0; b < DBITS; ++b) {
@@ -135,7 +136,8 @@ k_sort_pass(SortIO io, FrameCtl* ctl, unsigned long long* status, uint32_t pass,
     extern __shared__ __align__(128) unsigned char smem_raw[];
     SortSmem<PACKED>& sm = *reinterpret_cast<SortSmem<PACKED>*>(smem_raw);
 
-    const uint64_t K = ctl->num_keys;
+    const uint64_t K = ctl->pass_in[pass];  // elements read; a dropping pass writes fewer
+    const bool drop = PACKED && ctl->pass_drop[pass] != 0u;
     const uint32_t ntiles = (uint32_t)((K + kSortTile - 1) / kSortTile);
     const uint32_t shift = (PACKED ? ctl->idx_bits : 0u) + 8 * pass;
     const uint32_t mask = ctl->pass_mask[pass];
@@ -200,8 +202,11 @@ k_sort_pass(SortIO io, FrameCtl* ctl, unsigned long long* status, uint32_t pass,
         // ---- early counts: the tile's digit histogram, published before ranking so that later
         //      tiles' look-backs find it (and soon this tile's inclusive prefix) sooner
 #pragma unroll
-        for (int j = 0; j < kSortItems; ++j)
-            if ((uint32_t)j < valid_items) atomicAdd(&sm.tcount[(uint32_t)(sm.keys[cur][wpos + j * 32] >> shift) & mask], 1u);
+        for (int j = 0; j < kSortItems; ++j) {
+            const unsigned long long key = sm.keys[cur][wpos + j * 32];
+            if ((uint32_t)j < valid_items && !(drop && key == kDropKey))
+                atomicAdd(&sm.tcount[(uint32_t)(key >> shift) & mask], 1u);
+        }
         __syncthreads();
         const uint32_t cnt = sm.tcount[tid];
         unsigned long long* st = status + (uint64_t)tile * 256 + tid;
@@ -211,7 +216,7 @@ k_sort_pass(SortIO io, FrameCtl* ctl, unsigned long long* status, uint32_t pass,
         uint16_t rank[kSortItems];
         // one ranking routine for every digit width: fewer instantiations keep the kernel's code
         // in the instruction cache (narrow digits only have zero high bits)
-        rank_warp<8, PACKED>(sm, cur, wpos, valid_items, shift, mask, lane, lt, sm.whist[warp], rank);
+        rank_warp<8, PACKED>(sm, cur, wpos, valid_items, drop, shift, mask, lane, lt, sm.whist[warp], rank);
         __syncthreads();
 
         // ---- per digit (thread = digit): prefix over warps, then the look-back
@@ -265,7 +270,7 @@ k_sort_pass(SortIO io, FrameCtl* ctl, unsigned long long* status, uint32_t pass,
 #pragma unroll
         for (int j = 0; j < kSortItems; ++j) {
             const uint32_t p = wpos + j * 32;
-            if (tbase + p < K) {
+            if (tbase + p < K && !(drop && k[j] == kDropKey)) {
                 const uint32_t d = (uint32_t)(k[j] >> shift) & mask;
                 const uint32_t pos = sm.lstart[d] + sm.whist[warp][d] + rank[j];
                 sm.keys[cur][pos] = k[j];
@@ -274,8 +279,10 @@ k_sort_pass(SortIO io, FrameCtl* ctl, unsigned long long* status, uint32_t pass,
         }
         __syncthreads();
 
-        // ---- coalesced write-out
-        const uint32_t tn = (uint32_t)min((uint64_t)kSortTile, K - tbase);
+        // ---- coalesced write-out of the tile's kept elements
+        uint32_t tn = 0;
+#pragma unroll
+        for (int w = 0; w < kSortWarps; ++w) tn += sm.warp_tot[w];
         for (uint32_t i = tid; i < tn; i += kSortThreads) {
             const unsigned long long key = sm.keys[cur][i];
             const uint32_t d = (uint32_t)(key >> shift) & mask;
@@ -310,7 +317,7 @@ __global__ void __launch_bounds__(256) k_rts_upsweep(SortIO io, FrameCtl* ctl, u
 #pragma unroll
     for (int w = 0; w < 8; ++w) s_hist[w][tid] = 0u;
     __syncthreads();
-    const uint64_t K = ctl->num_keys;
+    const uint64_t K = ctl->pass_in[pass];
     const uint32_t ntiles = (uint32_t)((K + kSortTile - 1) / kSortTile);
     uint32_t t0, t1;
     rts_range(ntiles, t0, t1);
@@ -318,8 +325,11 @@ __global__ void __launch_bounds__(256) k_rts_upsweep(SortIO io, FrameCtl* ctl, u
     const uint32_t mask = ctl->pass_mask[pass];
     const unsigned long long* __restrict__ src = io_keys(io, ctl->pass_src[pass]);
     const uint64_t e0 = (uint64_t)t0 * kSortTile, e1 = min((uint64_t)t1 * kSortTile, K);
-    for (uint64_t i = e0 + tid; i < e1; i += 256)
-        atomicAdd(&s_hist[warp][(uint32_t)(__ldcs(src + i) >> shift) & mask], 1u);
+    const bool drop = PACKED && ctl->pass_drop[pass] != 0u;
+    for (uint64_t i = e0 + tid; i < e1; i += 256) {
+        const unsigned long long key = __ldcs(src + i);
+        if (!(drop && key == kDropKey)) atomicAdd(&s_hist[warp][(uint32_t)(key >> shift) & mask], 1u);
+    }
     __syncthreads();
     uint32_t sum = 0;
 #pragma unroll
@@ -365,7 +375,8 @@ k_rts_downsweep(SortIO io, FrameCtl* ctl, const uint32_t* __restrict__ tab, uint
     extern __shared__ __align__(128) unsigned char smem_raw[];
     SortSmem<PACKED>& sm = *reinterpret_cast<SortSmem<PACKED>*>(smem_raw);
 
-    const uint64_t K = ctl->num_keys;
+    const uint64_t K = ctl->pass_in[pass];  // elements read; a dropping pass writes fewer
+    const bool drop = PACKED && ctl->pass_drop[pass] != 0u;
     const uint32_t ntiles = (uint32_t)((K + kSortTile - 1) / kSortTile);
     uint32_t t0, t1;
     rts_range(ntiles, t0, t1);
@@ -425,7 +436,7 @@ k_rts_downsweep(SortIO io, FrameCtl* ctl, const uint32_t* __restrict__ tab, uint
         uint16_t rank[kSortItems];
         // one ranking routine for every digit width: fewer instantiations keep the kernel's code
         // in the instruction cache (narrow digits only have zero high bits)
-        rank_warp<8, PACKED>(sm, cur, wpos, valid_items, shift, mask, lane, lt, sm.whist[warp], rank);
+        rank_warp<8, PACKED>(sm, cur, wpos, valid_items, drop, shift, mask, lane, lt, sm.whist[warp], rank);
         __syncthreads();
 
         // per digit (thread = digit): prefix over warps, the tile's count, its global start
@@ -465,7 +476,7 @@ k_rts_downsweep(SortIO io, FrameCtl* ctl, const uint32_t* __restrict__ tab, uint
         __syncthreads();
 #pragma unroll
         for (int j = 0; j < kSortItems; ++j) {
-            if ((uint32_t)j < valid_items) {
+            if ((uint32_t)j < valid_items && !(drop && k[j] == kDropKey)) {
                 const uint32_t d = (uint32_t)(k[j] >> shift) & mask;
                 const uint32_t pos = sm.lstart[d] + sm.whist[warp][d] + rank[j];
                 sm.keys[cur][pos] = k[j];
@@ -474,8 +485,10 @@ k_rts_downsweep(SortIO io, FrameCtl* ctl, const uint32_t* __restrict__ tab, uint
         }
         __syncthreads();
 
-        // coalesced write-out
-        const uint32_t tn = (uint32_t)min((uint64_t)kSortTile, K - tbase);
+        // coalesced write-out of the tile's kept elements
+        uint32_t tn = 0;
+#pragma unroll
+        for (int w = 0; w < kSortWarps; ++w) tn += sm.warp_tot[w];
         for (uint32_t i = tid; i < tn; i += kSortThreads) {
             const unsigned long long key = sm.keys[cur][i];
             const uint32_t d = (uint32_t)(key >> shift) & mask;

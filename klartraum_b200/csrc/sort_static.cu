@@ -7,7 +7,7 @@
 // memory. They pass their inputs and outputs; the scratch (control block, the second key and
 // value buffers, look-back status words) lives in g_sort_scratch below.
 //
-// The array is KT_GS_STATIC_SORT_SCRATCH_BYTES (13,123,840 bytes, 12.5 MiB) and every device that
+// The array is KT_GS_STATIC_SORT_SCRATCH_BYTES (13,127,680 bytes, 12.52 MiB) and every device that
 // loads this module keeps it until the process exits. In host code the name g_sort_scratch is
 // only a host-side stand-in for the symbol, not a device address: every call looks the device
 // address up with cudaGetSymbolAddress on the current device (the first call on a device also
@@ -30,7 +30,8 @@ namespace kt {
 namespace {
 
 constexpr uint64_t kStaticMaxPairs = KT_GS_STATIC_SORT_MAX_PAIRS;
-constexpr size_t kCtlBytes = (sizeof(FrameCtl) + 255) & ~size_t(255);
+constexpr size_t kCtlBytes = 20480;  // control block region, fixed so the array's size is stable
+static_assert(sizeof(FrameCtl) <= kCtlBytes, "control block outgrew its region");
 constexpr size_t kKeyBytes = kStaticMaxPairs * 8;
 constexpr size_t kValBytes = kStaticMaxPairs * 4;
 constexpr size_t kStatusBytes = (kStaticMaxPairs / kSortTile) * 256 * 8;

@@ -51,6 +51,22 @@ def band_rows(tiles_y: int, world: int, weights=None) -> list[tuple[int, int]]:
     return [(cuts[k], cuts[k + 1]) for k in range(world)]
 
 
+def rebalance_bands(row_weights, bands: list[tuple[int, int]], band_ms) -> list[tuple[int, int]]:
+    """New cuts from the measured time of each band: the rows of band k are weighted by
+    band_ms[k] / (its summed row weight), i.e. by the measured cost per unit of weight of the rank
+    that drew them, and the rows are split again so that every band gets the same predicted
+    time. With per-row pair counts as weights this balances on time, not on pairs."""
+    w = np.asarray(row_weights, dtype=np.float64)
+    t = np.asarray(band_ms, dtype=np.float64)
+    if len(t) != len(bands):
+        raise ValueError("one time per band")
+    scale = np.ones_like(w)
+    for k, (y0, y1) in enumerate(bands):
+        total = w[y0:y1].sum()
+        scale[y0:y1] = t[k] / total if total > 0 else 0.0
+    return band_rows(len(w), len(bands), w * scale)
+
+
 def band_pixel_rows(band: tuple[int, int], bin_h: int, height: int) -> tuple[int, int]:
     """Pixel rows [r0, r1) covered by a band of bin rows."""
     y0, y1 = band

@@ -112,6 +112,18 @@ class Renderer:
         self._check(self._lib.kt_gs_render_host(self._ctx, cam.ctypes.data, N.as_ptr(image), path, stream or None))
         return image
 
+    def render_host_clear(self, cam: np.ndarray, image, clear=(0, 0, 0, 255), path: int = 0, stream: int = 0):
+        """Render into a host RGBA8 image with the device image first cleared to `clear` (the
+        render pass's clear colour) instead of copied in; returns the image."""
+        if isinstance(image, np.ndarray):
+            assert image.dtype == np.uint8 and image.flags.c_contiguous
+            assert image.size == self.width * self.height * 4
+        cam = self._cam(cam)
+        col = (C.c_uint8 * 4)(*[int(v) for v in clear])
+        self._check(self._lib.kt_gs_render_host_clear(self._ctx, cam.ctypes.data, col, N.as_ptr(image), path,
+                                                      stream or None))
+        return image
+
     def render_batch(self, cams: np.ndarray, images: list, stream: int = 0) -> None:
         cams = np.ascontiguousarray(cams, dtype=CAMERA_DTYPE)
         ptrs = (C.c_void_p * len(images))(*[N.as_ptr(i) for i in images])

@@ -81,7 +81,7 @@ def test_single_1m_every_stage_and_whole_image():
     cfg = oracle.config(w.width, w.height, bin_size=16, sh_degree=3)
     ref = oracle.render_frame(cfg, cam, g3d, bg)
     assert st["num_keys"] == ref["num_keys"]
-    compare_projected(r.dump(N.STAGE_PROJECTED), ref["g2d"])
+    compare_projected(r.dump(N.STAGE_PROJECTED), ref["g2d"], ref["counts"])
     assert np.array_equal(r.dump(N.STAGE_TILE_COUNTS), ref["counts"])
     assert np.array_equal(r.dump(N.STAGE_KEYS_SORTED), ref["keys"])
     assert np.array_equal(r.dump(N.STAGE_VALUES_SORTED), ref["vals"])
@@ -113,7 +113,7 @@ def test_multiview_3m_views(multiview_scene, view):
     cfg = oracle.config(w.width, w.height, bin_size=16, sh_degree=3)
     ref = oracle.render_frame(cfg, cam, g3d, bg)
     assert st["num_keys"] == ref["num_keys"] > 0
-    compare_projected(r.dump(N.STAGE_PROJECTED), ref["g2d"])
+    compare_projected(r.dump(N.STAGE_PROJECTED), ref["g2d"], ref["counts"])
     assert np.array_equal(r.dump(N.STAGE_TILE_COUNTS), ref["counts"])
     assert np.array_equal(r.dump(N.STAGE_VALUES_SORTED), ref["vals"])
     assert np.array_equal(r.dump(N.STAGE_KEYS_SORTED), ref["keys"])
@@ -140,8 +140,8 @@ def test_large_6m_whole_frame_band_by_band():
     out = img.cpu().numpy()
     cfg = oracle.config(w.width, w.height, bin_size=16, sh_degree=3)
     g2d = oracle.project(cfg, cam, g3d)
-    compare_projected(r.dump(N.STAGE_PROJECTED), g2d)
     counts = r.dump(N.STAGE_TILE_COUNTS)
+    compare_projected(r.dump(N.STAGE_PROJECTED), g2d, counts)
     assert np.array_equal(counts, oracle.tile_counts(cfg, g2d))
     assert int(counts.sum(dtype=np.uint64)) == st["num_keys"]
     ranges = r.dump(N.STAGE_TILE_RANGES)
@@ -177,8 +177,8 @@ def test_stress_2m_three_bands():
     out = img.cpu().numpy()
     cfg = oracle.config(w.width, w.height, bin_size=16, sh_degree=1)
     g2d = oracle.project(cfg, cam, g3d)
-    compare_projected(r.dump(N.STAGE_PROJECTED), g2d)
     counts = r.dump(N.STAGE_TILE_COUNTS)
+    compare_projected(r.dump(N.STAGE_PROJECTED), g2d, counts)
     assert np.array_equal(counts, oracle.tile_counts(cfg, g2d))
     assert int(counts.sum(dtype=np.uint64)) == st["num_keys"]
     ranges = r.dump(N.STAGE_TILE_RANGES)

@@ -75,7 +75,7 @@ def test_frame_parity(case, keys):
     st = r.stats()
     assert st["error_flags"] == 0
     assert st["num_keys"] == ref["num_keys"]
-    compare_projected(r.dump(N.STAGE_PROJECTED), ref["g2d"])
+    compare_projected(r.dump(N.STAGE_PROJECTED), ref["g2d"], ref["counts"])
     assert np.array_equal(r.dump(N.STAGE_TILE_COUNTS), ref["counts"])
     assert np.array_equal(r.dump(N.STAGE_OFFSETS), ref["offsets"])
     assert np.array_equal(r.dump(N.STAGE_KEYS_UNSORTED), ref["keys_unsorted"])
@@ -107,7 +107,7 @@ def test_projection_known_answer_on_gpu():
             else:
                 assert abs(p["position"][i, a] - exp[i, a]) <= k["tolerance"]
     cfg = oracle.config(512, 512, bin_size=128, sh_degree=1)
-    compare_projected(p, oracle.project(cfg, cam, g))
+    compare_projected(p, oracle.project(cfg, cam, g), r.dump(N.STAGE_TILE_COUNTS))
 
 
 def test_bin_known_answer_on_gpu():
@@ -352,3 +352,21 @@ def test_sorted_keys_path_draws_the_same_image(wname, n, wh):
     assert np.array_equal(imgs[0], imgs[1])
     for a, b in zip(keys[0], keys[1]):
         assert np.array_equal(a, b)
+
+
+def test_render_host_clear_equals_a_cleared_image():
+    """kt_gs_render_host_clear: the device image set to the clear colour, then the frame; the
+    same as kt_gs_render_host given an image of that colour, on both binning paths and a band."""
+    g3d = make_scene("plumbing", n=6000)
+    cam = workload_camera("plumbing")
+    for flags, rows in [(0, None), (N.FLAG_SORTED_KEYS, None), (0, (3, 9))]:
+        r = Renderer(256, 256, bin_size=16, sh_degree=0, flags=flags, tile_rows=rows)
+        r.set_gaussians(g3d)
+        for clear in [(0, 0, 0, 255), (10, 200, 30, 0)]:
+            host = np.full((256, 256, 4), 77, np.uint8)  # overwritten entirely
+            r.render_host_clear(cam, host, clear=clear)
+            expect = np.empty((256, 256, 4), np.uint8)
+            expect[:] = clear
+            r.render_host(cam, expect)
+            assert np.array_equal(host, expect)
+        r.close()

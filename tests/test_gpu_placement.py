@@ -5,9 +5,9 @@ then places the pairs by bin in two levels (klartraum_b200/csrc/place.cu). Its e
 pairs in bin order, is checked against the oracle in test_gpu_parity.py; this file checks the
 intermediate device buffers stage by stage, so that a fault in one level shows at that level:
 
-* DEPTH_ORDER   the depth sort's output: Gaussian indices stably sorted by
-                floatBitsToUint(z) ^ 0x80000000 (the depth digits of
-                shaders/gsplat/gsplat_radix_sort_include.glsl:51-63), Gaussians without bins last;
+* DEPTH_ORDER   the depth sort's output: the indices of the Gaussians that meet a bin, stably
+                sorted by floatBitsToUint(z) ^ 0x80000000 (the depth digits of
+                shaders/gsplat/gsplat_radix_sort_include.glsl:51-63);
 * COARSE_INFO   per coarse bin (4x4 bins): list start, entries, first segment;
 * COARSE_LISTS  per coarse bin, (Gaussian, mask of the 4x4 bins met) in depth order;
 * SEGMENT_COUNTS per 256-entry segment of a coarse list, the pairs of each of its 16 bins.
@@ -44,16 +44,12 @@ def placement_model(rects, depth_key, tx, rows):
     n = len(rects)
     rb, re = rows
     visible = (rects[:, 1] > rects[:, 0]) & (rects[:, 3] > rects[:, 2])
-    dk = np.zeros(n, np.int64)
-    if visible.any():
-        dmin, dmax = int(depth_key[visible].min()), int(depth_key[visible].max())
-        dk[visible] = depth_key[visible].astype(np.int64) - dmin
-        dk[~visible] = dmax - dmin
-    order = np.argsort(dk, kind="stable").astype(np.uint32)
+    vis_idx = np.nonzero(visible)[0]
+    order = vis_idx[np.argsort(depth_key[vis_idx], kind="stable")].astype(np.uint32)
 
     ctx, cty = (tx + 3) // 4, (re - rb + 3) // 4
     ncoarse = ctx * cty
-    q = order[visible[order]]
+    q = order
     x0, x1 = rects[q, 0].astype(np.int64), rects[q, 1].astype(np.int64)
     y0, y1 = rects[q, 2].astype(np.int64) - rb, rects[q, 3].astype(np.int64) - rb
     cx0, cx1 = x0 // 4, (x1 + 3) // 4
@@ -99,7 +95,8 @@ CASES = [
     ("plumbing", None, (256, 256), (5, 11)),     # a band of bin rows: ragged coarse rows
     ("plumbing", 5000, (200, 120), None),        # ragged coarse columns
     ("single_1m", 150000, (3840, 2160), None),   # 60 x 34 coarse bins: two placement bands
-    ("stress_2m", 8000, (1280, 720), None),      # large Gaussians: long coarse lists, many segments
+    ("stress_2m", 8000, (1280, 720), None),      # large Gaussians: long coarse lists
+    ("stress_2m", 200000, (640, 360), None),     # 60 coarse lists of ~60 segments: long runs, small bands
 ]
 
 

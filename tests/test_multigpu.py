@@ -54,6 +54,29 @@ def test_band_rows_balance_weights():
     assert eq == [(0, 34), (34, 68)]
 
 
+def test_rebalance_bands_follows_measured_time():
+    """Bands balanced on pairs, but the pairs of the top half cost three times as much (say,
+    larger Gaussians there): after one rebalance on the measured times each band's predicted
+    time is about equal, and a second rebalance with times that match the prediction keeps it."""
+    from klartraum_b200.multigpu import rebalance_bands
+
+    ty, world = 120, 4
+    pairs = np.full(ty, 100.0)
+    cost = np.r_[np.full(60, 3.0), np.full(60, 1.0)]  # time per pair, unknown to the splitter
+    bands = band_rows(ty, world, pairs)
+    times = [float((pairs * cost)[a:b].sum()) for a, b in bands]
+    assert max(times) / min(times) > 2.0
+    new = rebalance_bands(pairs, bands, times)
+    t2 = [float((pairs * cost)[a:b].sum()) for a, b in new]
+    assert max(t2) / min(t2) < 1.15
+    assert new[0][0] == 0 and new[-1][1] == ty and all(a1 == b0 for (_, a1), (b0, _) in zip(new, new[1:]))
+    again = rebalance_bands(pairs, new, t2)
+    t3 = [float((pairs * cost)[a:b].sum()) for a, b in again]
+    assert max(t3) / min(t3) < 1.15
+    with pytest.raises(ValueError):
+        rebalance_bands(pairs, bands, times[:2])
+
+
 def test_band_pixel_rows_clip_last_band():
     assert band_pixel_rows((0, 34), 16, 1080) == (0, 544)
     assert band_pixel_rows((34, 68), 16, 1080) == (544, 1080)
