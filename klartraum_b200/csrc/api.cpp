@@ -59,9 +59,12 @@ struct GraphKey {
     int src = 0;
     uint64_t scene_gen = 0;
     uint64_t buf_gen = 0;
+    bool skip_sh = false;
+    bool place_runs = false;
     bool operator==(const GraphKey& o) const {
         return img == o.img && n == o.n && cap == o.cap && flags == o.flags && src == o.src &&
-               scene_gen == o.scene_gen && buf_gen == o.buf_gen;
+               scene_gen == o.scene_gen && buf_gen == o.buf_gen && skip_sh == o.skip_sh &&
+               place_runs == o.place_runs;
     }
 };
 
@@ -127,6 +130,11 @@ struct PathWs {
     bool have_frame = false;
     uint64_t frame_n = 0;
     uint32_t last_ncoarse = 0;  // coarse bins of the last frame's pair placement
+    // K1 reads SH planes only for binned Gaussians while few Gaussians meet a bin (from the
+    // visible fraction of the path's last completed frame, with hysteresis)
+    bool skip_sh = false;
+    // pair placement by runs of segments while the path's frames have many segments per warp
+    bool place_runs = false;
     // device image for kt_gs_render_host
     uchar4* img = nullptr;
     // device copy of caller-supplied projected records
@@ -409,12 +417,39 @@ struct FramePlan {
     uint32_t scan_epoch = 1;    // keys path: scan
     uint32_t key_epoch0 = 1;    // keys path: sort passes
     bool clear_status = false;  // graph replays clear the look-back words at the frame's start
+    bool skip_sh = false;       // K1 variant: SH planes read only for Gaussians that meet a bin
+    bool place_runs = false;    // pair placement by runs of segments (k_fine_place_runs)
 };
 
+// The K1 variant for the next frame of a path: reading a Gaussian's SH planes only after its bin
+// count is known saves their bytes for the Gaussians that meet no bin but adds a dependent load,
+// which costs more than it saves when most Gaussians are visible. Decided from the visible fraction
+// of the path's last completed frame (its control block copy), switching below 70 % and back above
+// 80 %.
+bool choose_skip_sh(const PathWs& w) {
+    if (!w.have_frame || w.frame_n == 0 || !w.host_ctl) return w.skip_sh;
+    const double frac = (double)w.host_ctl->num_visible / (double)w.frame_n;
+    if (w.skip_sh) return frac < 0.80;
+    return frac < 0.70;
+}
+
 // Allocations and look-back epochs of a frame. Never called inside a stream capture.
+// The pair-placement kernel for the next frame of a path: a warp per segment while the segments
+// are at most a few per warp (few registers, full occupancy), runs of segments with the next one
+// prefetched when each warp would take many (long coarse lists). From the segment count of the
+// path's last completed frame, switching above 6 and back below 4 segments per warp.
+bool choose_place_runs(const PathWs& w, const PlaceGeom& pg) {
+    if (!w.have_frame || !w.host_ctl || w.keys_frame) return w.place_runs;
+    const double per_warp = (double)w.host_ctl->num_segments / (double)std::max<uint32_t>(1u, fine_place_warps(pg));
+    if (w.place_runs) return per_warp > 4.0;
+    return per_warp > 6.0;
+}
+
 kt_status prepare_frame(kt_gs_ctx* c, PathWs& w, uint64_t n, bool graph, FramePlan& fp, cudaStream_t stream) {
     fp.keys = (c->cfg.flags & KT_GS_FLAG_SORTED_KEYS) != 0;
     fp.clear_status = graph;
+    w.skip_sh = choose_skip_sh(w);
+    fp.skip_sh = w.skip_sh;
     if (fp.keys) {
         kt_status st = ensure_keys(c, w, std::max<uint64_t>(n, 1));
         if (st != KT_OK) return st;
@@ -437,6 +472,8 @@ kt_status prepare_frame(kt_gs_ctx* c, PathWs& w, uint64_t n, bool graph, FramePl
         return KT_OK;
     }
     KT_TRY_CUDA(c, place_geometry(c->gp, n, w.cap, &fp.pg));
+    w.place_runs = choose_place_runs(w, fp.pg);
+    fp.place_runs = w.place_runs;
     if (fp.pg.table_words > w.ctable_words) {
         dfree(w.ctable);
         w.ctable_words = 0;
@@ -513,7 +550,7 @@ kt_status record_frame(kt_gs_ctx* c, PathWs& w, Source src, uint64_t n, const Ca
     if (src == Source::Scene) {
         SceneDev sc{c->pos, c->rot, c->scale, c->sh, c->nplanes, c->deg, c->n};
         const CamParams none{};
-        KT_TRY_CUDA(c, launch_project_count(sc, cam ? *cam : none, cam_dev, c->gp, fb, stream));
+        KT_TRY_CUDA(c, launch_project_count(sc, cam ? *cam : none, cam_dev, c->gp, fb, fp.skip_sh, stream));
     } else {
         KT_TRY_CUDA(c, launch_load_projected(w.g2d, n, c->gp, fb, stream));
     }
@@ -553,7 +590,7 @@ kt_status record_frame(kt_gs_ctx* c, PathWs& w, Source src, uint64_t n, const Ca
         KT_TRY_CUDA(c, launch_coarse_place(fb, c->gp, fp.pg, n, stream));
         if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[4], stream));
         // bin counts and ranges; every pair at its place in bin order (depth order within a bin)
-        KT_TRY_CUDA(c, launch_fine_place(fb, c->gp, fp.pg, n, stream));
+        KT_TRY_CUDA(c, launch_fine_place(fb, c->gp, fp.pg, n, fp.place_runs, stream));
     }
     KT_TRY_CUDA(c, launch_frame_totals(w.ctl, w.ctl_depth, w.totals, stream));
     if (timed) KT_TRY_CUDA(c, cudaEventRecord(ev[5], stream));
@@ -607,7 +644,8 @@ kt_status enqueue_graph_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamPara
     if (!w.cam_dev) KT_TRY_CUDA(c, cudaMalloc(&w.cam_dev, sizeof(CamParams)));
     if (!w.cap_stream) KT_TRY_CUDA(c, cudaStreamCreateWithFlags(&w.cap_stream, cudaStreamNonBlocking));
     const uint32_t kFlagsBaked = ~(KT_GS_FLAG_ASYNC | KT_GS_FLAG_TIMING | KT_GS_FLAG_NO_AUTOGROW);
-    const GraphKey key{img, n, w.cap, c->cfg.flags & kFlagsBaked, (int)src, c->scene_gen, w.buf_gen};
+    const GraphKey key{img, n,         w.cap,      c->cfg.flags & kFlagsBaked, (int)src, c->scene_gen, w.buf_gen,
+                       fp.skip_sh, fp.place_runs};
     if (!w.gexec || !(key == w.gkey)) {
         if (w.gexec) cudaGraphExecDestroy(w.gexec);
         w.gexec = nullptr;

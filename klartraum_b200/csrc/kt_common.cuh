@@ -133,7 +133,8 @@ struct PlaceGeom {
     uint32_t place_ctas;      // persistent coarse-placement CTAs
     uint32_t band_bins;       // coarse bins of the largest placement band (cursor stride)
     uint32_t place_smem;      // dynamic shared memory of a coarse-placement CTA
-    uint32_t seg_ctas;        // CTAs of the pair placement
+    uint32_t seg_ctas;        // CTAs of the pair placement (a warp per segment)
+    uint32_t run_ctas;        // CTAs of the pair placement by runs of segments
     uint32_t count_ctas;      // CTAs of the bin count
     uint64_t table_words;     // u32 words of table[chunk][coarse bin]
     uint64_t gtable_words;    // u32 words of gtable[group][coarse bin]
@@ -154,7 +155,7 @@ struct FrameBufs {
     uint4* cinfo;                  // per coarse bin: list start, entries, first segment, 0
     uint2* clist;                  // (Gaussian index, 4x4 bin mask) by coarse bin, depth order
     uint32_t* seg_coarse;          // coarse bin of every segment
-    uint32_t* seg_cnt;             // pairs per (segment, bin of the 4x4), then their prefix
+    uint32_t* seg_cnt;             // pairs per (segment, bin of the 4x4)
     // reference-structured path (KT_GS_FLAG_SORTED_KEYS): offsets, keys and values
     unsigned long long* offsets;   // exclusive scan of the counts, index order
     unsigned long long* keys[2];   // bin << depth_bits | (depth - depth_min), ping-pong

@@ -29,8 +29,10 @@ constexpr int kScanChunk = 2048;  // Gaussians per scan/emit CTA (keys path)
 
 // project.cu (compiled with -fmad=false)
 // cam_dev: when not null the kernel reads the camera from device memory (graph replays)
+// skip_unbinned_sh: read the SH planes only for Gaussians that meet a bin
 cudaError_t launch_project_count(const SceneDev& sc, const CamParams& cam, const CamParams* cam_dev,
-                                 const GridParams& gp, const FrameBufs& fb, cudaStream_t stream);
+                                 const GridParams& gp, const FrameBufs& fb, bool skip_unbinned_sh,
+                                 cudaStream_t stream);
 cudaError_t launch_load_projected(const float* d_g2d, uint64_t n, const GridParams& gp,
                                   const FrameBufs& fb, cudaStream_t stream);
 cudaError_t launch_pack_scene(const float* d_aos, uint64_t n, float4* pos, float4* rot,
@@ -57,9 +59,11 @@ cudaError_t launch_coarse_count(const FrameBufs& fb, const GridParams& gp, const
 // every (Gaussian, coarse bin) entry at its place in its coarse list
 cudaError_t launch_coarse_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
                                 cudaStream_t stream);
-// bin counts, bin ranges, and every pair at its place in bin order
+// bin counts, bin ranges, and every pair at its place in bin order; runs: a warp per run of
+// consecutive segments with the next one prefetched (frames with many segments per warp)
 cudaError_t launch_fine_place(const FrameBufs& fb, const GridParams& gp, const PlaceGeom& pg, uint64_t n,
-                              cudaStream_t stream);
+                              bool runs, cudaStream_t stream);
+uint32_t fine_place_warps(const PlaceGeom& pg);  // warps of the per-segment pair placement
 
 // keys.cu: the reference-structured path (scan, key emission, boundary search)
 cudaError_t launch_key_scan_emit(const FrameBufs& fb, const GridParams& gp, uint64_t n, uint32_t epoch,

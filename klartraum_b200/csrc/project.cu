@@ -150,7 +150,10 @@ __device__ __forceinline__ void store_outputs(uint64_t i, float px, float py, fl
 
 // DEV_CAM: the camera comes from device memory (a captured frame graph replayed with new cameras)
 // instead of the kernel parameters.
-template <int DEG, bool DEV_CAM>
+// SKIP_SH: read a Gaussian's SH planes only once it is known to meet a bin (saves their bytes when
+// many Gaussians meet none, at the price of a second dependent load); otherwise every plane is
+// loaded up front with the geometry. Either way a Gaussian that meets no bin stores colour 0.
+template <int DEG, bool DEV_CAM, bool SKIP_SH>
 __global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams cam_arg, const CamParams* cam_dev,
                                                         GridParams gp, FrameBufs fb) {
     const CamParams& cam = DEV_CAM ? *cam_dev : cam_arg;
@@ -163,6 +166,17 @@ __global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams
         const float4 P = __ldg(&sc.pos[i]);
         const float4 Q = __ldg(&sc.rot[i]);
         const float4 S = __ldg(&sc.scale[i]);
+        float f[4 * kPlanes];
+        if (!SKIP_SH) {
+#pragma unroll
+            for (int p = 0; p < kPlanes; ++p) {
+                const float4 v = __ldg(&sc.sh[(uint64_t)p * sc.n + i]);
+                f[4 * p + 0] = v.x;
+                f[4 * p + 1] = v.y;
+                f[4 * p + 2] = v.z;
+                f[4 * p + 3] = v.w;
+            }
+        }
 
         // comp:198-203: clip position, pixel position, depth
         float pos[4];
@@ -235,17 +249,18 @@ __global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams
         count = bin_span(px, py, z, ci, gp, rect);
         flip = __float_as_uint(z) ^ 0x80000000u;
         // comp:218-224: view direction and SH colour, for Gaussians that meet a bin: no later
-        // stage reads the colour of the others (stored as 0), so their SH planes are not read
+        // stage reads the colour of the others (stored as 0)
         float rgb[3] = {0.0f, 0.0f, 0.0f};
         if (count != 0u) {
-        float f[4 * kPlanes];
+        if (SKIP_SH) {
 #pragma unroll
-        for (int p = 0; p < kPlanes; ++p) {
-            const float4 v = __ldg(&sc.sh[(uint64_t)p * sc.n + i]);
-            f[4 * p + 0] = v.x;
-            f[4 * p + 1] = v.y;
-            f[4 * p + 2] = v.z;
-            f[4 * p + 3] = v.w;
+            for (int p = 0; p < kPlanes; ++p) {
+                const float4 v = __ldg(&sc.sh[(uint64_t)p * sc.n + i]);
+                f[4 * p + 0] = v.x;
+                f[4 * p + 1] = v.y;
+                f[4 * p + 2] = v.z;
+                f[4 * p + 3] = v.w;
+            }
         }
         const float len = sqrtf(t4[0] * t4[0] + t4[1] * t4[1] + t4[2] * t4[2]);
         const float dx = t4[0] / len, dy = t4[1] / len, dz = t4[2] / len;
@@ -328,24 +343,28 @@ __global__ void __launch_bounds__(256) k_pack_scene(const float* __restrict__ ao
 
 // ------------------------------------------------------------------ launchers
 
+template <bool DEV_CAM, bool SKIP>
+static void launch_k1(const SceneDev& sc, const CamParams& cam, const CamParams* cam_dev, const GridParams& gp,
+                      const FrameBufs& fb, dim3 grid, cudaStream_t stream) {
+    switch (sc.deg) {
+        case 0: k_project_count<0, DEV_CAM, SKIP><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
+        case 1: k_project_count<1, DEV_CAM, SKIP><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
+        case 2: k_project_count<2, DEV_CAM, SKIP><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
+        default: k_project_count<3, DEV_CAM, SKIP><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
+    }
+}
+
 cudaError_t launch_project_count(const SceneDev& sc, const CamParams& cam, const CamParams* cam_dev,
-                                 const GridParams& gp, const FrameBufs& fb, cudaStream_t stream) {
+                                 const GridParams& gp, const FrameBufs& fb, bool skip_unbinned_sh,
+                                 cudaStream_t stream) {
     if (sc.n == 0) return cudaSuccess;
     const dim3 grid((unsigned)((sc.n + 255) / 256));
     if (cam_dev) {
-        switch (sc.deg) {
-            case 0: k_project_count<0, true><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
-            case 1: k_project_count<1, true><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
-            case 2: k_project_count<2, true><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
-            default: k_project_count<3, true><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
-        }
+        if (skip_unbinned_sh) launch_k1<true, true>(sc, cam, cam_dev, gp, fb, grid, stream);
+        else launch_k1<true, false>(sc, cam, cam_dev, gp, fb, grid, stream);
     } else {
-        switch (sc.deg) {
-            case 0: k_project_count<0, false><<<grid, 256, 0, stream>>>(sc, cam, nullptr, gp, fb); break;
-            case 1: k_project_count<1, false><<<grid, 256, 0, stream>>>(sc, cam, nullptr, gp, fb); break;
-            case 2: k_project_count<2, false><<<grid, 256, 0, stream>>>(sc, cam, nullptr, gp, fb); break;
-            default: k_project_count<3, false><<<grid, 256, 0, stream>>>(sc, cam, nullptr, gp, fb); break;
-        }
+        if (skip_unbinned_sh) launch_k1<false, true>(sc, cam, nullptr, gp, fb, grid, stream);
+        else launch_k1<false, false>(sc, cam, nullptr, gp, fb, grid, stream);
     }
     return cudaGetLastError();
 }
