@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define KT_GS_ABI_VERSION 2
+#define KT_GS_ABI_VERSION 3
 
 typedef enum kt_status {
     KT_OK = 0,
@@ -144,6 +144,9 @@ typedef struct kt_gs_stats {
     uint32_t idx_bits;       /* index bits of a packed element */
     uint32_t place_chunks;   /* chunks of depth order the pair placement split the Gaussians into */
     uint32_t place_bands;    /* bands of coarse-bin rows (4x4 bins each) of the pair placement */
+    uint32_t place_runs;     /* 1: pairs placed by runs of segments (long coarse lists), 0: a warp
+                                per segment */
+    uint32_t sh_after_count; /* 1: the projection read SH planes only for Gaussians that meet a bin */
 } kt_gs_stats;
 
 /* Totals accumulated on the device over every frame rendered on a path since the last

@@ -91,6 +91,7 @@ class Stats(C.Structure):
         ("status_bytes", C.c_uint32), ("launches", C.c_uint32),
         ("packed", C.c_uint32), ("idx_bits", C.c_uint32),
         ("place_chunks", C.c_uint32), ("place_bands", C.c_uint32),
+        ("place_runs", C.c_uint32), ("sh_after_count", C.c_uint32),
     ]
 
     def as_dict(self) -> dict:
@@ -106,7 +107,7 @@ class Counters(C.Structure):
 
 
 assert C.sizeof(Config) == 48
-assert C.sizeof(Stats) == 88
+assert C.sizeof(Stats) == 96
 assert C.sizeof(Counters) == 48
 
 _lib = None

@@ -1173,6 +1173,8 @@ kt_status kt_gs_frame_stats(kt_gs_ctx* c, uint32_t path, kt_gs_stats* out) {
         out->place_chunks = pg.nchunks;
         out->place_bands = h.place_nbands ? h.place_nbands : pg.nbands;  // the device's choice for the frame
     }
+    out->place_runs = (!w.keys_frame && w.place_runs) ? 1u : 0u;
+    out->sh_after_count = w.skip_sh ? 1u : 0u;
     return KT_OK;
 }
 

@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_status_strings():
     lib = N.load()
-    assert lib.kt_gs_abi_version() == 2
+    assert lib.kt_gs_abi_version() == 3
     for code, name in N.STATUS_NAMES.items():
         assert lib.kt_gs_status_string(code).decode() == name
 
@@ -52,7 +52,7 @@ def test_record_sizes_match_header():
     assert GAUSSIAN3D_DTYPE.itemsize == 236
     assert GAUSSIAN2D_DTYPE.itemsize == 48
     assert CAMERA_DTYPE.itemsize == 192
-    assert C.sizeof(N.Config) == 48 and C.sizeof(N.Stats) == 88
+    assert C.sizeof(N.Config) == 48 and C.sizeof(N.Stats) == 96
 
 
 def test_invalid_configs_are_rejected_before_touching_a_device():

@@ -152,25 +152,25 @@ def test_placement_dumps_are_refused_on_the_keys_path():
 def test_both_pair_placement_kernels_match_the_oracle():
     """The first frame of a path places pairs with a warp per segment; when the path's last frame
     had many segments per warp (here ~70k segments for ~9.5k warps), the next frames take runs of
-    segments with the next one prefetched, starting from per-list prefixes (one more launch). Both
-    must give the oracle's sorted pairs, ranges and image."""
+    segments with the next one prefetched (kt_gs_stats.place_runs). Both must give the oracle's
+    sorted pairs, ranges and image."""
     w = WORKLOADS["stress_2m"]
     g3d = make_scene(w, n=150000)
     cam = orbit_camera(w.distance, w.width, w.height, fovy_deg=60.0, up="y")
     cfg = oracle.config(w.width, w.height, bin_size=16, sh_degree=1)
     ref = oracle.render_frame(cfg, cam, g3d, background(w.height, w.width))
-    r = Renderer(w.width, w.height, bin_size=16, sh_degree=1)
+    r = Renderer(w.width, w.height, bin_size=16, sh_degree=1, key_capacity=ref["num_keys"] + 4096)
     r.set_gaussians(g3d)
-    launches = []
+    runs = []
     for frame in range(3):
         img = torch.from_numpy(background(w.height, w.width)).cuda()
         r.render(cam, img)
         st = r.stats()
-        launches.append(st["launches"])
+        runs.append(st["place_runs"])
         assert st["num_keys"] == ref["num_keys"]
         assert np.array_equal(r.dump(N.STAGE_VALUES_SORTED), ref["vals"]), f"frame {frame}"
         assert np.array_equal(r.dump(N.STAGE_TILE_RANGES), ref["ranges"]), f"frame {frame}"
         assert np.abs(img.cpu().numpy().astype(int) - ref["image"].astype(int)).max() <= 1
     assert len(r.dump(N.STAGE_SEGMENT_COUNTS)) > 60000
-    assert launches[1] == launches[2] == launches[0] + 1, launches  # the segment-prefix launch
+    assert runs == [0, 1, 1], runs
     r.close()
