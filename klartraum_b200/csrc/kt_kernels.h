@@ -24,7 +24,10 @@ __device__ __forceinline__ const unsigned long long* io_select(unsigned long lon
     return i == 0 ? b[0] : b[1];
 }
 
-constexpr int kSortTile = 4096;   // keys per sort tile
+#ifndef KT_SORT_TILE
+#define KT_SORT_TILE 4096
+#endif
+constexpr int kSortTile = KT_SORT_TILE;  // keys per sort tile
 constexpr int kScanChunk = 2048;  // Gaussians per scan/emit CTA (keys path)
 
 // project.cu (compiled with -fmad=false)
@@ -94,8 +97,12 @@ uint32_t sort_pass_launches(uint64_t max_keys, bool packed);  // kernels one pas
 // raster.cu
 // every pixel of an RGBA8 image set to `value` (the render pass's clear before the splatting)
 cudaError_t launch_fill_image(uchar4* img, uint64_t pixels, uchar4 value, cudaStream_t stream);
+// 16-pixel rows of blocks of the rasterised band, and the rasteriser over block rows
+// [first_block_row, first_block_row + block_rows) of it (all of them by default)
+uint32_t raster_block_rows(const GridParams& gp);
 cudaError_t launch_rasterize(const float4* rec, const SortIO& io, const uint2* ranges,
                              const FrameCtl* ctl, const GridParams& gp, uchar4* img,
-                             bool per_element_exit, cudaStream_t stream);
+                             bool per_element_exit, cudaStream_t stream, uint32_t first_block_row = 0,
+                             uint32_t block_rows = 0xFFFFFFFFu);
 
 }  // namespace kt

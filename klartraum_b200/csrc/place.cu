@@ -697,7 +697,11 @@ __global__ void __launch_bounds__(kSegWarps * 32) k_fine_place(FrameBufs fb, Gri
 // earlier segments is taken once per run). About 100 registers (two CTAs per SM); measured on the
 // 2M stress frame against precomputed per-list prefixes, longer runs and a 128-register build: this
 // one is the fastest (3.9 against 4.7-4.9 ms for the stage).
-__global__ void __launch_bounds__(kSegWarps * 32, 1) k_fine_place_runs(FrameBufs fb, GridParams gp, PlaceGeom pg) {
+#ifndef KT_FINE_RUNS_MIN_CTAS
+#define KT_FINE_RUNS_MIN_CTAS 1
+#endif
+__global__ void __launch_bounds__(kSegWarps * 32, KT_FINE_RUNS_MIN_CTAS) k_fine_place_runs(FrameBufs fb, GridParams gp,
+                                                                                         PlaceGeom pg) {
     const FrameCtl* ctl = fb.ctl;
     if (!ctl->plan_ok) return;
     const uint32_t ns = ctl->num_segments;

@@ -250,14 +250,22 @@ cudaError_t launch_fill_image(uchar4* img, uint64_t pixels, uchar4 value, cudaSt
     return cudaGetLastError();
 }
 
-cudaError_t launch_rasterize(const float4* rec, const SortIO& io, const uint2* ranges,
-                             const FrameCtl* ctl, const GridParams& gp, uchar4* img,
-                             bool per_element_exit, cudaStream_t stream) {
+uint32_t raster_block_rows(const GridParams& gp) {
     const uint32_t y0 = gp.row_begin * gp.bin_h;
     uint32_t y1 = gp.row_end * gp.bin_h;
     if (y1 > gp.height) y1 = gp.height;
-    if (y1 <= y0) return cudaSuccess;
-    const dim3 grid((gp.width + 15) / 16, (y1 - y0 + 15) / 16);
+    return y1 > y0 ? (y1 - y0 + 15) / 16 : 0u;
+}
+
+cudaError_t launch_rasterize(const float4* rec, const SortIO& io, const uint2* ranges,
+                             const FrameCtl* ctl, const GridParams& gp, uchar4* img,
+                             bool per_element_exit, cudaStream_t stream, uint32_t first_block_row,
+                             uint32_t block_rows) {
+    const uint32_t total = raster_block_rows(gp);
+    if (first_block_row >= total) return cudaSuccess;
+    const uint32_t rows = block_rows < total - first_block_row ? block_rows : total - first_block_row;
+    const uint32_t y0 = gp.row_begin * gp.bin_h + 16u * first_block_row;
+    const dim3 grid((gp.width + 15) / 16, rows);
     if (per_element_exit)
         k_rasterize<true><<<grid, kRasterThreads, 0, stream>>>(rec, io, ranges, ctl, gp, img, y0);
     else
