@@ -83,6 +83,9 @@ def parse():
                         "pairs, boundary search) instead of placing the pairs in bin order")
     p.add_argument("--workload", default=None, help="scene of scenes.WORKLOADS (default: single_1m for views, "
                                                     "large_6m for bands)")
+    p.add_argument("--n", type=int, default=None,
+                   help="Gaussians drawn from the workload's distributions instead of its full count (reduced cases "
+                        "for profiler captures)")
     return p.parse_args()
 
 
@@ -228,9 +231,11 @@ def stage_report(w, cnt, st, stage_ms, timed_frames, nplanes, stage_names=None):
     # bytes the placement writes: 8 per (Gaussian, coarse bin) entry, 4 per pair
     placed = cnt["sort_bytes"] / nf
     entries = max(placed - 4 * K_avg, 0.0) / 8
+    vis_avg = cnt["visible"] / nf
     per_frame_bytes = {
-        # scene planes read; record 48 + count 4 + rect 8 + depth 4 written
-        "project_count": w.n * (16 * (3 + nplanes) + 64),
+        # geometry planes read, SH planes read (for every Gaussian, or with the SH-after-count variant
+        # only for those that meet a bin); record 48 + count 4 + rect 8 + depth 4 written
+        "project_count": w.n * (16 * 3 + 64) + 16 * nplanes * (vis_avg if st.get("sh_after_count") else w.n),
         # depth keys (counts + depths read, 8-B keys written) and the depth sort passes (16 B per
         # Gaussian per pass)
         "depth_sort": w.n * (4 + 4 + 8) + cnt["depth_sort_bytes"] / nf,
@@ -842,6 +847,8 @@ def main():
     from klartraum_b200.scenes import WORKLOADS
 
     w = WORKLOADS[args.workload or (WORKLOAD if args.mode == "views" else "large_6m")]
+    if args.n is not None:
+        w = type(w)(**{**w.__dict__, "n": args.n})
     cfg_block = workload_config(w)
     cfg_block["binning"] = "sorted_keys" if args.sorted_keys else "placed"
     cfg_block["launch"] = "cuda_graph" if (args.launch == 'graph') else "stream"
