@@ -293,7 +293,13 @@ __global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams
             rgb[ch] = value;
         }
         }
-        store_outputs(i, px, py, z, ci, rgb[0], rgb[1], rgb[2], P.w, count, rect, fb);
+        // A rank that draws a band of bin rows culls to it: a Gaussian that meets none of the band's
+        // bins stores only its zero count (no later stage reads its record, rectangle or depth). The
+        // full frame keeps every record, so the projection stage dumps whole.
+        if (count != 0u || !gp.banded)
+            store_outputs(i, px, py, z, ci, rgb[0], rgb[1], rgb[2], P.w, count, rect, fb);
+        else
+            fb.counts[i] = 0u;
     }
     reduce_depth(count, flip, fb.ctl);
 }
