@@ -175,8 +175,7 @@ typedef struct kt_gs_counters {
 typedef enum kt_gs_stage {
     KT_GS_STAGE_PROJECTED = 0,       /* kt_gaussian2d[N], binMask = 0xFFFFFFFF as projected
                                         (gsplat_projection.comp:228); the colour of a Gaussian that
-                                        meets no bin is 0; with a band of bin rows (tile_row_begin/end)
-                                        only the records of Gaussians that meet the band are written */
+                                        meets no bin is 0 (no later stage reads it) */
     KT_GS_STAGE_TILE_COUNTS = 1,     /* uint32[N] bins overlapped by each Gaussian (0 if culled) */
     KT_GS_STAGE_OFFSETS = 2,         /* uint64[N] exclusive scan of the tile counts in Gaussian index
                                         order (default path: host-rebuilt from the counts) */

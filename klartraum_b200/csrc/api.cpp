@@ -219,7 +219,6 @@ GridParams make_grid(const kt_gs_config& c) {
     g.tiles_y = (c.height + c.bin_height - 1) / c.bin_height;
     g.row_end = c.tile_row_end == 0 ? g.tiles_y : std::min(c.tile_row_end, g.tiles_y);
     g.row_begin = std::min(c.tile_row_begin, g.row_end);
-    g.banded = (g.row_begin > 0 || g.row_end < g.tiles_y) ? 1u : 0u;
     g.tile_bits = bits_for((uint64_t)g.tiles_x * g.tiles_y - 1);
     return g;
 }

@@ -104,7 +104,6 @@ struct GridParams {
     float cull_z;
     uint32_t tiles_x, tiles_y;
     uint32_t row_begin, row_end; // binned bin rows [begin, end)
-    uint32_t banded;             // 1: [row_begin, row_end) is not every bin row
     uint32_t width, height;
     uint32_t bin_w, bin_h;       // bin size in px
     uint32_t tile_bits;          // bits of (tiles_x * tiles_y - 1)

@@ -72,16 +72,13 @@ def bits(a: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(a, np.float32).view(np.uint32)
 
 
-def compare_projected(gpu: np.ndarray, ref: np.ndarray, counts: np.ndarray, banded: bool = False) -> None:
+def compare_projected(gpu: np.ndarray, ref: np.ndarray, counts: np.ndarray) -> None:
     """Projected records bit for bit. The colour is compared for Gaussians that meet a bin
-    (counts > 0); the projection stores 0 for the others, whose colour no later stage reads. With
-    a band of bin rows the projection writes only the records of Gaussians that meet the band."""
+    (counts > 0); the projection stores 0 for the others, whose colour no later stage reads."""
     counts = np.asarray(counts)
     for f in ("position", "z", "covInv", "color", "alpha"):
         g, r = bits(gpu[f]), bits(ref[f])
-        if banded:
-            g, r = g[counts > 0], r[counts > 0]
-        elif f == "color":
+        if f == "color":
             assert not g[counts == 0].any(), "colour of Gaussians without bins is not 0"
             g, r = g[counts > 0], r[counts > 0]
         bad = np.nonzero((g != r).reshape(len(g), -1).any(axis=1))[0]

@@ -75,7 +75,7 @@ def test_frame_parity(case, keys):
     st = r.stats()
     assert st["error_flags"] == 0
     assert st["num_keys"] == ref["num_keys"]
-    compare_projected(r.dump(N.STAGE_PROJECTED), ref["g2d"], ref["counts"], banded=case[7] is not None)
+    compare_projected(r.dump(N.STAGE_PROJECTED), ref["g2d"], ref["counts"])
     assert np.array_equal(r.dump(N.STAGE_TILE_COUNTS), ref["counts"])
     assert np.array_equal(r.dump(N.STAGE_OFFSETS), ref["offsets"])
     assert np.array_equal(r.dump(N.STAGE_KEYS_UNSORTED), ref["keys_unsorted"])
