@@ -278,8 +278,9 @@ kt_status kt_gs_ply_decode(const char* path, kt_gaussian3d* out, uint64_t capaci
 
 /*
  * Render one frame. `cam` is host memory (the per-path camera UBO, uniformbufferobject.hpp:67-70).
- * `d_rgba8` is a device image of width*height RGBA8 pixels, row-major, row 0 at the top; it
- * is read-modify-written: out = clamp(in + vec4(C,1)*(1-T)) (gsplat_binned_splatting.comp:119-121).
+ * `d_rgba8` is a device image of width*height RGBA8 pixels, row-major, row 0 at the top, 4-byte
+ * aligned (KT_ERR_ARG otherwise); it is read-modify-written:
+ * out = clamp(in + vec4(C,1)*(1-T)) (gsplat_binned_splatting.comp:119-121).
  * Work is enqueued on `stream`; unless KT_GS_FLAG_ASYNC is set the call waits for the frame
  * status and, on key overflow, grows the key buffers and renders again.
  * Replaces ComputeGraph::submitTo of the node's sub-graph (computegraph.hpp:122-139).

@@ -695,6 +695,7 @@ kt_status render_impl(kt_gs_ctx* c, uint32_t path, Source src, const kt_camera_m
     if (src == Source::Scene && !c->has_scene)
         return fail(c, KT_ERR_STATE, "no Gaussians set on this context");
     if (!img) return fail(c, KT_ERR_ARG, "output image is NULL");
+    if (reinterpret_cast<uintptr_t>(img) & 3u) return fail(c, KT_ERR_ARG, "output image is not 4-byte aligned");
     KT_TRY_CUDA(c, cudaSetDevice(c->device));
     PathWs& w = c->paths[path];
     kt_status s = ensure_path_base(c, w);

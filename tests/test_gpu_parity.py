@@ -229,18 +229,45 @@ def test_deterministic_replay():
         assert np.array_equal(a, b)
 
 
-def test_render_host_matches_device_render():
+def host_image(a, kind):
+    """A host image holding `a`: a pageable numpy array (the runtime stages its copies) or a
+    page-locked torch tensor (copied by DMA)."""
+    if kind == "pageable":
+        return a.copy()
+    t = torch.empty(a.shape, dtype=torch.uint8, pin_memory=True)
+    t.copy_(torch.from_numpy(a))
+    return t
+
+
+def host_array(h):
+    return h if isinstance(h, np.ndarray) else h.numpy()
+
+
+@pytest.mark.parametrize("kind", ["pageable", "pinned"])
+def test_render_host_matches_device_render(kind):
     w = WORKLOADS["plumbing"]
     g3d = make_scene(w)
     cam = workload_camera(w)
     bg = background(w.height, w.width, "random")
     r = Renderer(w.width, w.height, bin_size=16, sh_degree=0)
     r.set_gaussians(g3d)
-    host = bg.copy()
+    host = host_image(bg, kind)
     r.render_host(cam, host)
     img = device_image(bg)
     r.render(cam, img)
-    assert np.array_equal(host, img.cpu().numpy())
+    assert np.array_equal(host_array(host), img.cpu().numpy())
+
+
+def test_unaligned_images_are_refused():
+    """RGBA8 pixels are written as 4-byte words: an image address that is not 4-byte aligned is
+    refused before anything is launched."""
+    r = Renderer(64, 64, bin_size=16, sh_degree=0)
+    r.set_gaussians(make_scene("plumbing", n=100))
+    img = torch.zeros(64 * 64 * 4 + 4, dtype=torch.uint8, device="cuda")
+    with pytest.raises(N.KtError) as e:
+        r.render(workload_camera("plumbing"), img.data_ptr() + 1)
+    assert e.value.status == N.KT_ERR_ARG
+    r.close()
 
 
 def test_render_batch_matches_single_views():
@@ -354,21 +381,23 @@ def test_sorted_keys_path_draws_the_same_image(wname, n, wh):
         assert np.array_equal(a, b)
 
 
-def test_render_host_clear_equals_a_cleared_image():
+@pytest.mark.parametrize("kind", ["pageable", "pinned"])
+def test_render_host_clear_equals_a_cleared_image(kind):
     """kt_gs_render_host_clear: the device image set to the clear colour, then the frame; the
-    same as kt_gs_render_host given an image of that colour, on both binning paths and a band."""
+    same as kt_gs_render_host given an image of that colour, on both binning paths, bands (whose
+    rows outside the band stay cleared) and a graph replay, into pageable and pinned images."""
     g3d = make_scene("plumbing", n=6000)
     cam = workload_camera("plumbing")
-    for flags, rows in [(0, None), (N.FLAG_SORTED_KEYS, None), (0, (3, 9))]:
+    for flags, rows in [(0, None), (N.FLAG_SORTED_KEYS, None), (0, (3, 9)), (N.FLAG_GRAPH, (0, 5))]:
         r = Renderer(256, 256, bin_size=16, sh_degree=0, flags=flags, tile_rows=rows)
         r.set_gaussians(g3d)
         for clear in [(0, 0, 0, 255), (10, 200, 30, 0)]:
-            host = np.full((256, 256, 4), 77, np.uint8)  # overwritten entirely
+            host = host_image(np.full((256, 256, 4), 77, np.uint8), kind)  # overwritten entirely
             r.render_host_clear(cam, host, clear=clear)
             expect = np.empty((256, 256, 4), np.uint8)
             expect[:] = clear
             r.render_host(cam, expect)
-            assert np.array_equal(host, expect)
+            assert np.array_equal(host_array(host), expect)
         r.close()
 
 
