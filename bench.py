@@ -231,11 +231,9 @@ def stage_report(w, cnt, st, stage_ms, timed_frames, nplanes, stage_names=None):
     # bytes the placement writes: 8 per (Gaussian, coarse bin) entry, 4 per pair
     placed = cnt["sort_bytes"] / nf
     entries = max(placed - 4 * K_avg, 0.0) / 8
-    vis_avg = cnt["visible"] / nf
     per_frame_bytes = {
-        # geometry planes read, SH planes read (for every Gaussian, or with the SH-after-count variant
-        # only for those that meet a bin); record 48 + count 4 + rect 8 + depth 4 written
-        "project_count": w.n * (16 * 3 + 64) + 16 * nplanes * (vis_avg if st.get("sh_after_count") else w.n),
+        # geometry and SH planes read; record 48 + count 4 + rect 8 + depth 4 written
+        "project_count": w.n * (16 * 3 + 64 + 16 * nplanes),
         # depth keys (counts + depths read, 8-B keys written) and the depth sort passes (16 B per
         # Gaussian per pass)
         "depth_sort": w.n * (4 + 4 + 8) + cnt["depth_sort_bytes"] / nf,

@@ -146,7 +146,6 @@ typedef struct kt_gs_stats {
     uint32_t place_bands;    /* bands of coarse-bin rows (4x4 bins each) of the pair placement */
     uint32_t place_runs;     /* 1: pairs placed by runs of segments (long coarse lists), 0: a warp
                                 per segment */
-    uint32_t sh_after_count; /* 1: the projection read SH planes only for Gaussians that meet a bin */
 } kt_gs_stats;
 
 /* Totals accumulated on the device over every frame rendered on a path since the last

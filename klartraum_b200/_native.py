@@ -91,7 +91,7 @@ class Stats(C.Structure):
         ("status_bytes", C.c_uint32), ("launches", C.c_uint32),
         ("packed", C.c_uint32), ("idx_bits", C.c_uint32),
         ("place_chunks", C.c_uint32), ("place_bands", C.c_uint32),
-        ("place_runs", C.c_uint32), ("sh_after_count", C.c_uint32),
+        ("place_runs", C.c_uint32),
     ]
 
     def as_dict(self) -> dict:

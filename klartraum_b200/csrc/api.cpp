@@ -59,12 +59,10 @@ struct GraphKey {
     int src = 0;
     uint64_t scene_gen = 0;
     uint64_t buf_gen = 0;
-    bool skip_sh = false;
     bool place_runs = false;
     bool operator==(const GraphKey& o) const {
         return img == o.img && n == o.n && cap == o.cap && flags == o.flags && src == o.src &&
-               scene_gen == o.scene_gen && buf_gen == o.buf_gen && skip_sh == o.skip_sh &&
-               place_runs == o.place_runs;
+               scene_gen == o.scene_gen && buf_gen == o.buf_gen && place_runs == o.place_runs;
     }
 };
 
@@ -108,8 +106,16 @@ struct PathWs {
     bool keys_frame = false;  // the path's last frame took the keys path
     // frame graph (KT_GS_FLAG_GRAPH)
     cudaGraphExec_t gexec = nullptr;
+    cudaGraph_t graph = nullptr;        // the captured graph gexec was made from (owns k1_node)
     GraphKey gkey{};
-    CamParams* cam_dev = nullptr;       // camera read by the replayed projection
+    // the projection's kernel node and its arguments: each replay sets its camera argument
+    cudaGraphNode_t k1_node = nullptr;
+    cudaKernelNodeParams k1_params{};
+    SceneDev k1_sc{};
+    CamParams k1_cam{};
+    GridParams k1_gp{};
+    FrameBufs k1_fb{};
+    void* k1_args[4] = {};
     cudaStream_t cap_stream = nullptr;  // capture stream
     uint64_t buf_gen = 0;               // bumped whenever a buffer of the path is reallocated
     FrameCtl* ctl = nullptr;
@@ -130,9 +136,6 @@ struct PathWs {
     bool have_frame = false;
     uint64_t frame_n = 0;
     uint32_t last_ncoarse = 0;  // coarse bins of the last frame's pair placement
-    // K1 reads SH planes only for binned Gaussians while few Gaussians meet a bin (from the
-    // visible fraction of the path's last completed frame, with hysteresis)
-    bool skip_sh = false;
     // pair placement by runs of segments while the path's frames have many segments per warp
     bool place_runs = false;
     // device image for kt_gs_render_host
@@ -198,6 +201,12 @@ CamParams make_cam(const kt_camera_mvp* cam) {
     mat4_mul(cam->model, cam->view, p.mv);  // ubo.model * ubo.view
     p.focal_x = cam->proj[0];
     p.focal_y = cam->proj[5];
+    // tanFov = 1 / focal, lim = 1.3 * tanFov (gsplat_projection.comp:76-77, 86-87): IEEE float
+    // division and product, the values the shader's own operations give
+    const float tan_fov_x = 1.0f / p.focal_x;
+    const float tan_fov_y = 1.0f / p.focal_y;
+    p.lim_x = 1.3f * tan_fov_x;
+    p.lim_y = 1.3f * tan_fov_y;
     return p;
 }
 
@@ -214,6 +223,8 @@ GridParams make_grid(const kt_gs_config& c) {
     g.sxy = (float)c.width * (float)c.height;
     g.cell_w = (float)c.bin_width;
     g.cell_h = (float)c.bin_height;
+    g.inv_cell_w = 1.0f / g.cell_w;
+    g.inv_cell_h = 1.0f / g.cell_h;
     g.cull_z = c.cull_z;
     g.tiles_x = (c.width + c.bin_width - 1) / c.bin_width;
     g.tiles_y = (c.height + c.bin_height - 1) / c.bin_height;
@@ -236,7 +247,9 @@ void free_path(PathWs& w) {
     w.key_cap = w.key_n = 0;
     if (w.gexec) cudaGraphExecDestroy(w.gexec);
     w.gexec = nullptr;
-    dfree(w.cam_dev);
+    if (w.graph) cudaGraphDestroy(w.graph);
+    w.graph = nullptr;
+    w.k1_node = nullptr;
     if (w.cap_stream) cudaStreamDestroy(w.cap_stream);
     w.cap_stream = nullptr;
     dfree(w.img); dfree(w.g2d);
@@ -417,22 +430,8 @@ struct FramePlan {
     uint32_t scan_epoch = 1;    // keys path: scan
     uint32_t key_epoch0 = 1;    // keys path: sort passes
     bool clear_status = false;  // graph replays clear the look-back words at the frame's start
-    bool skip_sh = false;       // K1 variant: SH planes read only for Gaussians that meet a bin
     bool place_runs = false;    // pair placement by runs of segments (k_fine_place_runs)
 };
-
-// The K1 variant for the next frame of a path: reading a Gaussian's SH planes only after its bin
-// count is known saves their bytes for the Gaussians that meet no bin but adds a dependent load,
-// which costs more than it saves unless most Gaussians meet no bin (measured: 73 against 64 us at
-// 83 % visible on the 1M frame, 319 against 277 us at 50 % on a half-screen band of the 6M frame).
-// Decided from the visible fraction of the path's last completed frame (its control block copy),
-// switching below 35 % and back above 45 %.
-bool choose_skip_sh(const PathWs& w) {
-    if (!w.have_frame || w.frame_n == 0 || !w.host_ctl) return w.skip_sh;
-    const double frac = (double)w.host_ctl->num_visible / (double)w.frame_n;
-    if (w.skip_sh) return frac < 0.45;
-    return frac < 0.35;
-}
 
 // Allocations and look-back epochs of a frame. Never called inside a stream capture.
 // The pair-placement kernel for the next frame of a path: a warp per segment while the segments
@@ -449,8 +448,6 @@ bool choose_place_runs(const PathWs& w, const PlaceGeom& pg) {
 kt_status prepare_frame(kt_gs_ctx* c, PathWs& w, uint64_t n, bool graph, FramePlan& fp, cudaStream_t stream) {
     fp.keys = (c->cfg.flags & KT_GS_FLAG_SORTED_KEYS) != 0;
     fp.clear_status = graph;
-    w.skip_sh = choose_skip_sh(w);
-    fp.skip_sh = w.skip_sh;
     if (fp.keys) {
         kt_status st = ensure_keys(c, w, std::max<uint64_t>(n, 1));
         if (st != KT_OK) return st;
@@ -524,15 +521,13 @@ kt_status prepare_frame(kt_gs_ctx* c, PathWs& w, uint64_t n, bool graph, FramePl
 
 // The kernels and copies of one frame on `stream`: no allocation and no host wait, so the
 // sequence can be captured into a CUDA graph. `ev` (may be null) receives the stage events.
-// The camera comes from `cam_dev` (device memory) when it is not null, else from `cam`.
 //   default: init -> K1 -> depth keys + plan -> depth passes -> rectangles in depth order +
 //            coarse counts -> prefix over chunks + coarse ranges -> coarse placement -> bin
 //            counts + bin ranges + pair placement -> totals -> K6
 //   keys:    init -> K1 -> scan + key emission -> plan + key sort passes -> boundary search ->
 //            totals -> K6
-kt_status record_frame(kt_gs_ctx* c, PathWs& w, Source src, uint64_t n, const CamParams* cam,
-                       const CamParams* cam_dev, uchar4* img, cudaStream_t stream, cudaEvent_t* ev,
-                       const FramePlan& fp) {
+kt_status record_frame(kt_gs_ctx* c, PathWs& w, Source src, uint64_t n, const CamParams* cam, uchar4* img,
+                       cudaStream_t stream, cudaEvent_t* ev, const FramePlan& fp) {
     const bool timed = ev != nullptr;
     FrameBufs fb = frame_bufs(w);
     if (fp.clear_status) {
@@ -551,7 +546,7 @@ kt_status record_frame(kt_gs_ctx* c, PathWs& w, Source src, uint64_t n, const Ca
     if (src == Source::Scene) {
         SceneDev sc{c->pos, c->rot, c->scale, c->sh, c->nplanes, c->deg, c->n};
         const CamParams none{};
-        KT_TRY_CUDA(c, launch_project_count(sc, cam ? *cam : none, cam_dev, c->gp, fb, fp.skip_sh, stream));
+        KT_TRY_CUDA(c, launch_project_count(sc, cam ? *cam : none, c->gp, fb, stream));
     } else {
         KT_TRY_CUDA(c, launch_load_projected(w.g2d, n, c->gp, fb, stream));
     }
@@ -625,33 +620,72 @@ kt_status enqueue_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* ca
     if (s != KT_OK) return s;
     w.keys_frame = fp.keys;
     w.last_ncoarse = fp.keys ? 0u : fp.pg.ncoarse;
-    if ((s = record_frame(c, w, src, n, cam, nullptr, img, stream, ev, fp)) != KT_OK) return s;
+    if ((s = record_frame(c, w, src, n, cam, img, stream, ev, fp)) != KT_OK) return s;
     KT_TRY_CUDA(c, cudaEventRecord(w.done_ev, stream));
     w.have_frame = true;
     w.frame_n = n;
     return KT_OK;
 }
 
+// The projection's kernel node of a captured frame graph and a copy of its arguments, so that a
+// replay can be given a new camera (cudaGraphExecKernelNodeSetParams). Leaves k1_node null when the
+// graph has no projection (caller-supplied projected records).
+cudaError_t find_k1_node(kt_gs_ctx* c, PathWs& w, cudaGraph_t g) {
+    w.k1_node = nullptr;
+    size_t count = 0;
+    cudaError_t e = cudaGraphGetNodes(g, nullptr, &count);
+    if (e != cudaSuccess || count == 0) return e;
+    std::vector<cudaGraphNode_t> nodes(count);
+    if ((e = cudaGraphGetNodes(g, nodes.data(), &count)) != cudaSuccess) return e;
+    const void* fn = project_count_kernel(c->deg);
+    for (cudaGraphNode_t nd : nodes) {
+        cudaGraphNodeType t;
+        if ((e = cudaGraphNodeGetType(nd, &t)) != cudaSuccess) return e;
+        if (t != cudaGraphNodeTypeKernel) continue;
+        cudaKernelNodeParams p{};
+        if ((e = cudaGraphKernelNodeGetParams(nd, &p)) != cudaSuccess) return e;
+        if (p.func != fn) continue;
+        // k_project_count(SceneDev, CamParams, GridParams, FrameBufs)
+        std::memcpy(&w.k1_sc, p.kernelParams[0], sizeof(SceneDev));
+        std::memcpy(&w.k1_cam, p.kernelParams[1], sizeof(CamParams));
+        std::memcpy(&w.k1_gp, p.kernelParams[2], sizeof(GridParams));
+        std::memcpy(&w.k1_fb, p.kernelParams[3], sizeof(FrameBufs));
+        w.k1_args[0] = &w.k1_sc;
+        w.k1_args[1] = &w.k1_cam;
+        w.k1_args[2] = &w.k1_gp;
+        w.k1_args[3] = &w.k1_fb;
+        w.k1_params = p;
+        w.k1_params.kernelParams = w.k1_args;
+        w.k1_params.extra = nullptr;
+        w.k1_node = nd;
+        break;
+    }
+    return cudaSuccess;
+}
+
 // Enqueue one frame as a replay of the path's captured frame graph (KT_GS_FLAG_GRAPH). The graph
 // is captured again when anything baked into it changed: the image pointer, the scene or any
 // buffer of the path, the Gaussian count, the flags or the source. Only the camera changes
-// between replays; it is copied into the path's device camera before the launch.
+// between replays: it is the projection kernel's argument, set in the executable graph before the
+// launch (launches already enqueued keep the camera they were launched with).
 kt_status enqueue_graph_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamParams* cam, uchar4* img,
                               cudaStream_t stream) {
     const uint64_t n = src == Source::Scene ? c->n : w.g2d_n;
     FramePlan fp;
     kt_status s = prepare_frame(c, w, n, true, fp, stream);
     if (s != KT_OK) return s;
-    if (!w.cam_dev) KT_TRY_CUDA(c, cudaMalloc(&w.cam_dev, sizeof(CamParams)));
     if (!w.cap_stream) KT_TRY_CUDA(c, cudaStreamCreateWithFlags(&w.cap_stream, cudaStreamNonBlocking));
     const uint32_t kFlagsBaked = ~(KT_GS_FLAG_ASYNC | KT_GS_FLAG_TIMING | KT_GS_FLAG_NO_AUTOGROW);
-    const GraphKey key{img, n,         w.cap,      c->cfg.flags & kFlagsBaked, (int)src, c->scene_gen, w.buf_gen,
-                       fp.skip_sh, fp.place_runs};
+    const GraphKey key{img, n, w.cap, c->cfg.flags & kFlagsBaked, (int)src, c->scene_gen, w.buf_gen, fp.place_runs};
+    bool captured = false;
     if (!w.gexec || !(key == w.gkey)) {
         if (w.gexec) cudaGraphExecDestroy(w.gexec);
         w.gexec = nullptr;
+        if (w.graph) cudaGraphDestroy(w.graph);
+        w.graph = nullptr;
+        w.k1_node = nullptr;
         KT_TRY_CUDA(c, cudaStreamBeginCapture(w.cap_stream, cudaStreamCaptureModeThreadLocal));
-        const kt_status rs = record_frame(c, w, src, n, nullptr, w.cam_dev, img, w.cap_stream, nullptr, fp);
+        const kt_status rs = record_frame(c, w, src, n, cam, img, w.cap_stream, nullptr, fp);
         cudaGraph_t g = nullptr;
         const cudaError_t e = cudaStreamEndCapture(w.cap_stream, &g);  // ends the capture in every case
         if (rs != KT_OK) {
@@ -660,12 +694,17 @@ kt_status enqueue_graph_frame(kt_gs_ctx* c, PathWs& w, Source src, const CamPara
         }
         KT_TRY_CUDA(c, e);
         const cudaError_t ei = cudaGraphInstantiate(&w.gexec, g, 0);
-        cudaGraphDestroy(g);
+        if (ei != cudaSuccess) cudaGraphDestroy(g);
         KT_TRY_CUDA(c, ei);
+        w.graph = g;
+        KT_TRY_CUDA(c, find_k1_node(c, w, g));
+        if (src == Source::Scene && !w.k1_node) return fail(c, KT_ERR_STATE, "frame graph without its projection node");
         w.gkey = key;
+        captured = true;  // the capture holds this frame's camera
     }
-    if (cam) {  // pageable source: the copy is staged before the call returns
-        KT_TRY_CUDA(c, cudaMemcpyAsync(w.cam_dev, cam, sizeof(CamParams), cudaMemcpyHostToDevice, stream));
+    if (cam && w.k1_node && !captured) {
+        w.k1_cam = *cam;
+        KT_TRY_CUDA(c, cudaGraphExecKernelNodeSetParams(w.gexec, w.k1_node, &w.k1_params));
     }
     KT_TRY_CUDA(c, cudaGraphLaunch(w.gexec, stream));
     KT_TRY_CUDA(c, cudaEventRecord(w.done_ev, stream));
@@ -1176,7 +1215,6 @@ kt_status kt_gs_frame_stats(kt_gs_ctx* c, uint32_t path, kt_gs_stats* out) {
         out->place_bands = h.place_nbands ? h.place_nbands : pg.nbands;  // the device's choice for the frame
     }
     out->place_runs = (!w.keys_frame && w.place_runs) ? 1u : 0u;
-    out->sh_after_count = w.skip_sh ? 1u : 0u;
     return KT_OK;
 }
 

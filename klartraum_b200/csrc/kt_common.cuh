@@ -94,6 +94,8 @@ struct CamParams {
     float mv[16];    // ubo.model * ubo.view
     float focal_x;   // ubo.proj[0][0]
     float focal_y;   // ubo.proj[1][1]
+    float lim_x;     // 1.3 * (1 / focal_x) (gsplat_projection.comp:76-77, 86-87)
+    float lim_y;     // 1.3 * (1 / focal_y)
 };
 
 // Screen / binning geometry.
@@ -101,6 +103,7 @@ struct GridParams {
     float half_w, half_h;        // W/2, H/2 (256 at 512: gsplat_projection.comp:202)
     float sxx, syy, sxy;         // covariance scale (512*512 at 512: comp:208)
     float cell_w, cell_h;        // bin size in px, as float
+    float inv_cell_w, inv_cell_h; // 1 / cell (rounded; seeds the exact overlap search)
     float cull_z;
     uint32_t tiles_x, tiles_y;
     uint32_t row_begin, row_end; // binned bin rows [begin, end)

@@ -31,11 +31,11 @@ constexpr int kSortTile = KT_SORT_TILE;  // keys per sort tile
 constexpr int kScanChunk = 2048;  // Gaussians per scan/emit CTA (keys path)
 
 // project.cu (compiled with -fmad=false)
-// cam_dev: when not null the kernel reads the camera from device memory (graph replays)
-// skip_unbinned_sh: read the SH planes only for Gaussians that meet a bin
-cudaError_t launch_project_count(const SceneDev& sc, const CamParams& cam, const CamParams* cam_dev,
-                                 const GridParams& gp, const FrameBufs& fb, bool skip_unbinned_sh,
+// The camera is a kernel parameter; a captured frame graph gets each frame's camera by an update of
+// that parameter (project_count_kernel identifies the kernel node among the graph's nodes).
+cudaError_t launch_project_count(const SceneDev& sc, const CamParams& cam, const GridParams& gp, const FrameBufs& fb,
                                  cudaStream_t stream);
+const void* project_count_kernel(int deg);
 cudaError_t launch_load_projected(const float* d_g2d, uint64_t n, const GridParams& gp,
                                   const FrameBufs& fb, cudaStream_t stream);
 cudaError_t launch_pack_scene(const float* d_aos, uint64_t n, float4* pos, float4* rot,

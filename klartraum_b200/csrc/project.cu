@@ -5,10 +5,10 @@
 // atomics). This file is compiled with -fmad=false and IEEE division / square root, so every
 // float result is the correctly rounded value of the shader's own operation sequence.
 //
-// Roofline: HBM bound. Per Gaussian it reads the geometry planes (48 B) and, for a Gaussian that
-// meets a bin, its SH planes (16 B per float4 plane: 192 B at SH3); it writes 48 B record + 4 B
-// count + 8 B rect + 4 B depth. The colour of a Gaussian that meets no bin is stored as 0 (the
-// reference computes it but no later stage reads it).
+// Roofline: HBM bound. Per Gaussian it reads the geometry planes (48 B) and its SH planes (16 B
+// per float4 plane: 192 B at SH3), loaded together up front; it writes 48 B record + 4 B count +
+// 8 B rect + 4 B depth. The colour of a Gaussian that meets no bin is stored as 0 (the reference
+// computes it but no later stage reads it).
 #include "kt_common.cuh"
 #include "kt_kernels.h"
 
@@ -62,13 +62,15 @@ __device__ __forceinline__ bool left_of_max(float mx, int i, float cell) {
     return !(mx < (float)i * cell);
 }
 
-__device__ __forceinline__ void axis_span(float mn, float mx, float cell, int n, int& lo,
+// `inv_cell` (1 / cell, rounded) only seeds the search: the exact comparisons that follow move the
+// run's ends to the bins that pass whatever the estimate, so no division is needed.
+__device__ __forceinline__ void axis_span(float mn, float mx, float cell, float inv_cell, int n, int& lo,
                                           int& hi) {
-    float e = floorf(mn / cell) - 1.0f;
+    float e = floorf(mn * inv_cell) - 1.0f;
     int l = !(e > 0.0f) ? 0 : (e > (float)n ? n : (int)e);
     while (l > 0 && right_of_min(mn, l - 1, cell)) --l;
     while (l < n && !right_of_min(mn, l, cell)) ++l;
-    float f = floorf(mx / cell);
+    float f = floorf(mx * inv_cell);
     int h = (mx != mx) ? n - 1 : (!(f > -1.0f) ? -1 : (f > (float)(n - 1) ? n - 1 : (int)f));
     while (h < n - 1 && left_of_max(mx, h + 1, cell)) ++h;
     while (h >= 0 && !left_of_max(mx, h, cell)) --h;
@@ -88,8 +90,8 @@ __device__ __forceinline__ uint32_t bin_span(float px, float py, float z, const 
     float mnx = px - spreadX, mny = py - spreadY;
     float mxx = px + spreadX, mxy = py + spreadY;
     int x0, x1, y0, y1;
-    axis_span(mnx, mxx, gp.cell_w, (int)gp.tiles_x, x0, x1);
-    axis_span(mny, mxy, gp.cell_h, (int)gp.tiles_y, y0, y1);
+    axis_span(mnx, mxx, gp.cell_w, gp.inv_cell_w, (int)gp.tiles_x, x0, x1);
+    axis_span(mny, mxy, gp.cell_h, gp.inv_cell_h, (int)gp.tiles_y, y0, y1);
     y0 = max(y0, (int)gp.row_begin);
     y1 = min(y1, (int)gp.row_end);
     if (x1 <= x0 || y1 <= y0) return 0u;
@@ -148,15 +150,8 @@ __device__ __forceinline__ void store_outputs(uint64_t i, float px, float py, fl
 
 // --------------------------------------------------------------------- K1
 
-// DEV_CAM: the camera comes from device memory (a captured frame graph replayed with new cameras)
-// instead of the kernel parameters.
-// SKIP_SH: read a Gaussian's SH planes only once it is known to meet a bin (saves their bytes when
-// many Gaussians meet none, at the price of a second dependent load); otherwise every plane is
-// loaded up front with the geometry. Either way a Gaussian that meets no bin stores colour 0.
-template <int DEG, bool DEV_CAM, bool SKIP_SH>
-__global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams cam_arg, const CamParams* cam_dev,
-                                                        GridParams gp, FrameBufs fb) {
-    const CamParams& cam = DEV_CAM ? *cam_dev : cam_arg;
+template <int DEG>
+__global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams cam, GridParams gp, FrameBufs fb) {
     constexpr int kCoef = (DEG + 1) * (DEG + 1);
     constexpr int kPlanes = (3 * kCoef + 3) / 4;
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -167,15 +162,13 @@ __global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams
         const float4 Q = __ldg(&sc.rot[i]);
         const float4 S = __ldg(&sc.scale[i]);
         float f[4 * kPlanes];
-        if (!SKIP_SH) {
 #pragma unroll
-            for (int p = 0; p < kPlanes; ++p) {
-                const float4 v = __ldg(&sc.sh[(uint64_t)p * sc.n + i]);
-                f[4 * p + 0] = v.x;
-                f[4 * p + 1] = v.y;
-                f[4 * p + 2] = v.z;
-                f[4 * p + 3] = v.w;
-            }
+        for (int p = 0; p < kPlanes; ++p) {
+            const float4 v = __ldg(&sc.sh[(uint64_t)p * sc.n + i]);
+            f[4 * p + 0] = v.x;
+            f[4 * p + 1] = v.y;
+            f[4 * p + 2] = v.z;
+            f[4 * p + 3] = v.w;
         }
 
         // comp:198-203: clip position, pixel position, depth
@@ -215,10 +208,10 @@ __global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams
         float tx = t4[0], ty = t4[1];
         const float tz = t4[2];
         const float focalX = cam.focal_x, focalY = cam.focal_y;
-        const float tanFovX = 1.0f / focalX;
-        const float tanFovY = 1.0f / focalY;
-        const float limx = 1.3f * tanFovX;
-        const float limy = 1.3f * tanFovY;
+        // tanFov = 1 / focal and lim = 1.3 * tanFov are the same for every Gaussian: the host
+        // computes them once with the same float operations
+        const float limx = cam.lim_x;
+        const float limy = cam.lim_y;
         const float txtz = tx / tz;
         const float tytz = ty / tz;
         tx = fminf(limx, fmaxf(-limx, txtz)) * tz;
@@ -252,16 +245,6 @@ __global__ void __launch_bounds__(256, 3) k_project_count(SceneDev sc, CamParams
         // stage reads the colour of the others (stored as 0)
         float rgb[3] = {0.0f, 0.0f, 0.0f};
         if (count != 0u) {
-        if (SKIP_SH) {
-#pragma unroll
-            for (int p = 0; p < kPlanes; ++p) {
-                const float4 v = __ldg(&sc.sh[(uint64_t)p * sc.n + i]);
-                f[4 * p + 0] = v.x;
-                f[4 * p + 1] = v.y;
-                f[4 * p + 2] = v.z;
-                f[4 * p + 3] = v.w;
-            }
-        }
         const float len = sqrtf(t4[0] * t4[0] + t4[1] * t4[1] + t4[2] * t4[2]);
         const float dx = t4[0] / len, dy = t4[1] / len, dz = t4[2] / len;
         float sh[16];
@@ -346,30 +329,26 @@ __global__ void __launch_bounds__(256) k_pack_scene(const float* __restrict__ ao
 
 // ------------------------------------------------------------------ launchers
 
-template <bool DEV_CAM, bool SKIP>
-static void launch_k1(const SceneDev& sc, const CamParams& cam, const CamParams* cam_dev, const GridParams& gp,
-                      const FrameBufs& fb, dim3 grid, cudaStream_t stream) {
-    switch (sc.deg) {
-        case 0: k_project_count<0, DEV_CAM, SKIP><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
-        case 1: k_project_count<1, DEV_CAM, SKIP><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
-        case 2: k_project_count<2, DEV_CAM, SKIP><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
-        default: k_project_count<3, DEV_CAM, SKIP><<<grid, 256, 0, stream>>>(sc, cam, cam_dev, gp, fb); break;
-    }
-}
-
-cudaError_t launch_project_count(const SceneDev& sc, const CamParams& cam, const CamParams* cam_dev,
-                                 const GridParams& gp, const FrameBufs& fb, bool skip_unbinned_sh,
+cudaError_t launch_project_count(const SceneDev& sc, const CamParams& cam, const GridParams& gp, const FrameBufs& fb,
                                  cudaStream_t stream) {
     if (sc.n == 0) return cudaSuccess;
     const dim3 grid((unsigned)((sc.n + 255) / 256));
-    if (cam_dev) {
-        if (skip_unbinned_sh) launch_k1<true, true>(sc, cam, cam_dev, gp, fb, grid, stream);
-        else launch_k1<true, false>(sc, cam, cam_dev, gp, fb, grid, stream);
-    } else {
-        if (skip_unbinned_sh) launch_k1<false, true>(sc, cam, nullptr, gp, fb, grid, stream);
-        else launch_k1<false, false>(sc, cam, nullptr, gp, fb, grid, stream);
+    switch (sc.deg) {
+        case 0: k_project_count<0><<<grid, 256, 0, stream>>>(sc, cam, gp, fb); break;
+        case 1: k_project_count<1><<<grid, 256, 0, stream>>>(sc, cam, gp, fb); break;
+        case 2: k_project_count<2><<<grid, 256, 0, stream>>>(sc, cam, gp, fb); break;
+        default: k_project_count<3><<<grid, 256, 0, stream>>>(sc, cam, gp, fb); break;
     }
     return cudaGetLastError();
+}
+
+const void* project_count_kernel(int deg) {
+    switch (deg) {
+        case 0: return reinterpret_cast<const void*>(&k_project_count<0>);
+        case 1: return reinterpret_cast<const void*>(&k_project_count<1>);
+        case 2: return reinterpret_cast<const void*>(&k_project_count<2>);
+        default: return reinterpret_cast<const void*>(&k_project_count<3>);
+    }
 }
 
 cudaError_t launch_load_projected(const float* d_g2d, uint64_t n, const GridParams& gp,

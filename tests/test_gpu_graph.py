@@ -39,6 +39,28 @@ def test_graph_replays_match_stream_frames(extra):
         assert torch.equal(a, b)
 
 
+def test_graph_replays_in_flight_keep_their_cameras():
+    """Replays of one path's graph enqueued back to back, each with its own camera (set as the
+    projection kernel's argument in the executable graph) and no wait between them: every frame
+    draws its own view."""
+    g3d = _scene(n=30000)
+    cams = orbit_views(5, 2.5, W, H, fovy_deg=60.0)
+    bgh = background(H, W, "random")
+    r = Renderer(W, H, bin_size=16, sh_degree=3)
+    r.set_gaussians(g3d)
+    ref = [r.render_host(c, bgh.copy()) for c in cams]
+    r.set_flags(N.FLAG_GRAPH | N.FLAG_ASYNC)
+    stream = torch.cuda.Stream()
+    hosts = [torch.from_numpy(bgh.copy()).pin_memory() for _ in cams]
+    for c, h in zip(cams, hosts):
+        r.render_host(c, h.data_ptr(), stream=stream.cuda_stream)
+    r.sync()
+    for a, h in zip(ref, hosts):
+        assert np.array_equal(a, h.numpy())
+    assert len({h.numpy().tobytes() for h in hosts}) == len(cams)
+    r.close()
+
+
 def test_graph_recaptures_on_new_image_scene_and_capacity():
     g3d, g3d_b = _scene(seed=21), _scene(n=40000, seed=22)
     cams = orbit_views(3, 2.5, W, H, fovy_deg=60.0)

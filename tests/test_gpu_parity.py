@@ -399,33 +399,3 @@ def test_render_host_clear_equals_a_cleared_image(kind):
             r.render_host(cam, expect)
             assert np.array_equal(host_array(host), expect)
         r.close()
-
-
-def test_projection_variants_give_the_same_frame():
-    """The first frame of a path reads every Gaussian's SH planes with its geometry; when most
-    Gaussians of the previous frame met no bin (here 68 %; the switch is below 35 % visible), the
-    next frames read them only for Gaussians that meet a bin. Both variants must give the oracle's
-    stage buffers and image."""
-    w = WORKLOADS["stress_2m"]
-    g3d = make_scene(w, n=6000)
-    cam = workload_camera(w)
-    bg = background(w.height, w.width)
-    cfg = oracle.config(w.width, w.height, bin_size=16, sh_degree=1)
-    ref = oracle.render_frame(cfg, cam, g3d, bg)
-    assert ref["counts"].astype(bool).mean() < 0.33  # below the 35 % switch
-    # buffers sized up front: a first frame that overflowed would be re-rendered, and the retry
-    # already knows the visible fraction
-    r = Renderer(w.width, w.height, bin_size=16, sh_degree=1, key_capacity=ref["num_keys"] + 4096)
-    r.set_gaussians(g3d)
-    variants = []
-    for frame in range(3):
-        img = device_image(bg)
-        r.render(cam, img)
-        variants.append(r.stats()["sh_after_count"])
-        compare_projected(r.dump(N.STAGE_PROJECTED), ref["g2d"], ref["counts"])
-        assert np.array_equal(r.dump(N.STAGE_TILE_COUNTS), ref["counts"])
-        assert np.array_equal(r.dump(N.STAGE_VALUES_SORTED), ref["vals"])
-        assert np.array_equal(r.dump(N.STAGE_TILE_RANGES), ref["ranges"])
-        assert np.abs(img.cpu().numpy().astype(int) - ref["image"].astype(int)).max() <= 1
-    assert variants == [0, 1, 1], variants
-    r.close()
