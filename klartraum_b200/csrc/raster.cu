@@ -109,8 +109,16 @@ __device__ __forceinline__ void blend_tail(const float4* __restrict__ rec, Index
 
 // Each thread shades two pixels of the 16x16 block, rows y and y + 8 of one column, so every
 // staged Gaussian read from shared memory serves both.
+// Ten resident CTAs (40 warps) per SM: the register budget drops from 61 to 48 per thread (a few
+// spilled bytes outside the blend loop) and more warps hide the staging batches' gathers. Measured on
+// one B200: 134 against 143 us on the 1M frame, 437 against 507 us on the 6M frame; twelve CTAs
+// (40 registers) were no better.
+#ifndef KT_RASTER_MIN_CTAS
+#define KT_RASTER_MIN_CTAS 10
+#endif
+
 template <bool PER_ELEM>
-__global__ void __launch_bounds__(kRasterThreads)
+__global__ void __launch_bounds__(kRasterThreads, KT_RASTER_MIN_CTAS)
 k_rasterize(const float4* __restrict__ rec, SortIO io, const uint2* __restrict__ ranges,
             const FrameCtl* __restrict__ ctl, GridParams gp, uchar4* __restrict__ img,
             uint32_t ypix0) {
