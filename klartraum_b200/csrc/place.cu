@@ -555,7 +555,11 @@ __device__ void fine_ranges(const FrameBufs& fb, const GridParams& gp) {
 
 // A warp per segment: pairs per bin of the 4x4, stored per segment and added to the bins' totals
 // (ranges[.].y); the last CTA to finish scans the totals into the bin ranges.
-__global__ void __launch_bounds__(kCountWarps * 32) k_fine_count(FrameBufs fb, GridParams gp, PlaceGeom pg) {
+// Two resident CTAs of 32 warps per SM (32 registers instead of 40, no spills), as the grid assumes.
+#ifndef KT_FINE_COUNT_MIN_CTAS
+#define KT_FINE_COUNT_MIN_CTAS 2
+#endif
+__global__ void __launch_bounds__(kCountWarps * 32, KT_FINE_COUNT_MIN_CTAS) k_fine_count(FrameBufs fb, GridParams gp, PlaceGeom pg) {
     __shared__ uint32_t s_last;
     FrameCtl* ctl = fb.ctl;
     if (!ctl->plan_ok) return;  // the same for every CTA
@@ -671,7 +675,14 @@ __device__ __forceinline__ void load_segment(const FrameBufs& fb, const Segment&
 // ballot ranks the entries that meet it and they write consecutive addresses. For frames with
 // fewer segments than about two per warp (the whole segment is loaded at once; few registers, four
 // CTAs per SM).
-__global__ void __launch_bounds__(kSegWarps * 32) k_fine_place(FrameBufs fb, GridParams gp, PlaceGeom pg) {
+// Three resident CTAs per SM (80 registers instead of 106, no spills): the grid is sized for full
+// occupancy, and with two CTAs per SM it ran in four waves. Measured with the bin count below: the
+// pair-placement stage 68.8 -> 64.5 us on the 1M frame (frame rate +3 %); four CTAs (64 registers,
+// a few spilled bytes) were no better.
+#ifndef KT_FINE_PLACE_MIN_CTAS
+#define KT_FINE_PLACE_MIN_CTAS 3
+#endif
+__global__ void __launch_bounds__(kSegWarps * 32, KT_FINE_PLACE_MIN_CTAS) k_fine_place(FrameBufs fb, GridParams gp, PlaceGeom pg) {
     const FrameCtl* ctl = fb.ctl;
     if (!ctl->plan_ok) return;
     const uint32_t ns = ctl->num_segments;
